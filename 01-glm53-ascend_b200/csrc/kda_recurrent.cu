@@ -1,0 +1,454 @@
+// Token-at-a-time GLM KDA recurrence on sm_100a: decode, verify (per-step
+// checkpoints) and recurrent prefill, behind kda_recurrent_launch and
+// kda_prepared_recurrent_launch.
+//
+// Math per token t, head h (kda_python.py:271-303; decode kernel
+// sgl-glm53-ascend-ops/csrc/kda/recurrent/kda_varlen_recurrent_decode.h:630-741):
+//   S <- Diag(e^g) S ; pred = S^T kn ; delta = beta (v - pred) ;
+//   S <- S + kn delta^T ; o = S^T qn
+// The pool slot is physically [V][K] (K contiguous), so a value row of the
+// state is D contiguous floats and every row is independent given kn, qn,
+// e^g and beta.
+//
+// Work decomposition (B200-first, no counterpart in the reference):
+//   * one CTA per (request, head, 32-row value slice): 128 threads, 4 warps,
+//     8 value rows per warp, 8 lanes per row, each lane D/8 key elements in
+//     float4 groups (k = c*32 + sub*4 + e), so every global or shared access
+//     of a row is 128 contiguous bytes per 8 lanes.
+//   * the 32 x D fp32 slice (16 KiB at D=128) is staged into shared memory by
+//     one bulk TMA copy (cp.async.bulk, no multicast) while the warps compute
+//     the token prologue; the state then lives in registers for all tokens of
+//     the request.
+//   * the prologue (L2 norms, gate, beta) is computed per warp with
+//     8-lane shuffles; row reductions are 3 xor-shuffles per row quad.
+//   * write-back, per-step checkpoints and prefix checkpoints are coalesced
+//     float4 stores straight from registers.
+// The kernel is HBM-bound: 2 x 64 KiB of state traffic per (token, head) in
+// decode against ~1.5 KB of token inputs.
+
+#include "kda_common.cuh"
+
+namespace kda {
+
+constexpr int kBV = 32;            // value rows per CTA
+constexpr int kRowsPerWarp = 8;
+constexpr int kRecThreads = kBV / kRowsPerWarp * 32;  // 128
+
+template <int D, int MODE>
+struct TokenRaw {
+    static constexpr int NC = D / 32;
+    uint2 qb[NC], kb[NC];      // bf16 q, k (RAW, LOG)
+    float4 qf[NC], kf[NC];     // fp32 qn, kn (PREPARED)
+    float4 gf[NC];             // log-decay (LOG) or exp(g) (PREPARED)
+    uint2 ab[NC];              // bf16 a (RAW)
+    uint16_t vb[2];            // this lane's two value rows
+    float beta;                // LOG / PREPARED
+    uint16_t bb;               // RAW
+};
+
+template <int D, int MODE>
+__device__ __forceinline__ void load_token(TokenRaw<D, MODE> &r, const KdaArgs &p, int64_t t, int h,
+                                           int sub, int row0) {
+    constexpr int NC = D / 32;
+    const int64_t base = (t * p.num_heads + h) * D;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        const int64_t off = base + c * 32 + sub * 4;
+        if constexpr (MODE == KDA_GATE_PREPARED) {
+            r.qf[c] = load_f32x4(static_cast<const float *>(p.q), off);
+            r.kf[c] = load_f32x4(static_cast<const float *>(p.k), off);
+            r.gf[c] = load_f32x4(p.g, off);
+        } else {
+            r.qb[c] = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p.q) + off));
+            r.kb[c] = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p.k) + off));
+            if constexpr (MODE == KDA_GATE_LOG) {
+                r.gf[c] = load_f32x4(p.g, off);
+            } else {
+                r.ab[c] = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(p.a) + off));
+            }
+        }
+    }
+    const uint16_t *vp = static_cast<const uint16_t *>(p.v) + base;
+    r.vb[0] = vp[row0];
+    r.vb[1] = vp[row0 + 4];
+    if constexpr (MODE == KDA_GATE_RAW) {
+        r.bb = static_cast<const uint16_t *>(p.b)[t * p.num_heads + h];
+    } else {
+        r.beta = __ldg(p.beta + t * p.num_heads + h);
+    }
+}
+
+__device__ __forceinline__ float sum8(float x) {
+    x += __shfl_xor_sync(0xffffffffu, x, 1);
+    x += __shfl_xor_sync(0xffffffffu, x, 2);
+    x += __shfl_xor_sync(0xffffffffu, x, 4);
+    return x;
+}
+
+template <int D>
+__device__ __forceinline__ void unpack4(float *dst, float4 x) {
+    dst[0] = x.x; dst[1] = x.y; dst[2] = x.z; dst[3] = x.w;
+}
+
+__device__ __forceinline__ void unpack_bf4(float *dst, uint2 x) {
+    dst[0] = bf16_lo(x.x); dst[1] = bf16_hi(x.x); dst[2] = bf16_lo(x.y); dst[3] = bf16_hi(x.y);
+}
+
+// Store the lane's two rows of the state (k-contiguous layout when FAST).
+template <int D, bool FAST>
+__device__ __forceinline__ void store_rows(float *base, int64_t sk, int64_t sv, int row0, int sub,
+                                           const float (&s)[2][D / 8]) {
+    constexpr int NC = D / 32;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int row = row0 + j * 4;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+            const int k = c * 32 + sub * 4;
+            if constexpr (FAST) {
+                *reinterpret_cast<float4 *>(base + static_cast<int64_t>(row) * D + k) =
+                    make_float4(s[j][c * 4 + 0], s[j][c * 4 + 1], s[j][c * 4 + 2], s[j][c * 4 + 3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) base[row * sv + (k + e) * sk] = s[j][c * 4 + e];
+            }
+        }
+    }
+}
+
+template <int D, int MODE, bool FAST>
+__global__ void __launch_bounds__(kRecThreads, 3)
+recurrent_kernel(const KdaArgs p, int nslice) {
+    constexpr int NC = D / 32;
+    constexpr int NE = D / 8;
+    __shared__ __align__(128) float tile[FAST ? kBV * D : 4];
+    __shared__ __align__(8) uint64_t bar;
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int sub = lane & 7, rq = lane >> 3;
+    int64_t bid = blockIdx.x;
+    const int slice = static_cast<int>(bid % nslice);
+    bid /= nslice;
+    const int h = p.head_begin + static_cast<int>(bid % p.head_count);
+    const int req = static_cast<int>(bid / p.head_count);
+    const int v0 = slice * kBV;
+    const int row0 = warp * kRowsPerWarp + rq;   // this lane's rows: row0, row0 + 4
+
+    const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
+    const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
+    const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
+    if (bos < 0 || eos < bos || eos > p.num_tokens) {
+        if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
+        return;
+    }
+    if (slot < 0 || slot >= p.num_slots) {
+        if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+        return;
+    }
+    int64_t tslot = 0, tlen = -1;
+    if (p.track_indices != nullptr) {
+        tslot = load_index(p.track_indices, p.index_bytes[2], req);
+        if (tslot > 0) tlen = load_index(p.track_lens, p.index_bytes[3], req);
+        if (tslot < 0 || tslot >= p.num_slots) {
+            if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+            return;
+        }
+    }
+
+    const int64_t sk = p.state_stride[2], sv = p.state_stride[3];
+    float *const head_state = p.state + slot * p.state_stride[0] + h * p.state_stride[1];
+
+    if constexpr (FAST) {
+        if (tid == 0) {
+            mbar_init(&bar, 1);
+            fence_mbar_init();
+        }
+        __syncthreads();
+        if (slot > 0 && tid == 0) {
+            constexpr uint32_t bytes = kBV * D * sizeof(float);
+            mbar_arrive_expect_tx(&bar, bytes);
+            bulk_g2s(tile, head_state + static_cast<int64_t>(v0) * D, bytes, &bar);
+        }
+    }
+
+    // Per-head constants of the raw gate, hoisted out of the token loop.
+    float dtb[NE];
+    float expA = 0.f;
+    if constexpr (MODE == KDA_GATE_RAW) {
+        expA = expf(__ldg(p.A_log + h));
+#pragma unroll
+        for (int c = 0; c < NC; ++c) unpack4<D>(dtb + c * 4, load_f32x4(p.dt_bias, h * D + c * 32 + sub * 4));
+    }
+
+    TokenRaw<D, MODE> cur, nxt;
+    if (bos < eos) load_token<D, MODE>(cur, p, bos, h, sub, v0 + row0);
+
+    float s[2][NE];
+    if (slot > 0) {
+        if constexpr (FAST) {
+            if (!mbar_wait(&bar, 0, p.status)) return;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+                    unpack4<D>(&s[j][c * 4],
+                               *reinterpret_cast<const float4 *>(&tile[(row0 + j * 4) * D + c * 32 + sub * 4]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < NE; ++e) {
+                    const int k = (e >> 2) * 32 + sub * 4 + (e & 3);
+                    s[j][e] = head_state[(v0 + row0 + j * 4) * sv + k * sk];
+                }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < NE; ++e) s[j][e] = 0.f;
+    }
+
+    float *const track_state =
+        (tslot > 0) ? p.state + tslot * p.state_stride[0] + h * p.state_stride[1] + (FAST ? v0 * D : v0 * sv)
+                    : nullptr;
+    if (tslot > 0 && tlen == 0) store_rows<D, FAST>(track_state, sk, sv, row0, sub, s);
+
+    float *const mid_head =
+        (p.intermediate != nullptr && slot > 0)
+            ? p.intermediate + req * p.mid_stride[0] + h * p.mid_stride[2] +
+                  (FAST ? static_cast<int64_t>(v0) * D : v0 * p.mid_stride[4])
+            : nullptr;
+
+    for (int64_t t = bos; t < eos; ++t) {
+        if (t + 1 < eos) load_token<D, MODE>(nxt, p, t + 1, h, sub, v0 + row0);
+
+        // ---- prologue: norms, decay, beta (kda_python.py:26-38) ----
+        float qn[NE], kn[NE], dec[NE];
+        float beta;
+        if constexpr (MODE == KDA_GATE_PREPARED) {
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                unpack4<D>(qn + c * 4, cur.qf[c]);
+                unpack4<D>(kn + c * 4, cur.kf[c]);
+                unpack4<D>(dec + c * 4, cur.gf[c]);
+            }
+            beta = cur.beta;
+        } else {
+            float q[NE], k[NE];
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                unpack_bf4(q + c * 4, cur.qb[c]);
+                unpack_bf4(k + c * 4, cur.kb[c]);
+            }
+            float sq = 0.f, sk2 = 0.f;
+#pragma unroll
+            for (int e = 0; e < NE; ++e) {
+                sq = fmaf(q[e], q[e], sq);
+                sk2 = fmaf(k[e], k[e], sk2);
+            }
+            sq = sum8(sq);
+            sk2 = sum8(sk2);
+            const float nq = sqrtf(sq + kNormEps), nk = sqrtf(sk2 + kNormEps);
+#pragma unroll
+            for (int e = 0; e < NE; ++e) {
+                qn[e] = q[e] / nq * p.scale;
+                kn[e] = k[e] / nk;
+            }
+            if constexpr (MODE == KDA_GATE_LOG) {
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    float g4[4];
+                    unpack4<D>(g4, cur.gf[c]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) dec[c * 4 + e] = expf(g4[e]);
+                }
+                beta = cur.beta;
+            } else {
+#pragma unroll
+                for (int c = 0; c < NC; ++c) {
+                    float a4[4];
+                    unpack_bf4(a4, cur.ab[c]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float gate = expA * (a4[e] + dtb[c * 4 + e]);
+                        dec[c * 4 + e] = expf(p.lower_bound * sigmoidf_(gate));
+                    }
+                }
+                beta = sigmoidf_(__uint_as_float(static_cast<uint32_t>(cur.bb) << 16));
+            }
+        }
+
+        // ---- recurrence step ----
+        float pa[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float acc = 0.f;
+#pragma unroll
+            for (int e = 0; e < NE; ++e) {
+                s[j][e] *= dec[e];
+                acc = fmaf(s[j][e], kn[e], acc);
+            }
+            pa[j] = acc;
+        }
+        pa[0] = sum8(pa[0]);
+        pa[1] = sum8(pa[1]);
+        float po[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float vv = __uint_as_float(static_cast<uint32_t>(cur.vb[j]) << 16);
+            const float d = (vv - pa[j]) * beta;
+            float acc = 0.f;
+#pragma unroll
+            for (int e = 0; e < NE; ++e) {
+                s[j][e] = fmaf(kn[e], d, s[j][e]);
+                acc = fmaf(s[j][e], qn[e], acc);
+            }
+            po[j] = acc;
+        }
+        po[0] = sum8(po[0]);
+        po[1] = sum8(po[1]);
+        if (sub == 0) {
+            const int64_t oi = (t * p.num_heads + h) * D + v0 + row0;
+            if (p.out_fp32) {
+                float *o = static_cast<float *>(p.out) + oi;
+                o[0] = po[0];
+                o[4] = po[1];
+            } else {
+                __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + oi;
+                o[0] = __float2bfloat16_rn(po[0]);
+                o[4] = __float2bfloat16_rn(po[1]);
+            }
+        }
+        const int64_t step = t - bos;
+        if (tslot > 0 && step + 1 == tlen) store_rows<D, FAST>(track_state, sk, sv, row0, sub, s);
+        if (mid_head != nullptr)
+            store_rows<D, FAST>(mid_head + step * p.mid_stride[1], p.mid_stride[3], p.mid_stride[4], row0,
+                                sub, s);
+        cur = nxt;
+    }
+
+    if (p.intermediate == nullptr && slot > 0)
+        store_rows<D, FAST>(head_state + (FAST ? static_cast<int64_t>(v0) * D : v0 * sv), sk, sv, row0, sub,
+                            s);
+}
+
+// ---------------------------------------------------------------------------
+// Host side: validation and dispatch
+// ---------------------------------------------------------------------------
+
+static bool aligned16(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+static int validate_common(const KdaArgs *a) {
+    if (a == nullptr) return KDA_ERR_INVALID_ARGUMENT;
+    if (a->head_dim != 64 && a->head_dim != 128) return KDA_ERR_UNSUPPORTED;
+    if (a->num_req < 0 || a->num_tokens < 0 || a->num_heads <= 0) return KDA_ERR_INVALID_ARGUMENT;
+    if (a->head_begin < 0 || a->head_count < 0 || a->head_begin + a->head_count > a->num_heads)
+        return KDA_ERR_INVALID_ARGUMENT;
+    for (int i = 0; i < 4; ++i)
+        if (a->index_bytes[i] != 4 && a->index_bytes[i] != 8) return KDA_ERR_INVALID_ARGUMENT;
+    if (a->num_req == 0 || a->head_count == 0) return KDA_OK;
+    if (a->state == nullptr || a->num_slots <= 0 || a->indices == nullptr || a->cu_seqlens == nullptr ||
+        a->out == nullptr || a->v == nullptr || a->q == nullptr || a->k == nullptr)
+        return KDA_ERR_INVALID_ARGUMENT;
+    if ((a->track_indices == nullptr) != (a->track_lens == nullptr)) return KDA_ERR_INVALID_ARGUMENT;
+    switch (a->gate_mode) {
+        case KDA_GATE_RAW:
+            if (a->a == nullptr || a->b == nullptr || a->A_log == nullptr || a->dt_bias == nullptr)
+                return KDA_ERR_INVALID_ARGUMENT;
+            break;
+        case KDA_GATE_LOG:
+        case KDA_GATE_PREPARED:
+            if (a->g == nullptr || a->beta == nullptr) return KDA_ERR_INVALID_ARGUMENT;
+            break;
+        default:
+            return KDA_ERR_INVALID_ARGUMENT;
+    }
+    // Four-element vector loads: bf16 rows need 8-byte, fp32 rows 16-byte
+    // alignment of the base pointer (row offsets are multiples of 4 elements).
+    auto aligned8 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 7u) == 0; };
+    if (a->gate_mode == KDA_GATE_PREPARED) {
+        if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->g)) return KDA_ERR_ALIGNMENT;
+    } else {
+        if (!aligned8(a->q) || !aligned8(a->k)) return KDA_ERR_ALIGNMENT;
+        if (a->gate_mode == KDA_GATE_LOG && !aligned16(a->g)) return KDA_ERR_ALIGNMENT;
+        if (a->gate_mode == KDA_GATE_RAW && (!aligned8(a->a) || !aligned16(a->dt_bias)))
+            return KDA_ERR_ALIGNMENT;
+    }
+    return KDA_OK;
+}
+
+// The state slice is one contiguous, 16-byte aligned run of kBV rows.
+static bool state_fast(const KdaArgs *a) {
+    const int64_t D = a->head_dim;
+    return aligned16(a->state) && a->state_stride[2] == 1 && a->state_stride[3] == D &&
+           a->state_stride[0] % 4 == 0 && a->state_stride[1] % 4 == 0;
+}
+
+static bool mid_fast(const KdaArgs *a) {
+    if (a->intermediate == nullptr) return true;
+    const int64_t D = a->head_dim;
+    return aligned16(a->intermediate) && a->mid_stride[3] == 1 && a->mid_stride[4] == D &&
+           a->mid_stride[0] % 4 == 0 && a->mid_stride[1] % 4 == 0 && a->mid_stride[2] % 4 == 0;
+}
+
+template <int D, int MODE>
+static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st) {
+    const int nslice = D / kBV;
+    const int64_t grid = static_cast<int64_t>(a->num_req) * a->head_count * nslice;
+    if (fast)
+        recurrent_kernel<D, MODE, true><<<static_cast<unsigned>(grid), kRecThreads, 0, st>>>(*a, nslice);
+    else
+        recurrent_kernel<D, MODE, false><<<static_cast<unsigned>(grid), kRecThreads, 0, st>>>(*a, nslice);
+}
+
+template <int D>
+static void dispatch_mode(const KdaArgs *a, bool fast, cudaStream_t st) {
+    switch (a->gate_mode) {
+        case KDA_GATE_RAW: launch_rec<D, KDA_GATE_RAW>(a, fast, st); break;
+        case KDA_GATE_LOG: launch_rec<D, KDA_GATE_LOG>(a, fast, st); break;
+        default: launch_rec<D, KDA_GATE_PREPARED>(a, fast, st); break;
+    }
+}
+
+}  // namespace kda
+
+extern "C" int kda_abi_version(void) { return KDA_ABI_VERSION; }
+
+extern "C" const char *kda_status_string(int code) {
+    switch (code) {
+        case KDA_OK: return "ok";
+        case KDA_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case KDA_ERR_UNSUPPORTED: return "unsupported configuration";
+        case KDA_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
+        case KDA_ERR_WORKSPACE: return "workspace missing or too small";
+        case KDA_ERR_LAUNCH: return "CUDA launch failed";
+        case KDA_DEVICE_ERR_WAIT_TIMEOUT: return "device: bounded mbarrier wait expired";
+        case KDA_DEVICE_ERR_BAD_SLOT: return "device: state slot index out of range";
+        case KDA_DEVICE_ERR_BAD_SEQLENS: return "device: cu_seqlens not monotone or beyond T";
+        case KDA_DEVICE_ERR_GATE_RANGE: return "device: gate span beyond the chunk kernel's exponent range";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int kda_recurrent_launch(const KdaArgs *args, void *stream) {
+    const int rc = kda::validate_common(args);
+    if (rc != KDA_OK) return rc;
+    if (args->num_req == 0 || args->head_count == 0) return KDA_OK;
+    const bool fast = kda::state_fast(args) && kda::mid_fast(args);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (args->head_dim == 128)
+        kda::dispatch_mode<128>(args, fast, st);
+    else
+        kda::dispatch_mode<64>(args, fast, st);
+    return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+}
+
+extern "C" int kda_prepared_recurrent_launch(const KdaArgs *args, void *stream) {
+    if (args == nullptr) return KDA_ERR_INVALID_ARGUMENT;
+    KdaArgs a = *args;
+    a.gate_mode = KDA_GATE_PREPARED;
+    a.intermediate = nullptr;
+    return kda_recurrent_launch(&a, stream);
+}

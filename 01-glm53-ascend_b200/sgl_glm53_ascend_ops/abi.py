@@ -1,0 +1,165 @@
+"""ctypes binding of the C ABI in ``include/kda_b200.h`` (``libkda_b200.so``).
+
+This is the binding a non-torch host (or a maintainer wiring the library into
+another runtime) would write: a ``KdaArgs`` struct of raw device pointers,
+strides and sizes, and the four launch entry points. ``args_from_tensors``
+fills the struct from torch tensors for tests and the benchmark; the library
+itself never sees a torch type.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+from typing import Optional
+
+import torch
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libkda_b200.so"
+
+KDA_OK = 0
+KDA_GATE_RAW, KDA_GATE_LOG, KDA_GATE_PREPARED = 0, 1, 2
+
+# Entry points declared in include/kda_b200.h.
+EXPORTED = (
+    "kda_abi_version",
+    "kda_status_string",
+    "kda_recurrent_launch",
+    "kda_chunk_workspace_bytes",
+    "kda_chunk_launch",
+    "kda_prepared_recurrent_launch",
+)
+
+
+class KdaArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("a", ctypes.c_void_p),
+        ("b", ctypes.c_void_p),
+        ("A_log", ctypes.c_void_p),
+        ("dt_bias", ctypes.c_void_p),
+        ("g", ctypes.c_void_p),
+        ("beta", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("state", ctypes.c_void_p),
+        ("state_stride", ctypes.c_int64 * 4),
+        ("num_slots", ctypes.c_int64),
+        ("indices", ctypes.c_void_p),
+        ("cu_seqlens", ctypes.c_void_p),
+        ("track_indices", ctypes.c_void_p),
+        ("track_lens", ctypes.c_void_p),
+        ("intermediate", ctypes.c_void_p),
+        ("mid_stride", ctypes.c_int64 * 5),
+        ("index_bytes", ctypes.c_int32 * 4),
+        ("num_req", ctypes.c_int32),
+        ("num_tokens", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("head_begin", ctypes.c_int32),
+        ("head_count", ctypes.c_int32),
+        ("gate_mode", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("lower_bound", ctypes.c_float),
+        ("status", ctypes.c_void_p),
+        ("out_fp32", ctypes.c_int32),
+    ]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing; run 01-glm53-ascend_b200/build.py")
+        L = ctypes.CDLL(str(LIB_PATH))
+        L.kda_abi_version.restype = ctypes.c_int
+        L.kda_status_string.restype = ctypes.c_char_p
+        L.kda_status_string.argtypes = [ctypes.c_int]
+        for name in ("kda_recurrent_launch", "kda_prepared_recurrent_launch"):
+            getattr(L, name).restype = ctypes.c_int
+            getattr(L, name).argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p]
+        L.kda_chunk_workspace_bytes.restype = ctypes.c_size_t
+        L.kda_chunk_workspace_bytes.argtypes = [ctypes.c_int32] * 4
+        L.kda_chunk_launch.restype = ctypes.c_int
+        L.kda_chunk_launch.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
+                                       ctypes.c_void_p]
+        _lib = L
+    return _lib
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _ibytes(t: Optional[torch.Tensor]) -> int:
+    return 8 if (t is not None and t.dtype == torch.int64) else 4
+
+
+def args_from_tensors(*, q, k, v, out, state, indices, cu_seqlens, scale, gate_mode,
+                      g=None, beta=None, a=None, b=None, A_log=None, dt_bias=None,
+                      lower_bound=0.0, track_indices=None, track_lens=None,
+                      intermediate=None, head_begin=0, head_count=None,
+                      status=None, out_fp32=False) -> KdaArgs:
+    """Fill KdaArgs from device tensors ([1,T,H,D] token tensors, [slots,H,K,V] pool)."""
+    H, D = state.shape[1], state.shape[2]
+    T = q.numel() // (H * D)
+    x = KdaArgs()
+    x.q, x.k, x.v, x.out = _ptr(q), _ptr(k), _ptr(v), _ptr(out)
+    x.a, x.b, x.A_log, x.dt_bias = _ptr(a), _ptr(b), _ptr(A_log), _ptr(dt_bias)
+    x.g, x.beta = _ptr(g), _ptr(beta)
+    x.state = _ptr(state)
+    for i in range(4):
+        x.state_stride[i] = state.stride(i)
+    x.num_slots = state.shape[0]
+    x.indices, x.cu_seqlens = _ptr(indices), _ptr(cu_seqlens)
+    x.track_indices, x.track_lens = _ptr(track_indices), _ptr(track_lens)
+    x.intermediate = _ptr(intermediate)
+    if intermediate is not None:
+        for i in range(5):
+            x.mid_stride[i] = intermediate.stride(i)
+    for i, t in enumerate((indices, cu_seqlens, track_indices, track_lens)):
+        x.index_bytes[i] = _ibytes(t)
+    x.num_req = indices.numel()
+    x.num_tokens = T
+    x.num_heads = H
+    x.head_dim = D
+    x.head_begin = head_begin
+    x.head_count = H - head_begin if head_count is None else head_count
+    x.gate_mode = gate_mode
+    x.scale = float(scale)
+    x.lower_bound = float(lower_bound)
+    x.status = _ptr(status)
+    x.out_fp32 = int(bool(out_fp32))
+    return x
+
+
+def stream_handle(stream: Optional[torch.cuda.Stream] = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def recurrent_launch(args: KdaArgs, stream: Optional[torch.cuda.Stream] = None) -> int:
+    return lib().kda_recurrent_launch(ctypes.byref(args), stream_handle(stream))
+
+
+def prepared_recurrent_launch(args: KdaArgs, stream: Optional[torch.cuda.Stream] = None) -> int:
+    return lib().kda_prepared_recurrent_launch(ctypes.byref(args), stream_handle(stream))
+
+
+def chunk_workspace_bytes(num_req: int, num_tokens: int, num_heads: int, head_dim: int) -> int:
+    return lib().kda_chunk_workspace_bytes(num_req, num_tokens, num_heads, head_dim)
+
+
+def chunk_launch(args: KdaArgs, workspace: Optional[torch.Tensor], workspace_bytes: int,
+                 stream: Optional[torch.cuda.Stream] = None) -> int:
+    return lib().kda_chunk_launch(ctypes.byref(args), _ptr(workspace), workspace_bytes,
+                                  stream_handle(stream))
+
+
+def status_string(code: int) -> str:
+    return lib().kda_status_string(code).decode()

@@ -1,0 +1,19 @@
+from .kda import (
+    kda_varlen_chunk,
+    kda_varlen_chunk_g,
+    kda_varlen_chunk_v2,
+    kda_varlen_recurrent,
+    kda_varlen_recurrent_g,
+    kda_varlen_recurrent_v2,
+    prepared_recurrent,
+)
+
+__all__ = [
+    "kda_varlen_chunk",
+    "kda_varlen_chunk_g",
+    "kda_varlen_chunk_v2",
+    "kda_varlen_recurrent",
+    "kda_varlen_recurrent_g",
+    "kda_varlen_recurrent_v2",
+    "prepared_recurrent",
+]

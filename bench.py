@@ -1,0 +1,378 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 GLM KDA operator (the driver's contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+For N > 1 launch under torchrun (one process per GPU, NCCL). Prints ONE JSON
+line on rank 0.
+
+Headline (BASELINE.json ``configs[1]``): recurrent decode, 256 requests x 1
+token, H=32, K=V=128, fp32 pool of 512 slots with 256 distinct slots updated in
+place; the metric is tokens/s. A step is one call of the public op
+``kda_varlen_recurrent_g`` over that batch. Per-GPU work is fixed (weak
+scaling): every rank owns its own 256 requests and its own pool, with no
+collective on the data path; ``value`` = tokens of all ranks / max-over-ranks
+device time. The touched state (512 MiB read + 512 MiB written per step) is
+larger than the 126 MB L2, so no flush is needed between steps.
+
+Also reported:
+* ``roofline``: the decode kernel alone (C-ABI launches timed with CUDA events
+  on the launching stream) against the measured HBM copy bandwidth;
+* ``e2e``: the same metric through the public op with inputs copied from pinned
+  host memory each step and the output read back;
+* ``cpu_baseline``: the CPU oracle (``oracle/kda_ref.py``, a port of the
+  reference's PyTorch recurrence) on this host's cores, on a bounded sample;
+* ``prefill``: the chunked prefill of ``configs[2]`` (8 varlen sequences,
+  33,494 tokens, H=32) with its tensor/HBM roofline;
+* ``clocks``: SM clock and throttle reasons sampled by NVML during timing.
+
+``--impl reference`` times the reference's own CPU algorithm (the oracle port;
+the reference is Python and Ascend-only, so nothing of it can run on the GPU
+box) on the same metric and configuration.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "01-glm53-ascend_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+# Algorithmic bytes per (token, head) of the log-gate decode at K=V=128:
+# state 64 KiB read + 64 KiB write, q/k/v bf16 768 B, g fp32 512 B, beta 4 B,
+# output bf16 256 B.
+DECODE_BYTES_PER_TOKEN_HEAD = 65536 * 2 + 768 + 512 + 4 + 256
+
+# DRAM bytes per decode launch (read + write) from one ncu capture of the
+# decode kernel at the benchmark shape; see profiles/decode_cfg2_ncu.md.
+# None until a capture exists.
+DECODE_TRAFFIC_PER_LAUNCH = None
+
+METRIC = "KDA tokens/s (prefill, decode) H32 d128 @1/2/4/8 B200; decode HBM GB/s vs peak"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", 0) or 0), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init_gpu(self):
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            self.pg.barrier(device_ids=[self.local])
+        torch.cuda.synchronize()
+
+    def max(self, x: float) -> float:
+        if self.pg is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (NVML) during the timed region
+# ---------------------------------------------------------------------------
+
+_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+            0x10: "sync_boost", 0x100: "display_clock_setting"}
+
+
+class ClockSampler(threading.Thread):
+    def __init__(self, device: int, period: float = 0.02):
+        super().__init__(daemon=True)
+        self.period = period
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop_evt = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as exc:  # no NVML: report what we could not sample
+            self.err = f"{type(exc).__name__}: {exc}"
+
+    def run(self):
+        while self.ok and not self._stop_evt.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def stop(self) -> dict:
+        self._stop_evt.set()
+        if self.is_alive():
+            self.join(timeout=2)
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": getattr(self, "err", "no samples")}
+        names = [n for bit, n in sorted(_REASONS.items()) if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# Timing helpers
+# ---------------------------------------------------------------------------
+
+def time_steps(fn, steps: int, warmup: int, dist: Dist, stream=None):
+    """W untimed steps, then exactly K timed steps bracketed by barrier+sync;
+    returns the max-over-ranks device milliseconds of the K steps."""
+    for _ in range(warmup):
+        fn()
+    dist.barrier()
+    s = stream or torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s)
+    for _ in range(steps):
+        fn()
+    end.record(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return dist.max(start.elapsed_time(end))
+
+
+# ---------------------------------------------------------------------------
+# Decode (headline)
+# ---------------------------------------------------------------------------
+
+def bench_decode(args, dist: Dist, hbm_gbs: float, peak_kind: str) -> dict:
+    from sgl_glm53_ascend_ops import abi, ops, workloads
+
+    w = workloads.config2(seed=1000 + dist.rank)
+    d = w.to("cuda")
+    kw = d.kwargs()
+    tokens = w.tokens
+    heads = w.heads
+
+    def step():
+        ops.kda_varlen_recurrent_g(**kw, prefill=False)
+
+    sampler = ClockSampler(dist.local)
+    sampler.start()
+    ms = time_steps(step, args.steps, args.warmup, dist)
+    clocks = sampler.stop()
+    ms_per_step = ms / args.steps
+    value = dist.world * tokens / (ms_per_step / 1e3)
+
+    # Kernel alone through the C ABI (same stream, CUDA events).
+    out = torch.empty_like(d.v)
+    cargs = abi.args_from_tensors(q=d.q, k=d.k, v=d.v, out=out, state=d.pool, indices=d.indices,
+                                  cu_seqlens=d.cu_seqlens, scale=d.scale, gate_mode=abi.KDA_GATE_LOG,
+                                  g=d.g, beta=d.beta)
+
+    def launch():
+        rc = abi.recurrent_launch(cargs)
+        if rc != 0:
+            raise RuntimeError(f"kda_recurrent_launch: {abi.status_string(rc)}")
+
+    kms = time_steps(launch, args.steps, args.warmup, dist) / args.steps
+    alg_bytes = tokens * heads * DECODE_BYTES_PER_TOKEN_HEAD
+    achieved = alg_bytes / (kms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_gbs, "unit": "GB/s",
+                "frac": round(achieved / hbm_gbs, 4), "traffic": DECODE_TRAFFIC_PER_LAUNCH,
+                "kernel_us": round(kms * 1e3, 2), "algorithmic_bytes": alg_bytes,
+                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s"}
+
+    # End to end through the public op: pinned host inputs in, output out.
+    host = {n: t.cpu().pin_memory() for n, t in
+            dict(q=w.q, k=w.k, v=w.v, g=w.g, beta=w.beta, indices=w.indices, cu=w.cu_seqlens).items()}
+    dev = {n: torch.empty_like(t, device="cuda") for n, t in host.items()}
+    out_host = torch.empty(w.v.shape, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        for n, t in host.items():
+            dev[n].copy_(t, non_blocking=True)
+        o = ops.kda_varlen_recurrent_g(q=dev["q"], k=dev["k"], v=dev["v"], g=dev["g"], beta=dev["beta"],
+                                       initial_state_source=d.pool, initial_state_indices=dev["indices"],
+                                       cu_seqlens=dev["cu"], scale=d.scale, prefill=False)
+        out_host.copy_(o, non_blocking=True)
+
+    ems = time_steps(e2e_step, args.steps, args.warmup, dist) / args.steps
+    e2e = {"value": round(dist.world * tokens / (ems / 1e3), 1), "unit": "tokens/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 4)}
+    return dict(value=value, ms_per_step=ms_per_step, roofline=roofline, e2e=e2e, clocks=clocks,
+                gpu_launches=args.steps, tokens=tokens)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (rank 0, N = 1): the oracle port on this host's cores
+# ---------------------------------------------------------------------------
+
+def cpu_decode_rate(requests: int, budget_s: float, seed: int = 7):
+    """tokens/s of the CPU oracle on `requests` cfg2-shaped requests; repeats
+    until `budget_s` seconds of work. Returns (rate, threads, sample text)."""
+    from oracle import kda_ref
+    from sgl_glm53_ascend_ops import workloads
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w = workloads.config2(seed=seed, requests=requests, slots=requests + 1)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        kda_ref.kda_varlen_recurrent_g(**w.kwargs(), out_fp32=True)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return reps * w.tokens / el, threads, f"{reps} x {requests} decode requests x 32 heads, {el:.1f} s"
+
+
+def run_reference(args, dist: Dist):
+    if dist.rank != 0:
+        return
+    from oracle import kda_ref
+    from sgl_glm53_ascend_ops import workloads
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample_req = 8
+    w = workloads.config2(seed=11, requests=sample_req, slots=sample_req + 1)
+
+    def step():
+        kda_ref.kda_varlen_recurrent_g(**w.kwargs(), out_fp32=True)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = args.steps * w.tokens / el
+    sample = f"each step: {sample_req} of config 2's 256 requests x 32 heads (oracle port, fp32)"
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg2 decode: 256 req x 1 tok, H=32, K=V=128, pool 512 slots (sampled)",
+                       "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-oracle work")
+    ap.add_argument("--mode", choices=("full", "kernel"), default="full",
+                    help="kernel: only the timed decode op loop (for profiler captures)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    dist = Dist()
+    if args.impl == "reference":
+        run_reference(args, dist)
+        return
+
+    dist.init_gpu()
+    hbm_gbs, bf16_tf, bf16_tf_sus, peak_kind = _peaks()
+    if args.mode == "kernel":
+        from sgl_glm53_ascend_ops import ops, workloads
+        kw = workloads.config2(seed=1000 + dist.rank).to("cuda").kwargs()
+        ms = time_steps(lambda: ops.kda_varlen_recurrent_g(**kw, prefill=False), args.steps, args.warmup, dist)
+        if dist.rank == 0:
+            print(json.dumps({"mode": "kernel", "ms_per_step": ms / args.steps}), flush=True)
+        dist.close()
+        return
+    dec = bench_decode(args, dist, hbm_gbs, peak_kind)
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1:
+        rate, threads, sample = cpu_decode_rate(32, args.cpu_budget)
+        cpu = {"value": round(rate, 2), "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
+
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(dec["value"], 1),
+            "unit": "tokens/s",
+            "n_gpus": dist.world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dec["ms_per_step"], 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "cfg2 decode: 256 req x 1 tok, H=32, K=V=128, fp32 pool 512 slots, "
+                                   "256 distinct slots updated in place (log-gate op)",
+                       "global_batch": 256 * dist.world, "per_gpu_batch": 256,
+                       "l2": "inputs larger than L2 (1 GiB of state traffic per step), no flush",
+                       "parallelism": f"dp{dist.world} (independent request batches, no collective)"},
+            "roofline": dec["roofline"],
+            "cpu_baseline": cpu,
+            "e2e": dec["e2e"],
+            "gpu_launches": dec["gpu_launches"],
+            "clocks": dec["clocks"],
+        }
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,149 @@
+/*
+ * kda_b200.h -- C ABI of the B200 (sm_100a) GLM KDA varlen operator.
+ *
+ * Plain pointers, sizes and strides; no torch types. Every entry point is
+ * asynchronous on the given CUDA stream (a cudaStream_t passed as void*),
+ * never synchronises the host, never allocates, and returns a KdaStatus.
+ * Device-side failures (a bounded wait that gave up) are reported through the
+ * optional `status` word, which the caller reads after the stream drains.
+ *
+ * The entry points replace the reference's host-to-kernel seam:
+ *   KdaArgs                         <- KdaLaunchArgs
+ *       (sgl-glm53-ascend-ops/csrc/kda/recurrent/kda_varlen_recurrent.h:59-92)
+ *       and KdaChunkLaunchArgs
+ *       (sgl-glm53-ascend-ops/csrc/kda/chunk/kda_varlen_chunk.h:120-141)
+ *   kda_recurrent_launch            <- LaunchKdaDecodeH16/H32/H64 and
+ *       LaunchKdaPrefillH4/H8 (kda_varlen_recurrent.h:94-98), selected at
+ *       kda_varlen_recurrent.cpp:218-253
+ *   kda_chunk_workspace_bytes       <- the per-block workspace sizing
+ *       kda_chunk::kWorkspaceFloatsPerBlock (kda_varlen_chunk.h:79-116) and
+ *       its allocation at kda_varlen_chunk.cpp:154-166
+ *   kda_chunk_launch                <- LaunchKdaVarlenChunk
+ *       (kda_varlen_chunk.h:143-144; launched at kda_varlen_chunk.cpp:190-191)
+ *   kda_prepared_recurrent_launch   <- the prepared_recurrent_kernel_* launches
+ *       (sgl-glm53-ascend-ops/csrc/kda/prepared_recurrent.cpp:684-710)
+ *
+ * Layouts (all row-major, element strides):
+ *   q, k, v, a, g, out : [T, H, D]   (the torch [1, T, H, D] contiguous tensor)
+ *   b, beta            : [T, H]
+ *   A_log              : [H];  dt_bias : [H * D]
+ *   state pool         : element (slot, h, k, v) at
+ *                        slot*s[0] + h*s[1] + k*s[2] + v*s[3]; the production
+ *                        pool is K-contiguous (s[2] == 1, s[3] == D)
+ *   intermediate       : element (req, step, h, k, v) at
+ *                        req*m[0] + step*m[1] + h*m[2] + k*m[3] + v*m[4]
+ *   indices, cu_seqlens, track_indices, track_lens : int32 or int64
+ *                        (index_bytes[] = 4 or 8 each)
+ * Slot 0 of the pool is the padding row: it reads as a zero state and is never
+ * written.
+ */
+#ifndef KDA_B200_H
+#define KDA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KDA_ABI_VERSION 1
+
+typedef enum KdaStatus {
+    KDA_OK = 0,
+    KDA_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size or dimension */
+    KDA_ERR_UNSUPPORTED = 2,      /* head_dim other than 64/128, ... */
+    KDA_ERR_ALIGNMENT = 3,        /* a pointer or stride breaks a 16-byte rule */
+    KDA_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
+    KDA_ERR_LAUNCH = 5            /* the CUDA launch itself failed */
+} KdaStatus;
+
+/* Codes a kernel may write into *status (first error wins). */
+#define KDA_DEVICE_ERR_WAIT_TIMEOUT 0x101  /* a bounded mbarrier wait expired */
+#define KDA_DEVICE_ERR_BAD_SLOT     0x102  /* a slot index outside [0, num_slots) */
+#define KDA_DEVICE_ERR_BAD_SEQLENS  0x103  /* cu_seqlens not monotone / beyond T */
+#define KDA_DEVICE_ERR_GATE_RANGE   0x104  /* a 16-row gate span beyond the chunk
+                                              kernel's exponent range */
+
+typedef enum KdaGateMode {
+    /* g = lower_bound * sigmoid(exp(A_log[h]) * (a + dt_bias[h])), beta =
+     * sigmoid(b); q, k normalised in the kernel (kda_python.py:16-39). */
+    KDA_GATE_RAW = 0,
+    /* g (fp32 log-decay [T,H,D]) and beta (fp32 [T,H]) given directly; q, k
+     * still normalised in the kernel. */
+    KDA_GATE_LOG = 1,
+    /* prepared_recurrent: q, k are fp32 and already normalised/scaled, g holds
+     * exp(gate) (fp32), beta fp32; nothing is recomputed. */
+    KDA_GATE_PREPARED = 2
+} KdaGateMode;
+
+typedef struct KdaArgs {
+    const void *q;            /* bf16, or fp32 under KDA_GATE_PREPARED */
+    const void *k;            /* bf16, or fp32 under KDA_GATE_PREPARED */
+    const void *v;            /* bf16 */
+    const void *a;            /* bf16 [T,H,D]  (RAW) */
+    const void *b;            /* bf16 [T,H]    (RAW) */
+    const float *A_log;       /* [H]           (RAW) */
+    const float *dt_bias;     /* [H*D]         (RAW) */
+    const float *g;           /* [T,H,D] log-decay (LOG) or exp(g) (PREPARED) */
+    const float *beta;        /* [T,H]         (LOG, PREPARED) */
+    void *out;                /* bf16 [T,H,D], written for every token */
+    float *state;             /* fp32 pool, updated in place */
+    int64_t state_stride[4];  /* slot, head, k, v */
+    int64_t num_slots;        /* pool rows; slots are checked against it */
+    const void *indices;      /* [num_req] pool slot per request */
+    const void *cu_seqlens;   /* [num_req + 1] packed sequence boundaries */
+    const void *track_indices;/* [num_req] or NULL: prefix-checkpoint slot */
+    const void *track_lens;   /* [num_req] or NULL: tokens before the checkpoint */
+    float *intermediate;      /* recurrent only: per-step checkpoints or NULL */
+    int64_t mid_stride[5];    /* req, step, head, k, v */
+    int32_t index_bytes[4];   /* indices, cu_seqlens, track_indices, track_lens */
+    int32_t num_req;
+    int32_t num_tokens;       /* T */
+    int32_t num_heads;        /* H of the token tensors and the pool */
+    int32_t head_dim;         /* D = K = V: 64 or 128 */
+    int32_t head_begin;       /* heads processed: [head_begin, head_begin+head_count) */
+    int32_t head_count;
+    int32_t gate_mode;        /* KdaGateMode */
+    float scale;              /* applied to q after the L2 norm */
+    float lower_bound;        /* RAW gate bound (negative) */
+    int32_t *status;          /* optional device word for KDA_DEVICE_ERR_* */
+    int32_t out_fp32;         /* verification: nonzero -> `out` is fp32 [T,H,D],
+                                 the pre-cast values of the bf16 output */
+} KdaArgs;
+
+/* ABI version compiled into the library (KDA_ABI_VERSION). */
+int kda_abi_version(void);
+
+/* Human-readable name of a KdaStatus or KDA_DEVICE_ERR_* code. */
+const char *kda_status_string(int code);
+
+/* Token-at-a-time recurrence: decode (one or more tokens per request, the
+ * EAGLE verify regime with `intermediate`) and recurrent prefill. One CTA per
+ * (request, head, 32-row value slice); the 128x128 fp32 state slice is staged
+ * into shared memory with a bulk TMA copy. Replaces LaunchKdaDecodeH{16,32,64}
+ * and LaunchKdaPrefillH{4,8} (kda_varlen_recurrent.h:94-98). */
+int kda_recurrent_launch(const KdaArgs *args, void *stream);
+
+/* Bytes of device workspace kda_chunk_launch needs for these sizes (replaces
+ * kda_chunk::kWorkspaceFloatsPerBlock, kda_varlen_chunk.h:79-116). */
+size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens,
+                                 int32_t num_heads, int32_t head_dim);
+
+/* Chunk-64 WY/UT prefill over a varlen batch, any sequence lengths. The
+ * workspace must be at least kda_chunk_workspace_bytes(...) bytes; its
+ * contents need no initialisation. Replaces LaunchKdaVarlenChunk
+ * (kda_varlen_chunk.h:143-144). `intermediate` must be NULL. */
+int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes,
+                     void *stream);
+
+/* The recurrence on prepared fp32 inputs (gate_mode is forced to
+ * KDA_GATE_PREPARED). Replaces the prepared_recurrent_kernel_* launches
+ * (prepared_recurrent.cpp:578-604, 684-710). */
+int kda_prepared_recurrent_launch(const KdaArgs *args, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KDA_B200_H */

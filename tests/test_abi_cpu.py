@@ -1,0 +1,118 @@
+"""CPU checks of the C ABI boundary (no kernel is launched).
+
+* every function ``include/kda_b200.h`` declares is exported by
+  ``libkda_b200.so``;
+* the ctypes mirror of ``KdaArgs`` has the header's size and field offsets
+  (checked against a tiny C program compiled here with gcc);
+* argument validation returns the documented KdaStatus codes before any CUDA
+  call is made;
+* the sglang plugin hook registers the prepared recurrence.
+"""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "kda_b200.h"
+
+
+@pytest.fixture(scope="module")
+def abi():
+    from sgl_glm53_ascend_ops import abi as _abi
+    return _abi
+
+
+def _declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kda_[a-z_]+)\s*\(", text)))
+
+
+def test_header_functions_are_exported(abi):
+    lib = abi.lib()
+    declared = _declared_functions()
+    assert declared, "no declarations parsed"
+    assert sorted(abi.EXPORTED) == declared
+    for name in declared:
+        assert hasattr(lib, name), f"{name} missing from {abi.LIB_PATH.name}"
+    assert lib.kda_abi_version() == 1
+
+
+def test_struct_layout_matches_header(abi, tmp_path):
+    fields = [f[0] for f in abi.KdaArgs._fields_]
+    src = ["#include <stdio.h>", "#include <stddef.h>", '#include "kda_b200.h"', "int main(void){",
+           'printf("%zu\\n", sizeof(KdaArgs));']
+    src += [f'printf("%zu\\n", offsetof(KdaArgs, {f}));' for f in fields]
+    src += ["return 0;}"]
+    c = tmp_path / "layout.c"
+    c.write_text("\n".join(src))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(ROOT / "include"), str(c), "-o", str(exe)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True,
+                                           text=True).stdout.split()]
+    assert vals[0] == ctypes.sizeof(abi.KdaArgs)
+    for f, off in zip(fields, vals[1:]):
+        assert getattr(abi.KdaArgs, f).offset == off, f"offset of {f}"
+
+
+def test_invalid_arguments_rejected_without_launch(abi):
+    lib = abi.lib()
+    assert lib.kda_recurrent_launch(None, None) == 1              # KDA_ERR_INVALID_ARGUMENT
+    assert lib.kda_prepared_recurrent_launch(None, None) == 1
+    assert lib.kda_chunk_launch(None, None, 0, None) == 1
+    a = abi.KdaArgs()
+    a.head_dim = 96
+    a.num_heads = 1
+    a.index_bytes[:] = [4, 4, 4, 4]
+    assert lib.kda_recurrent_launch(ctypes.byref(a), None) == 2   # KDA_ERR_UNSUPPORTED
+    a.head_dim = 128
+    a.index_bytes[1] = 3
+    assert lib.kda_recurrent_launch(ctypes.byref(a), None) == 1
+    a.index_bytes[1] = 4
+    a.num_req = 0
+    assert lib.kda_recurrent_launch(ctypes.byref(a), None) == 0   # nothing to do, no launch
+    a.num_req = 2
+    a.head_count = 1
+    assert lib.kda_recurrent_launch(ctypes.byref(a), None) == 1   # null pointers
+    assert abi.status_string(0x102).startswith("device: state slot")
+
+
+def test_workspace_size_is_queryable(abi):
+    n = abi.chunk_workspace_bytes(8, 33494, 32, 128)
+    assert n >= 0
+
+
+def test_plugin_registers_prepared_recurrent():
+    from sgl_glm53_ascend_ops import plugin
+
+    calls = []
+
+    class Registry:
+        @staticmethod
+        def register(target, fn, hook_type):
+            calls.append((target, fn, hook_type))
+
+    plugin.register(Registry)
+    assert calls == [(plugin.SGLANG_TARGET_PATH, plugin._prepared_recurrent, "REPLACE")]
+
+
+def test_ops_registered_with_reference_schemas():
+    import torch
+    import sgl_glm53_ascend_ops  # noqa: F401
+
+    ns = torch.ops.sgl_glm53_ascend
+    rec = str(ns.kda_varlen_recurrent.default._schema)
+    assert rec.startswith("sgl_glm53_ascend::kda_varlen_recurrent(*, Tensor A_log, Tensor a, Tensor dt_bias, "
+                          "Tensor q, Tensor k, Tensor v, Tensor b, Tensor(a!) initial_state_source")
+    assert "Tensor(b!)? intermediate_state=None, bool prefill=False" in rec
+    chunk = str(ns.kda_varlen_chunk.default._schema)
+    assert "bool prefill=False, Tensor? track_state_indices=None, Tensor? track_state_lens=None) -> Tensor" in chunk
+    prep = str(ns.prepared_recurrent.default._schema)
+    assert prep.endswith("bool track_state=False, int head_offset=0) -> ()")
+    for name in ("kda_varlen_recurrent_v2", "kda_varlen_chunk_v2", "kda_varlen_recurrent_g",
+                 "kda_varlen_chunk_g"):
+        assert hasattr(ns, name)
