@@ -116,63 +116,55 @@ __device__ __forceinline__ void store_rows(float *base, int64_t sk, int64_t sv, 
     }
 }
 
+// Everything one work item -- (request, head, 32-row value slice) -- needs
+// besides its state rows.
+struct Item {
+    int req, h, v0;
+    int64_t bos, eos, slot, tslot, tlen;
+};
+
+// Decodes item `it` and checks its metadata; false (with the status word set)
+// when the request must be skipped. Identical in every thread of the CTA.
+__device__ __forceinline__ bool decode_item(const KdaArgs &p, int64_t it, int nslice, Item &m) {
+    m.v0 = static_cast<int>(it % nslice) * kBV;
+    it /= nslice;
+    m.h = p.head_begin + static_cast<int>(it % p.head_count);
+    m.req = static_cast<int>(it / p.head_count);
+    m.bos = load_index(p.cu_seqlens, p.index_bytes[1], m.req);
+    m.eos = load_index(p.cu_seqlens, p.index_bytes[1], m.req + 1);
+    m.slot = load_index(p.indices, p.index_bytes[0], m.req);
+    m.tslot = 0;
+    m.tlen = -1;
+    if (m.bos < 0 || m.eos < m.bos || m.eos > p.num_tokens) {
+        if (threadIdx.x == 0) report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
+        return false;
+    }
+    if (m.slot < 0 || m.slot >= p.num_slots) {
+        if (threadIdx.x == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+        return false;
+    }
+    if (p.track_indices != nullptr) {
+        m.tslot = load_index(p.track_indices, p.index_bytes[2], m.req);
+        if (m.tslot < 0 || m.tslot >= p.num_slots) {
+            if (threadIdx.x == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+            return false;
+        }
+        if (m.tslot > 0) m.tlen = load_index(p.track_lens, p.index_bytes[3], m.req);
+    }
+    return true;
+}
+
+// The token loop of one item with the state rows already in registers:
+// prologue, recurrence step, output, prefix/per-step checkpoints, final
+// write-back (kda_python.py:271-307).
 template <int D, int MODE, bool FAST>
-__global__ void __launch_bounds__(kRecThreads, 3)
-recurrent_kernel(const KdaArgs p, int nslice) {
+__device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float (&s)[2][D / 8], int row0, int sub) {
     constexpr int NC = D / 32;
     constexpr int NE = D / 8;
-    __shared__ __align__(128) float tile[FAST ? kBV * D : 4];
-    __shared__ __align__(8) uint64_t bar;
-
-    const int tid = threadIdx.x;
-    const int lane = tid & 31, warp = tid >> 5;
-    const int sub = lane & 7, rq = lane >> 3;
-    int64_t bid = blockIdx.x;
-    const int slice = static_cast<int>(bid % nslice);
-    bid /= nslice;
-    const int h = p.head_begin + static_cast<int>(bid % p.head_count);
-    const int req = static_cast<int>(bid / p.head_count);
-    const int v0 = slice * kBV;
-    const int row0 = warp * kRowsPerWarp + rq;   // this lane's rows: row0, row0 + 4
-
-    const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
-    const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
-    const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
-    if (bos < 0 || eos < bos || eos > p.num_tokens) {
-        if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
-        return;
-    }
-    if (slot < 0 || slot >= p.num_slots) {
-        if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
-        return;
-    }
-    int64_t tslot = 0, tlen = -1;
-    if (p.track_indices != nullptr) {
-        tslot = load_index(p.track_indices, p.index_bytes[2], req);
-        if (tslot > 0) tlen = load_index(p.track_lens, p.index_bytes[3], req);
-        if (tslot < 0 || tslot >= p.num_slots) {
-            if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
-            return;
-        }
-    }
-
+    const int h = m.h, v0 = m.v0;
     const int64_t sk = p.state_stride[2], sv = p.state_stride[3];
-    float *const head_state = p.state + slot * p.state_stride[0] + h * p.state_stride[1];
+    const int64_t row_off = FAST ? static_cast<int64_t>(v0) * D : v0 * sv;
 
-    if constexpr (FAST) {
-        if (tid == 0) {
-            mbar_init(&bar, 1);
-            fence_mbar_init();
-        }
-        __syncthreads();
-        if (slot > 0 && tid == 0) {
-            constexpr uint32_t bytes = kBV * D * sizeof(float);
-            mbar_arrive_expect_tx(&bar, bytes);
-            bulk_g2s(tile, head_state + static_cast<int64_t>(v0) * D, bytes, &bar);
-        }
-    }
-
-    // Per-head constants of the raw gate, hoisted out of the token loop.
     float dtb[NE];
     float expA = 0.f;
     if constexpr (MODE == KDA_GATE_RAW) {
@@ -181,48 +173,21 @@ recurrent_kernel(const KdaArgs p, int nslice) {
         for (int c = 0; c < NC; ++c) unpack4<D>(dtb + c * 4, load_f32x4(p.dt_bias, h * D + c * 32 + sub * 4));
     }
 
-    TokenRaw<D, MODE> cur, nxt;
-    if (bos < eos) load_token<D, MODE>(cur, p, bos, h, sub, v0 + row0);
-
-    float s[2][NE];
-    if (slot > 0) {
-        if constexpr (FAST) {
-            if (!mbar_wait(&bar, 0, p.status)) return;
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int c = 0; c < NC; ++c)
-                    unpack4<D>(&s[j][c * 4],
-                               *reinterpret_cast<const float4 *>(&tile[(row0 + j * 4) * D + c * 32 + sub * 4]));
-        } else {
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int e = 0; e < NE; ++e) {
-                    const int k = (e >> 2) * 32 + sub * 4 + (e & 3);
-                    s[j][e] = head_state[(v0 + row0 + j * 4) * sv + k * sk];
-                }
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-#pragma unroll
-            for (int e = 0; e < NE; ++e) s[j][e] = 0.f;
-    }
-
     float *const track_state =
-        (tslot > 0) ? p.state + tslot * p.state_stride[0] + h * p.state_stride[1] + (FAST ? v0 * D : v0 * sv)
-                    : nullptr;
-    if (tslot > 0 && tlen == 0) store_rows<D, FAST>(track_state, sk, sv, row0, sub, s);
+        (m.tslot > 0) ? p.state + m.tslot * p.state_stride[0] + h * p.state_stride[1] + row_off : nullptr;
+    if (m.tslot > 0 && m.tlen == 0) store_rows<D, FAST>(track_state, sk, sv, row0, sub, s);
 
     float *const mid_head =
-        (p.intermediate != nullptr && slot > 0)
-            ? p.intermediate + req * p.mid_stride[0] + h * p.mid_stride[2] +
+        (p.intermediate != nullptr && m.slot > 0)
+            ? p.intermediate + m.req * p.mid_stride[0] + h * p.mid_stride[2] +
                   (FAST ? static_cast<int64_t>(v0) * D : v0 * p.mid_stride[4])
             : nullptr;
 
-    for (int64_t t = bos; t < eos; ++t) {
-        if (t + 1 < eos) load_token<D, MODE>(nxt, p, t + 1, h, sub, v0 + row0);
+    TokenRaw<D, MODE> cur, nxt;
+    if (m.bos < m.eos) load_token<D, MODE>(cur, p, m.bos, h, sub, v0 + row0);
+
+    for (int64_t t = m.bos; t < m.eos; ++t) {
+        if (t + 1 < m.eos) load_token<D, MODE>(nxt, p, t + 1, h, sub, v0 + row0);
 
         // ---- prologue: norms, decay, beta (kda_python.py:26-38) ----
         float qn[NE], kn[NE], dec[NE];
@@ -250,11 +215,13 @@ recurrent_kernel(const KdaArgs p, int nslice) {
             }
             sq = sum8(sq);
             sk2 = sum8(sk2);
-            const float nq = sqrtf(sq + kNormEps), nk = sqrtf(sk2 + kNormEps);
+            // One reciprocal per row instead of a division per element; the
+            // product differs from q / ||q|| by at most an ulp.
+            const float rq = p.scale / sqrtf(sq + kNormEps), rk = 1.0f / sqrtf(sk2 + kNormEps);
 #pragma unroll
             for (int e = 0; e < NE; ++e) {
-                qn[e] = q[e] / nq * p.scale;
-                kn[e] = k[e] / nk;
+                qn[e] = q[e] * rq;
+                kn[e] = k[e] * rk;
             }
             if constexpr (MODE == KDA_GATE_LOG) {
 #pragma unroll
@@ -321,17 +288,127 @@ recurrent_kernel(const KdaArgs p, int nslice) {
                 o[4] = __float2bfloat16_rn(po[1]);
             }
         }
-        const int64_t step = t - bos;
-        if (tslot > 0 && step + 1 == tlen) store_rows<D, FAST>(track_state, sk, sv, row0, sub, s);
+        const int64_t step = t - m.bos;
+        if (m.tslot > 0 && step + 1 == m.tlen) store_rows<D, FAST>(track_state, sk, sv, row0, sub, s);
         if (mid_head != nullptr)
-            store_rows<D, FAST>(mid_head + step * p.mid_stride[1], p.mid_stride[3], p.mid_stride[4], row0,
-                                sub, s);
+            store_rows<D, FAST>(mid_head + step * p.mid_stride[1], p.mid_stride[3], p.mid_stride[4], row0, sub, s);
         cur = nxt;
     }
 
-    if (p.intermediate == nullptr && slot > 0)
-        store_rows<D, FAST>(head_state + (FAST ? static_cast<int64_t>(v0) * D : v0 * sv), sk, sv, row0, sub,
-                            s);
+    if (p.intermediate == nullptr && m.slot > 0) {
+        float *head_state = p.state + m.slot * p.state_stride[0] + h * p.state_stride[1] + row_off;
+        store_rows<D, FAST>(head_state, sk, sv, row0, sub, s);
+    }
+}
+
+// Production layout (K-contiguous, 16-byte aligned): persistent CTAs walk the
+// items with a STAGES-deep ring of bulk-TMA state tiles, so each SM keeps
+// several 16 KiB loads in flight while it computes. Item n of a CTA uses ring
+// stage n % STAGES, whose mbarrier completes phase (n / STAGES) & 1.
+template <int D, int MODE, int STAGES>
+__global__ void __launch_bounds__(kRecThreads, 3)
+recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items) {
+    constexpr int NC = D / 32;
+    constexpr uint32_t kTileBytes = kBV * D * sizeof(float);
+    extern __shared__ __align__(128) float ring[];            // STAGES x kBV x D
+    __shared__ __align__(8) uint64_t bars[STAGES];
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int sub = lane & 7, rq = lane >> 3;
+    const int row0 = warp * kRowsPerWarp + rq;
+    const int64_t first = blockIdx.x, stride = gridDim.x;
+
+    // Thread 0 fills ring stage `st` with item `it` (or just arrives when the
+    // item has no state to read), so the stage's phase always completes.
+    auto issue = [&](int64_t it, int st) {
+        if (it >= num_items) return;
+        int64_t x = it / nslice;
+        const int h = p.head_begin + static_cast<int>(x % p.head_count);
+        const int req = static_cast<int>(x / p.head_count);
+        const int v0 = static_cast<int>(it % nslice) * kBV;
+        const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
+        if (slot > 0 && slot < p.num_slots) {
+            mbar_arrive_expect_tx(&bars[st], kTileBytes);
+            bulk_g2s(ring + static_cast<size_t>(st) * kBV * D,
+                     p.state + slot * p.state_stride[0] + h * p.state_stride[1] + static_cast<int64_t>(v0) * D,
+                     kTileBytes, &bars[st]);
+        } else {
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&bars[st])) : "memory");
+        }
+    };
+
+    if (tid == 0) {
+#pragma unroll
+        for (int st = 0; st < STAGES; ++st) mbar_init(&bars[st], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+#pragma unroll
+        for (int st = 0; st < STAGES; ++st) issue(first + st * stride, st);
+    }
+
+    int n = 0;
+    for (int64_t it = first; it < num_items; it += stride, ++n) {
+        const int st = n % STAGES;
+        const uint32_t phase = (n / STAGES) & 1;
+        Item m;
+        const bool ok = decode_item(p, it, nslice, m);
+        if (!mbar_wait(&bars[st], phase, p.status)) return;
+        float s[2][D / 8];
+        if (ok && m.slot > 0) {
+            const float *tile = ring + static_cast<size_t>(st) * kBV * D;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+                    unpack4<D>(&s[j][c * 4],
+                               *reinterpret_cast<const float4 *>(&tile[(row0 + j * 4) * D + c * 32 + sub * 4]));
+        } else {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+#pragma unroll
+                for (int e = 0; e < D / 8; ++e) s[j][e] = 0.f;
+        }
+        // Every thread has its rows in registers: refill this stage now so the
+        // load overlaps this item's arithmetic.
+        __syncthreads();
+        if (tid == 0) issue(it + STAGES * stride, st);
+        if (ok) run_item<D, MODE, true>(p, m, s, row0, sub);
+    }
+}
+
+// Any other pool layout: one CTA per item, strided loads straight from the
+// pool (used by prepared_recurrent on a [K,V]-contiguous state).
+template <int D, int MODE>
+__global__ void __launch_bounds__(kRecThreads, 3)
+recurrent_strided_kernel(const KdaArgs p, int nslice) {
+    constexpr int NE = D / 8;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+    const int sub = lane & 7, rq = lane >> 3;
+    const int row0 = warp * kRowsPerWarp + rq;
+    Item m;
+    if (!decode_item(p, blockIdx.x, nslice, m)) return;
+    const int64_t sk = p.state_stride[2], sv = p.state_stride[3];
+    float s[2][NE];
+    if (m.slot > 0) {
+        const float *hs = p.state + m.slot * p.state_stride[0] + m.h * p.state_stride[1];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < NE; ++e) {
+                const int k = (e >> 2) * 32 + sub * 4 + (e & 3);
+                s[j][e] = hs[(m.v0 + row0 + j * 4) * sv + k * sk];
+            }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < NE; ++e) s[j][e] = 0.f;
+    }
+    run_item<D, MODE, false>(p, m, s, row0, sub);
 }
 
 // ---------------------------------------------------------------------------
@@ -393,14 +470,52 @@ static bool mid_fast(const KdaArgs *a) {
            a->mid_stride[0] % 4 == 0 && a->mid_stride[1] % 4 == 0 && a->mid_stride[2] % 4 == 0;
 }
 
+constexpr int kRingStages = 4;
+
+struct DeviceInfo {
+    int sms = 0;
+};
+
+static int sm_count() {
+    static DeviceInfo info[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (info[dev].sms == 0) {
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        info[dev].sms = sms > 0 ? sms : 148;
+    }
+    return info[dev].sms;
+}
+
 template <int D, int MODE>
 static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st) {
     const int nslice = D / kBV;
-    const int64_t grid = static_cast<int64_t>(a->num_req) * a->head_count * nslice;
-    if (fast)
-        recurrent_kernel<D, MODE, true><<<static_cast<unsigned>(grid), kRecThreads, 0, st>>>(*a, nslice);
-    else
-        recurrent_kernel<D, MODE, false><<<static_cast<unsigned>(grid), kRecThreads, 0, st>>>(*a, nslice);
+    const int64_t items = static_cast<int64_t>(a->num_req) * a->head_count * nslice;
+    if (fast) {
+        constexpr size_t smem = static_cast<size_t>(kRingStages) * kBV * D * sizeof(float);
+        // Per device: opt in to the dynamic shared memory once and cache the
+        // resident-CTA count the grid is sized from (a multiple of the SMs).
+        static int per_sm[64];
+        int dev = 0;
+        cudaGetDevice(&dev);
+        dev = (dev >= 0 && dev < 64) ? dev : 0;
+        if (per_sm[dev] == 0) {
+            cudaFuncSetAttribute(recurrent_ring_kernel<D, MODE, kRingStages>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            int n = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, recurrent_ring_kernel<D, MODE, kRingStages>,
+                                                          kRecThreads, smem);
+            per_sm[dev] = n > 0 ? n : 1;
+        }
+        const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm[dev];
+        const int64_t grid = items < cap ? items : cap;
+        recurrent_ring_kernel<D, MODE, kRingStages>
+            <<<static_cast<unsigned>(grid), kRecThreads, smem, st>>>(*a, nslice, items);
+    } else {
+        recurrent_strided_kernel<D, MODE><<<static_cast<unsigned>(items), kRecThreads, 0, st>>>(*a, nslice);
+    }
 }
 
 template <int D>

@@ -268,9 +268,9 @@ def chunk_test_cases(tc):
 
 
 def prepared_triton(bp):
-    """Triton _prepared_recurrent (interpreter), H=4, D=32, tracked."""
+    """Triton _prepared_recurrent (interpreter), H=4, D=64, tracked."""
     import triton
-    H, D, BV, T = 4, 32, 16, 33
+    H, D, BV, T = 4, 64, 16, 33
     torch.manual_seed(99)
     qn = torch.randn(1, T, H, D) * 0.1
     kn = torch.randn(1, T, H, D) * 0.1
