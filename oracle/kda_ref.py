@@ -285,23 +285,25 @@ def prepared_recurrent(qn, kn, v, gdecay, beta, out, state, indices, starts,
 def kda_varlen_recurrent(*, A_log, a, dt_bias, q, k, v, b, initial_state_source,
                          initial_state_indices, cu_seqlens, lower_bound, scale,
                          intermediate_state=None, prefill=False,
-                         track_state_indices=None, track_state_lens=None) -> torch.Tensor:
-    """Oracle for ``sgl_glm53_ascend::kda_varlen_recurrent`` (raw gate)."""
+                         track_state_indices=None, track_state_lens=None,
+                         out_fp32: bool = False) -> torch.Tensor:
+    """Oracle for ``sgl_glm53_ascend::kda_varlen_recurrent`` (raw gate).
+    ``out_fp32`` returns the pre-cast fp32 output instead of the bf16 one."""
     qn, kn, g, beta = prologue_raw(q, k, a, b, A_log, dt_bias, lower_bound, scale)
     o = recurrent(qn, kn, v, g, beta, initial_state_source, initial_state_indices,
                   cu_seqlens, intermediate_state, track_state_indices, track_state_lens)
-    return o.to(torch.bfloat16)
+    return o if out_fp32 else o.to(torch.bfloat16)
 
 
 def kda_varlen_chunk(*, A_log, a, dt_bias, q, k, v, b, initial_state_source,
                      initial_state_indices, cu_seqlens, lower_bound, scale,
                      prefill=False, track_state_indices=None,
-                     track_state_lens=None) -> torch.Tensor:
+                     track_state_lens=None, out_fp32: bool = False) -> torch.Tensor:
     """Oracle for ``sgl_glm53_ascend::kda_varlen_chunk`` (raw gate)."""
     qn, kn, g, beta = prologue_raw(q, k, a, b, A_log, dt_bias, lower_bound, scale)
     o = chunk(qn, kn, v, g, beta, initial_state_source, initial_state_indices,
               cu_seqlens, track_state_indices, track_state_lens)
-    return o.to(torch.bfloat16)
+    return o if out_fp32 else o.to(torch.bfloat16)
 
 
 def kda_varlen_recurrent_g(*, q, k, v, g, beta, initial_state_source,

@@ -18,15 +18,19 @@ STATE_TOL = 1e-3
 
 
 def out_error(out: torch.Tensor, ref: torch.Tensor) -> float:
-    """Normalised max-abs error; bf16 outputs are credited the cast rounding."""
+    """Normalised max-abs error. A bf16 output against an fp32 reference is
+    credited half a bf16 ulp (its own round-to-nearest); against a reference
+    that is itself bf16 (both sides rounded), one ulp."""
+    ref_bf16 = ref.dtype == torch.bfloat16
     ref = ref.detach().float().cpu()
     got = out.detach().cpu()
     rms = ref.pow(2).mean().sqrt().clamp_min(1e-30)
     diff = (got.float() - ref).abs()
     if got.dtype == torch.bfloat16:
         _, e = torch.frexp(ref)
-        half_ulp = torch.ldexp(torch.ones_like(ref), e - 9)   # 2^(e-1-8): half of 2^(e-1-7)
-        diff = (diff - half_ulp).clamp_min(0.0)
+        # ulp of a bf16 in [2^(e-1), 2^e) is 2^(e-8); half of it 2^(e-9).
+        credit = torch.ldexp(torch.ones_like(ref), e - (8 if ref_bf16 else 9))
+        diff = (diff - credit).clamp_min(0.0)
     return float(diff.max() / rms)
 
 
