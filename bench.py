@@ -251,6 +251,87 @@ def bench_decode(args, dist: Dist, hbm_gbs: float, peak_kind: str) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Chunked prefill
+# ---------------------------------------------------------------------------
+
+# Dense tensor-core work per (token, head) of the chunk-64 algorithm at
+# K=V=128 (A_kk, A_qk, W, U, W.S, Q.S, Aqk.V', state update; the triangular
+# solve excluded) and the minimal HBM bytes per (token, head): q/k/v bf16,
+# g fp32, beta, output bf16.
+PREFILL_FLOPS_PER_TOKEN_HEAD = 180224
+PREFILL_BYTES_PER_TOKEN_HEAD = 768 + 512 + 4 + 256
+
+
+def bench_prefill(args, dist: Dist, hbm_gbs: float, bf16_tf: float, steps: int, warmup: int) -> dict:
+    from sgl_glm53_ascend_ops import abi, ops, workloads
+
+    w = workloads.config3(seed=2000 + dist.rank)
+    d = w.to("cuda")
+    kw = d.kwargs()
+    tokens, heads = w.tokens, w.heads
+
+    def step():
+        ops.kda_varlen_chunk_g(**kw, prefill=True)
+
+    ms = time_steps(step, steps, warmup, dist) / steps
+    # The chunk kernel alone through the C ABI (the workspace is allocated once).
+    out = torch.empty_like(d.v)
+    cargs = abi.args_from_tensors(q=d.q, k=d.k, v=d.v, out=out, state=d.pool, indices=d.indices,
+                                  cu_seqlens=d.cu_seqlens, scale=d.scale, gate_mode=abi.KDA_GATE_LOG,
+                                  g=d.g, beta=d.beta)
+    nws = abi.chunk_workspace_bytes(w.indices.numel(), tokens, heads, w.dim)
+    ws = torch.empty(max(nws, 1), dtype=torch.uint8, device="cuda")
+
+    def launch():
+        rc = abi.chunk_launch(cargs, ws, nws)
+        if rc != 0:
+            raise RuntimeError(f"kda_chunk_launch: {abi.status_string(rc)}")
+
+    kms = time_steps(launch, steps, warmup, dist) / steps
+    flops = tokens * heads * PREFILL_FLOPS_PER_TOKEN_HEAD
+    min_bytes = tokens * heads * PREFILL_BYTES_PER_TOKEN_HEAD + 2 * len(w.lengths) * heads * 65536
+    tflops = flops / (kms / 1e3) / 1e12
+    floor_ms = max(flops / (bf16_tf * 1e12), min_bytes / (hbm_gbs * 1e9)) * 1e3
+    return {
+        "metric": "KDA prefill tokens/s (chunk-64, configs[2])",
+        "value": round(dist.world * tokens / (ms / 1e3), 1),
+        "unit": "tokens/s",
+        "ms_per_step": round(ms, 4),
+        "steps": steps,
+        "warmup": warmup,
+        "config": {"workload": f"cfg3: 8 varlen sequences {w.lengths} (total {tokens}), H=32, K=V=128, "
+                               "zero initial state, log-gate op",
+                   "l2": "inputs larger than L2 (1.4 GB per step), no flush"},
+        "roofline": {"bound": "hbm", "achieved": round(min_bytes / (kms / 1e3) / 1e9, 1), "peak": hbm_gbs,
+                     "unit": "GB/s", "frac": round(min_bytes / (kms / 1e3) / 1e9 / hbm_gbs, 4),
+                     "traffic": None, "kernel_us": round(kms * 1e3, 1), "algorithmic_bytes": min_bytes,
+                     "tensor_tflops": round(tflops, 1), "tensor_frac": round(tflops / bf16_tf, 4),
+                     "attainable_frac": round(floor_ms / kms, 4),
+                     "note": "algorithmic FLOPs 180,224/token-head (bf16x3 split issues 3x that on the "
+                             "tensor pipe); attainable = max(flop floor, byte floor) / time"},
+        "gpu_launches": 2 * steps,
+    }
+
+
+def cpu_prefill_rate(tokens: int, budget_s: float, seed: int = 8):
+    """tokens/s of the CPU chunk oracle on one sequence of `tokens` tokens, H=32."""
+    from oracle import kda_ref
+    from sgl_glm53_ascend_ops import workloads
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w = workloads.config3(seed=seed, lengths=[tokens])
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        kda_ref.kda_varlen_chunk_g(**w.kwargs(), out_fp32=True)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return reps * tokens / el, threads, f"{reps} x one {tokens}-token sequence x 32 heads (chunk oracle), {el:.1f} s"
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline (rank 0, N = 1): the oracle port on this host's cores
 # ---------------------------------------------------------------------------
 
@@ -317,8 +398,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-oracle work")
-    ap.add_argument("--mode", choices=("full", "kernel"), default="full",
-                    help="kernel: only the timed decode op loop (for profiler captures)")
+    ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--mode", choices=("full", "kernel", "prefill-kernel"), default="full",
+                    help="kernel / prefill-kernel: only the timed decode / chunk op loop (profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -330,6 +412,14 @@ def main():
 
     dist.init_gpu()
     hbm_gbs, bf16_tf, bf16_tf_sus, peak_kind = _peaks()
+    if args.mode == "prefill-kernel":
+        from sgl_glm53_ascend_ops import ops, workloads
+        kw = workloads.config3(seed=2000 + dist.rank).to("cuda").kwargs()
+        ms = time_steps(lambda: ops.kda_varlen_chunk_g(**kw, prefill=True), args.steps, args.warmup, dist)
+        if dist.rank == 0:
+            print(json.dumps({"mode": "prefill-kernel", "ms_per_step": ms / args.steps}), flush=True)
+        dist.close()
+        return
     if args.mode == "kernel":
         from sgl_glm53_ascend_ops import ops, workloads
         kw = workloads.config2(seed=1000 + dist.rank).to("cuda").kwargs()
@@ -340,10 +430,15 @@ def main():
         return
     dec = bench_decode(args, dist, hbm_gbs, peak_kind)
 
+    pre = bench_prefill(args, dist, hbm_gbs, bf16_tf, steps=args.prefill_steps, warmup=3)
+
     cpu = None
     if dist.rank == 0 and dist.world == 1:
         rate, threads, sample = cpu_decode_rate(32, args.cpu_budget)
         cpu = {"value": round(rate, 2), "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
+        prate, pthreads, psample = cpu_prefill_rate(512, args.cpu_budget)
+        pre["cpu_baseline"] = {"value": round(prate, 2), "unit": "tokens/s", "cores": pthreads, "kind": "port",
+                               "sample": psample}
 
     if dist.rank == 0:
         line = {
@@ -369,6 +464,7 @@ def main():
             "e2e": dec["e2e"],
             "gpu_launches": dec["gpu_launches"],
             "clocks": dec["clocks"],
+            "prefill": pre,
         }
         print(json.dumps(line), flush=True)
     dist.close()

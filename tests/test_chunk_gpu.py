@@ -184,7 +184,7 @@ def test_chunk_equals_recurrent_kernel(ops):
     oa = ops.kda_varlen_chunk(**a, prefill=True)
     ob = ops.kda_varlen_recurrent(**b, prefill=True)
     torch.cuda.synchronize()
-    assert_out_close(oa.cpu(), ob.cpu().float())
+    assert_out_close(oa.cpu(), ob.cpu())          # both bf16: one-ulp credit
     assert_state_close(a["initial_state_source"].cpu()[1:3], b["initial_state_source"].cpu()[1:3])
 
 
