@@ -58,10 +58,10 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # output bf16 256 B.
 DECODE_BYTES_PER_TOKEN_HEAD = 65536 * 2 + 768 + 512 + 4 + 256
 
-# DRAM bytes per decode launch (read + write) from one ncu capture of the
-# decode kernel at the benchmark shape; see profiles/decode_cfg2_ncu.md.
-# None until a capture exists.
-DECODE_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) per launch from one ncu capture of each kernel at
+# the benchmark shape: profiles/decode_cfg2_ncu.md, profiles/chunk_cfg3_ncu.md.
+DECODE_TRAFFIC_PER_LAUNCH = 1026264832
+PREFILL_TRAFFIC_PER_LAUNCH = 1670459648
 
 METRIC = "KDA tokens/s (prefill, decode) H32 d128 @1/2/4/8 B200; decode HBM GB/s vs peak"
 
@@ -304,7 +304,8 @@ def bench_prefill(args, dist: Dist, hbm_gbs: float, bf16_tf: float, steps: int, 
                    "l2": "inputs larger than L2 (1.4 GB per step), no flush"},
         "roofline": {"bound": "hbm", "achieved": round(min_bytes / (kms / 1e3) / 1e9, 1), "peak": hbm_gbs,
                      "unit": "GB/s", "frac": round(min_bytes / (kms / 1e3) / 1e9 / hbm_gbs, 4),
-                     "traffic": None, "kernel_us": round(kms * 1e3, 1), "algorithmic_bytes": min_bytes,
+                     "traffic": PREFILL_TRAFFIC_PER_LAUNCH, "kernel_us": round(kms * 1e3, 1),
+                     "algorithmic_bytes": min_bytes,
                      "tensor_tflops": round(tflops, 1), "tensor_frac": round(tflops / bf16_tf, 4),
                      "attainable_frac": round(floor_ms / kms, 4),
                      "note": "algorithmic FLOPs 180,224/token-head (bf16x3 split issues 3x that on the "
