@@ -36,6 +36,8 @@
 
 #include "kda_common.cuh"
 
+#include <mutex>
+
 namespace kda {
 namespace chunk {
 
@@ -941,4 +943,54 @@ extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t wor
                                              : kda::launch_chunk<64, KDA_GATE_LOG>(args, order, st);
     if (rc != KDA_OK) return rc;
     return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of kda_chunk_launch
+//
+// Some callers cannot hand this library a workspace: a host that reserved
+// (almost) all device memory for its own pools before the first call, or a
+// runtime bound through a foreign-function layer that has no device allocator
+// at all. For them the only scratch this operator needs -- the longest-first
+// request order, one int32 per request -- lives in a fixed array inside the
+// library instead. It holds KDA_CHUNK_STATIC_MAX_REQUESTS entries (4 KiB);
+// every GPU that loads the library carries one copy until the process exits.
+// ---------------------------------------------------------------------------
+
+static __device__ __align__(256) int32_t g_chunk_order_scratch[KDA_CHUNK_STATIC_MAX_REQUESTS];
+
+namespace kda {
+
+// Device address of the scratch array on the current device. Looked up once
+// per device (with that device current) and cached; the array's host-side
+// name is only a handle and must never reach a kernel.
+static int chunk_static_scratch(int32_t **out) {
+    static std::mutex mu;
+    static int32_t *addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KDA_ERR_LAUNCH;
+    std::lock_guard<std::mutex> lk(mu);
+    if (addr[dev] == nullptr) {
+        void *ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_chunk_order_scratch) != cudaSuccess || ptr == nullptr)
+            return KDA_ERR_LAUNCH;
+        addr[dev] = static_cast<int32_t *>(ptr);
+    }
+    *out = addr[dev];
+    return KDA_OK;
+}
+
+}  // namespace kda
+
+extern "C" int kda_chunk_launch_no_alloc(const KdaArgs *args, void *stream) {
+    if (args == nullptr) return KDA_ERR_INVALID_ARGUMENT;
+    if (args->num_req > KDA_CHUNK_STATIC_MAX_REQUESTS) return KDA_ERR_TOO_LARGE;
+    int32_t *scratch = nullptr;
+    if (args->num_req > 0) {
+        const int rc = kda::chunk_static_scratch(&scratch);
+        if (rc != KDA_OK) return rc;
+    }
+    // The order kernel rewrites entries [0, num_req) on every call, so the
+    // array needs no clearing; only concurrent calls would interfere.
+    return kda_chunk_launch(args, scratch, sizeof(int32_t) * KDA_CHUNK_STATIC_MAX_REQUESTS, stream);
 }

@@ -539,6 +539,7 @@ extern "C" const char *kda_status_string(int code) {
         case KDA_ERR_ALIGNMENT: return "pointer or stride not 16-byte aligned";
         case KDA_ERR_WORKSPACE: return "workspace missing or too small";
         case KDA_ERR_LAUNCH: return "CUDA launch failed";
+        case KDA_ERR_TOO_LARGE: return "batch beyond the fixed in-library scratch capacity";
         case KDA_DEVICE_ERR_WAIT_TIMEOUT: return "device: bounded mbarrier wait expired";
         case KDA_DEVICE_ERR_BAD_SLOT: return "device: state slot index out of range";
         case KDA_DEVICE_ERR_BAD_SEQLENS: return "device: cu_seqlens not monotone or beyond T";

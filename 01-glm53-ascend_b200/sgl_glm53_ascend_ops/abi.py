@@ -29,6 +29,7 @@ EXPORTED = (
     "kda_chunk_workspace_bytes",
     "kda_chunk_launch",
     "kda_prepared_recurrent_launch",
+    "kda_chunk_launch_no_alloc",
 )
 
 
@@ -85,6 +86,8 @@ def lib() -> ctypes.CDLL:
             getattr(L, name).argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p]
         L.kda_chunk_workspace_bytes.restype = ctypes.c_size_t
         L.kda_chunk_workspace_bytes.argtypes = [ctypes.c_int32] * 4
+        L.kda_chunk_launch_no_alloc.restype = ctypes.c_int
+        L.kda_chunk_launch_no_alloc.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p]
         L.kda_chunk_launch.restype = ctypes.c_int
         L.kda_chunk_launch.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
                                        ctypes.c_void_p]
@@ -159,6 +162,11 @@ def chunk_launch(args: KdaArgs, workspace: Optional[torch.Tensor], workspace_byt
                  stream: Optional[torch.cuda.Stream] = None) -> int:
     return lib().kda_chunk_launch(ctypes.byref(args), _ptr(workspace), workspace_bytes,
                                   stream_handle(stream))
+
+
+def chunk_launch_no_alloc(args: KdaArgs, stream: Optional[torch.cuda.Stream] = None) -> int:
+    """kda_chunk_launch without a caller workspace (scratch inside the library)."""
+    return lib().kda_chunk_launch_no_alloc(ctypes.byref(args), stream_handle(stream))
 
 
 def status_string(code: int) -> str:

@@ -55,7 +55,8 @@ typedef enum KdaStatus {
     KDA_ERR_UNSUPPORTED = 2,      /* head_dim other than 64/128, ... */
     KDA_ERR_ALIGNMENT = 3,        /* a pointer or stride breaks a 16-byte rule */
     KDA_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
-    KDA_ERR_LAUNCH = 5            /* the CUDA launch itself failed */
+    KDA_ERR_LAUNCH = 5,           /* the CUDA launch itself failed */
+    KDA_ERR_TOO_LARGE = 6         /* beyond a fixed in-library capacity */
 } KdaStatus;
 
 /* Codes a kernel may write into *status (first error wins). */
@@ -136,6 +137,25 @@ size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens,
  * (kda_varlen_chunk.h:143-144). `intermediate` must be NULL. */
 int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes,
                      void *stream);
+
+/* Largest batch kda_chunk_launch_no_alloc accepts (its scratch capacity). */
+#define KDA_CHUNK_STATIC_MAX_REQUESTS 1024
+
+/* kda_chunk_launch for callers that cannot provide device memory: the same
+ * prefill, with its only scratch (the longest-first request order, one int32
+ * per request) kept in an array compiled into the library, so this entry
+ * point never allocates. It serves callers whose device memory is already
+ * fully claimed by their own pools, or hosts reaching the library through an
+ * FFI with no device allocator. No counterpart in the reference, which always
+ * allocates its workspace per call.
+ *   - num_req above KDA_CHUNK_STATIC_MAX_REQUESTS returns KDA_ERR_TOO_LARGE.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - All calls on a device share the one array and it keeps the last call's
+ *     contents (each call rewrites what it reads); calls that overlap on the
+ *     GPU, e.g. on two streams, race on it and must be serialised. */
+int kda_chunk_launch_no_alloc(const KdaArgs *args, void *stream);
 
 /* The recurrence on prepared fp32 inputs (gate_mode is forced to
  * KDA_GATE_PREPARED). Replaces the prepared_recurrent_kernel_* launches
