@@ -88,6 +88,10 @@ class Dist:
     def init_gpu(self):
         torch.cuda.set_device(self.local)
         if self.world > 1:
+            # Keep stdout to the one JSON line: NCCL prints its version banner
+            # at init unless its log level is WARN or quieter.
+            if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+                os.environ["NCCL_DEBUG"] = "WARN"
             import torch.distributed as dist
             dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                     device_id=torch.device("cuda", self.local))
