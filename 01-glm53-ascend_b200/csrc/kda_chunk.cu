@@ -1,5 +1,5 @@
 // Chunk-64 WY/UT prefill of the GLM KDA operator on sm_100a, behind
-// kda_chunk_launch / kda_chunk_workspace_bytes.
+// kda_chunk_launch / kda_chunk_workspace_bytes / kda_chunk_launch_no_alloc.
 //
 // Math per chunk of BT = 64 tokens (kda_python.py:121-182; reference kernel
 // sgl-glm53-ascend-ops/csrc/kda/chunk/kda_varlen_chunk_kernel.cpp):
@@ -12,27 +12,32 @@
 //   S   <- e^{gc_last} S + (kn e^{gc_last - gc})^T v'
 //
 // B200 design (no counterpart in the reference):
-//   * one CTA per (sequence, head), 8 warps, the whole chunk loop in one CTA;
+//   * one CTA per (sequence, head), 16 warps, the whole chunk loop in one CTA;
 //     requests are visited longest-first (a one-block prologue kernel writes
 //     the order into the workspace).
-//   * tensor-core products use mma.sync bf16 with every inexact fp32 operand
-//     split into hi + lo bf16 and three products (hi.hi + hi.lo + lo.hi):
-//     plain bf16 operands miss the output bar (5e-3 of the output RMS) by
-//     3-13x on these inputs, the split form lands at ~2e-4.
+//   * every tensor-core product splits each inexact fp32 operand into hi + lo
+//     bf16 and issues three products (hi.hi + hi.lo + lo.hi): plain bf16
+//     operands miss the output bar (5e-3 of the output RMS) by 3-13x on these
+//     inputs, the split form lands at ~2e-4.
 //   * the exponent range is handled with 16-row blocks anchored at their
 //     midpoint row m_I: X = kn e^{gc - m_I}, Y = qn e^{gc - m_I} and
 //     Z = kn e^{m_I - gc} stay within e^{+-8|g|}, and a block pair (I, J)
 //     is X_I (e^{m_I - m_J}) Z_J^T with the factor <= 1 (fp32 exp overflows at
 //     e^88.7; the reference rebases per 32 rows for the same reason,
 //     kda_varlen_chunk.h:24-29).
-//   * the state lives transposed (S^T, value rows x key columns, the pool's
-//     own [V][K] order) in registers: warp w owns value rows [16w, 16w+16) as
-//     mma C fragments, which feed the next product directly as A fragments;
-//     B operands come from swizzled bf16 hi/lo tiles through ldmatrix.
+//   * intra-chunk products (A blocks, W) run on mma.sync with fragments built
+//     in registers; the state scan runs on the 5th-gen tensor core: the state
+//     S^T (value rows x key columns, the pool's own [V][K] order) lives in
+//     tensor memory as a 128-lane fp32 accumulator, its bf16 hi/lo split is
+//     stored back to tensor memory and used as the A operand, and the
+//     intra-chunk results (W, QG, KD, TB, Aqk) are B operands in 128-byte
+//     swizzled shared-memory tiles. One thread issues the tcgen05.mma chain;
+//     warpgroup 0 converts accumulators and writes the output.
 //   * the next chunk's q/k/g (and v) are fetched with cp.async while the W
-//     product and the state scan of this chunk run.
+//     product and the scan of this chunk run.
 //   * any sequence length: a partial last chunk is zero-filled (k = q = v =
 //     g = beta = 0), which leaves the state and the real rows unchanged.
+//   * every mbarrier wait is bounded; tensor memory is freed on every path.
 
 #include "kda_common.cuh"
 
@@ -42,8 +47,7 @@ namespace kda {
 namespace chunk {
 
 constexpr int BT = 64;
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kThreads = 512;
 
 // ---------------------------------------------------------------------------
 // mma.sync / ldmatrix / cp.async primitives
@@ -113,30 +117,125 @@ __device__ __forceinline__ int swz(int r, int c) {
 }
 
 // ---------------------------------------------------------------------------
-// Shared-memory map (bytes), for head dim D
+// tcgen05 (5th-gen tensor core) primitives: tensor-memory allocation,
+// single-thread MMA issue, commit to an mbarrier, warp loads/stores of tensor
+// memory, and the shared-memory / instruction descriptors.
 // ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Generic-proxy shared-memory writes -> visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Named barrier for warpgroup 0 (the 128 threads that own the tensor-memory lanes).
+__device__ __forceinline__ void wg0_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] x B[smem desc]
+__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// D[tmem] (+)= A[tmem] x B[smem desc]
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// All previously issued MMAs of this thread arrive on `bar` when complete.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+                 :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+                 :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+                 : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100
+// version bit. Byte offsets: lbo = leading (MN-block) stride, sbo = 8-row
+// group stride.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor: fp32 accumulate, bf16 A and B, dense.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn, bool b_neg) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_neg ? 1u : 0u) << 14) | ((a_mn ? 1u : 0u) << 15) |
+           ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Tensor-memory column map (512 columns allocated; lane = value row).
+constexpr uint32_t kColS = 0;      // fp32 S^T, D columns
+constexpr uint32_t kColSH = 128;   // bf16x2 hi of S^T, D/2 columns
+constexpr uint32_t kColSL = 192;   // bf16x2 lo of S^T
+constexpr uint32_t kColTR = 128;   // fp32 tracked-prefix state, D columns (reuses SH/SL once consumed)
+constexpr uint32_t kColNU = 256;   // fp32 -v'^T, 64 columns
+constexpr uint32_t kColO = 320;    // fp32 o^T, 64 columns
+constexpr uint32_t kColVH = 384;   // bf16x2 hi of v'^T, 32 columns
+constexpr uint32_t kColVL = 416;   // bf16x2 lo of v'^T
+constexpr uint32_t kTmemCols = 512;
+
+// ---------------------------------------------------------------------------
+// Shared-memory map (bytes from a 1024-byte aligned base), for head dim D
+// ---------------------------------------------------------------------------
+
+__host__ __device__ constexpr int r1k(int x) { return (x + 1023) / 1024 * 1024; }
+
+// bf16 tiles of 64 rows use 64-column blocks in the canonical 128-byte swizzle
+// atom (8 rows x 128 B, 16-byte chunk c of row r at c ^ (r & 7)): element
+// (r, c) of a 64 x C tile sits at (c / 64) * 4096 + swz<64>(r, c % 64).
+__device__ __forceinline__ int f64(int r, int c) { return ((c >> 6) << 12) + swz<64>(r, c & 63); }
 
 template <int D>
 struct Smem {
     static constexpr int FS = D + 8;                       // fp32 tile row stride (conflict-free float2)
     static constexpr int AS = BT + 4;                      // fp32 64x64 tile row stride
-    static constexpr int kRawQ = 0;                        // bf16 [64][D]   q of the chunk
+    static constexpr int kRawQ = 0;                        // bf16 [64][D]   q of the chunk (plain rows)
     static constexpr int kRawK = kRawQ + BT * D * 2;       // bf16 [64][D]   k
     static constexpr int kRawG = kRawK + BT * D * 2;       // fp32 [64][D]   g (bf16 a for the raw gate)
     static constexpr int kRawEnd = kRawG + BT * D * 4;
-    // A' and T (fp32 [64][AS]) alias the raw region once X/Y/Z are built.
+    // A' and T (fp32 [64][AS]) alias the raw region once X/Y/Z are built;
+    // the tracked-prefix operand K_r (hi at kRawQ, lo at kRawK) as well.
     static constexpr int kAp = 0;
     static constexpr int kT = kAp + BT * AS * 4;
-    static constexpr int kRawBytes = (kRawEnd > kT + BT * AS * 4) ? kRawEnd : kT + BT * AS * 4;
-    static constexpr int kV = kRawBytes;                   // bf16 [64][D] swizzled, v of the chunk
-    static constexpr int kX = kV + BT * D * 2;             // fp32 [64][FS]  X, then W hi/lo
-    static constexpr int kY = kX + BT * FS * 4;            // fp32 [64][FS]  Y, then QG hi/lo
-    static constexpr int kZ = kY + BT * FS * 4;            // fp32 [64][FS]  Z, then KD hi/lo
-    static constexpr int kTBh = kZ + BT * FS * 4;          // bf16 [64][64] swizzled
+    static constexpr int kV = r1k(kRawEnd > kT + BT * AS * 4 ? kRawEnd : kT + BT * AS * 4);  // bf16 f64 tile [j][v]
+    static constexpr int kX = r1k(kV + BT * D * 2);        // fp32 [64][FS]  X, then W hi/lo (f64 tiles)
+    static constexpr int kY = r1k(kX + BT * FS * 4);       // fp32 [64][FS]  Y, then QG hi/lo
+    static constexpr int kZ = r1k(kY + BT * FS * 4);       // fp32 [64][FS]  Z, then KD hi/lo
+    static constexpr int kTBh = r1k(kZ + BT * FS * 4);     // bf16 [64][64] swizzled
     static constexpr int kTBl = kTBh + BT * BT * 2;
     static constexpr int kAQh = kTBl + BT * BT * 2;
     static constexpr int kAQl = kAQh + BT * BT * 2;
-    static constexpr int kVec = kAQl + BT * BT * 2;        // fp32 vectors below
+    static constexpr int kBar = kAQl + BT * BT * 2;        // 2 mbarriers + tensor-memory base slot
+    static constexpr int kVec = kBar + 32;                 // fp32 vectors below
     // vector offsets in floats from kVec
     static constexpr int vRq = 0, vRk = 64, vBeta = 128;
     static constexpr int vM = 192;                         // [4][D] anchors m_I
@@ -150,7 +249,8 @@ struct Smem {
     static constexpr int vEtr = vGtr + D;                  // [D]    e^{gtr}
     static constexpr int vEnd = vEtr + D;
     static constexpr int kBytes = kVec + vEnd * 4;
-    static_assert(kBytes <= 232448, "chunk kernel shared memory exceeds the 227 KiB per-CTA limit");
+    static constexpr int kAlloc = kBytes + 1024;           // room to align the base to 1024 B
+    static_assert(kAlloc <= 232448, "chunk kernel shared memory exceeds the 227 KiB per-CTA limit");
 };
 
 // Block pair index p -> (I, J), J <= I, in the order (0,0) (1,0) (1,1) (2,0) ...
@@ -207,11 +307,11 @@ template <int D, int MODE>
 __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, const int32_t *order) {
     using L = Smem<D>;
     constexpr int KS = D / 16;              // k-steps over the key dim
-    constexpr int NPART = kThreads / D;     // row parts of the column-per-thread mapping
-    constexpr int RPT = BT / NPART;         // rows per thread in that mapping
-    constexpr int SCAN_WARPS = D / 16;      // warps that own 16 value rows each
+    constexpr int ELEM = 4 * D;             // threads of the column-per-thread passes
+    constexpr int RPT = 16;                 // rows per thread in those passes (one 16-row block)
     constexpr int FS = L::FS, AS = L::AS;
-    extern __shared__ __align__(128) unsigned char sm[];
+    extern __shared__ __align__(1024) unsigned char sm_raw[];
+    unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
     uint16_t *const rawQ = reinterpret_cast<uint16_t *>(sm + L::kRawQ);
     uint16_t *const rawK = reinterpret_cast<uint16_t *>(sm + L::kRawK);
     float *const rawG = reinterpret_cast<float *>(sm + L::kRawG);
@@ -234,6 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
     uint16_t *const TBl = reinterpret_cast<uint16_t *>(sm + L::kTBl);
     uint16_t *const AQh = reinterpret_cast<uint16_t *>(sm + L::kAQh);
     uint16_t *const AQl = reinterpret_cast<uint16_t *>(sm + L::kAQl);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(sm + L::kBar);
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 16);
     float *const vec = reinterpret_cast<float *>(sm + L::kVec);
     const uint32_t s_base = smem_addr(sm);
 
@@ -267,17 +369,23 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
     const int nchunks = static_cast<int>((eos - bos + BT - 1) / BT);
     const int64_t s0 = p.state_stride[0], s1 = p.state_stride[1], sk = p.state_stride[2], sv = p.state_stride[3];
 
-    // Column-per-thread mapping of the elementwise passes.
+    // Column-per-thread mapping of the elementwise passes: column kc, rows
+    // [16 pt, 16 pt + 16) -- one anchor block per thread.
+    const bool elem = tid < ELEM;
     const int kc = tid % D, pt = tid / D;
     float dtb = 0.f, expA = 0.f;
     if constexpr (MODE == KDA_GATE_RAW) {
-        dtb = __ldg(p.dt_bias + h * D + kc);
+        if (elem) dtb = __ldg(p.dt_bias + h * D + kc);
         expA = expf(__ldg(p.A_log + h));
     }
 
+    auto chunk_rows = [&](int c) {
+        const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
+        return static_cast<int>(eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT));
+    };
     auto issue_qkg = [&](int c) {
         const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
-        const int n = static_cast<int>((eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT)));
+        const int n = chunk_rows(c);
         constexpr int CPR = D / 8;
         for (int e = tid; e < BT * CPR; e += kThreads) {
             const int i = e / CPR, cc = e % CPR;
@@ -298,15 +406,17 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
             }
         }
     };
-    auto issue_v = [&](int c) {
+    // v rows as the MN-major A tile [j][v] of the first scan product; issued
+    // by `nthreads` threads starting at thread 0.
+    auto issue_v = [&](int c, int nthreads) {
         const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
-        const int n = static_cast<int>((eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT)));
+        const int n = chunk_rows(c);
         constexpr int CPR = D / 8;
-        for (int e = tid; e < BT * CPR; e += kThreads) {
+        for (int e = tid; e < BT * CPR; e += nthreads) {
             const int i = e / CPR, cc = e % CPR;
             const bool ok = i < n;
             const int64_t off = (ok ? ((t0 + i) * H + h) * D : 0) + cc * 8;
-            cp_async16(Vt + swz<D>(i, cc * 8), static_cast<const uint16_t *>(p.v) + off, ok);
+            cp_async16(Vt + f64(i, cc * 8), static_cast<const uint16_t *>(p.v) + off, ok);
         }
     };
     float bnext = 0.f;   // beta (or raw b) of row `tid` of the next chunk
@@ -320,49 +430,57 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         }
     };
 
-    // ---- state S^T in registers: warp w < SCAN_WARPS owns value rows
-    // [16w, 16w + 16); fragment S[nt] covers key columns [8nt, 8nt + 8). ----
-    const bool scan_warp = warp < SCAN_WARPS;
-    const int vr = warp * 16 + g;                      // rows vr, vr + 8
-    float S[D / 8][4];
-    {
-        const float *hs = p.state + slot * s0 + h * s1;
-#pragma unroll
-        for (int nt = 0; nt < D / 8; ++nt) {
-            const int k = nt * 8 + 2 * t4;
-            const bool ld = scan_warp && slot > 0;
-            S[nt][0] = ld ? hs[vr * sv + k * sk] : 0.f;
-            S[nt][1] = ld ? hs[vr * sv + (k + 1) * sk] : 0.f;
-            S[nt][2] = ld ? hs[(vr + 8) * sv + k * sk] : 0.f;
-            S[nt][3] = ld ? hs[(vr + 8) * sv + (k + 1) * sk] : 0.f;
-        }
+    // ---- tensor memory, mbarriers ----
+    if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
     }
-    auto store_state = [&](float *hs) {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const bool wg0 = tid < 128;                  // owns tensor-memory lane `tid` = value row
+    const int vrow = tid;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(warp * 32) << 16);   // this warp's lane quadrant
+
+    // Initial state S^T row `vrow` -> tensor memory (zero for slot 0 and the
+    // padding rows of D = 64); a length-0 prefix checkpoint is the initial state.
+    if (wg0) {
+        const float *hs = p.state + slot * s0 + h * s1;
+        float *ts = p.state + tslot * s0 + h * s1;
+        const bool row_ok = vrow < D;
 #pragma unroll
-        for (int nt = 0; nt < D / 8; ++nt) {
-            const int k = nt * 8 + 2 * t4;
-            hs[vr * sv + k * sk] = S[nt][0];
-            hs[vr * sv + (k + 1) * sk] = S[nt][1];
-            hs[(vr + 8) * sv + k * sk] = S[nt][2];
-            hs[(vr + 8) * sv + (k + 1) * sk] = S[nt][3];
+        for (int c32 = 0; c32 < D / 32; ++c32) {
+            uint32_t r[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const int k = c32 * 32 + e;
+                const float x = (slot > 0 && row_ok) ? hs[vrow * sv + k * sk] : 0.f;
+                r[e] = __float_as_uint(x);
+                if (row_ok && tslot > 0 && tlen == 0) ts[vrow * sv + k * sk] = x;
+            }
+            tmem_st32(tl + kColS + 32 * c32, r);
         }
-    };
-    if (scan_warp && tslot > 0 && tlen == 0) store_state(p.state + tslot * s0 + h * s1);
+        tmem_st_wait();
+    }
 
     if (nchunks > 0) {
         issue_qkg(0);
-        issue_v(0);
+        issue_v(0, kThreads);
         cp_async_commit();
         load_beta(0);
     }
 
     for (int c = 0; c < nchunks; ++c) {
         const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
-        const int n = static_cast<int>((eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT)));
+        const int n = chunk_rows(c);
         const int64_t rtrack = tlen - static_cast<int64_t>(c) * BT;
         const bool track_here = tslot > 0 && rtrack > 0 && rtrack <= BT;
         const bool has_next = c + 1 < nchunks;
         cp_async_wait_all();
+        fence_async_smem();
         __syncthreads();
 
         // ---- P1: beta, row norms (scale folded into q), gate cumsum ----
@@ -380,8 +498,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
             const int grp = tid >> 4, l16 = tid & 15;
             constexpr int EPL = D / 16;             // elements per lane of a row
 #pragma unroll
-            for (int it = 0; it < 8; ++it) {
-                const int rowid = grp + 16 * it;   // 0..63 q rows, 64..127 k rows
+            for (int it = 0; it < 4; ++it) {
+                const int rowid = grp + 32 * it;   // 0..63 q rows, 64..127 k rows
                 const int row = rowid & 63;
                 const uint16_t *src = (rowid >= 64 ? rawK : rawQ) + row * D + l16 * EPL;
                 float ss = 0.f;
@@ -406,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         float gcr[RPT];
         const int trow = track_here ? static_cast<int>(rtrack) - 1 : -1;   // gc row of the checkpoint
         float gtr = 0.f;
-        {
+        if (elem) {
             float acc = 0.f;
 #pragma unroll
             for (int i = 0; i < RPT; ++i) {
@@ -422,10 +540,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
                 gcr[i] = acc;
                 gtr = (row == trow) ? acc : gtr;
             }
-            if (pt < NPART - 1) vec[L::vTot + pt * D + kc] = acc;
+            if (pt < 3) vec[L::vTot + pt * D + kc] = acc;
         }
         __syncthreads();
-        {
+        if (elem) {
             float off = 0.f;
             for (int q = 0; q < pt; ++q) off += vec[L::vTot + q * D + kc];
 #pragma unroll
@@ -435,21 +553,24 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         __syncthreads();   // vTot is read; vF (its alias) is written below
 
         // ---- P2a: anchors, last/tracked gate rows, X/Y/Z ----
+        if (elem) {
+            const float m = gcr[8];
+            vec[L::vM + pt * D + kc] = m;
+            if (pt == 3) vec[L::vGl + kc] = gcr[RPT - 1];
+            if (trow >= 0 && trow / RPT == pt) vec[L::vGtr + kc] = gtr;
 #pragma unroll
-        for (int lb = 0; lb < RPT / 16; ++lb) vec[L::vM + (pt * RPT / 16 + lb) * D + kc] = gcr[lb * 16 + 8];
-        if (pt == NPART - 1) vec[L::vGl + kc] = gcr[RPT - 1];
-        if (trow >= 0 && trow / RPT == pt) vec[L::vGtr + kc] = gtr;
-#pragma unroll
-        for (int i = 0; i < RPT; ++i) {
-            const int row = pt * RPT + i;
-            const float m = gcr[(i / 16) * 16 + 8];
-            const float x = gcr[i] - m;
-            const float E = expf(x), Ei = expf(-x);
-            const float kn = __uint_as_float(static_cast<uint32_t>(rawK[row * D + kc]) << 16) * vec[L::vRk + row];
-            const float qn = __uint_as_float(static_cast<uint32_t>(rawQ[row * D + kc]) << 16) * vec[L::vRq + row];
-            X[row * FS + kc] = kn * E;
-            Y[row * FS + kc] = qn * E;
-            Z[row * FS + kc] = kn * Ei;
+            for (int i = 0; i < RPT; ++i) {
+                const int row = pt * RPT + i;
+                const float x = gcr[i] - m;
+                const float E = expf(x), Ei = expf(-x);
+                const float kn =
+                    __uint_as_float(static_cast<uint32_t>(rawK[row * D + kc]) << 16) * vec[L::vRk + row];
+                const float qn =
+                    __uint_as_float(static_cast<uint32_t>(rawQ[row * D + kc]) << 16) * vec[L::vRq + row];
+                X[row * FS + kc] = kn * E;
+                Y[row * FS + kc] = qn * E;
+                Z[row * FS + kc] = kn * Ei;
+            }
         }
         __syncthreads();
 
@@ -474,10 +595,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         }
         __syncthreads();
 
-        // ---- P3: A' and Aqk, one 16x16 block pair per warp pass ----
-        for (int pidx = warp; pidx < 10; pidx += kWarps) {
+        // ---- P3: A' and Aqk, one 16x16 block pair per warp ----
+        if (warp < 10) {
             int I, J;
-            pair_ij(pidx, I, J);
+            pair_ij(warp, I, J);
             const float *F = (J < I) ? vec + L::vF + fslot(I, J) * D : nullptr;
             float akk[2][4] = {}, aqk[2][4] = {};
             const int ra = 16 * I + g, rb = ra + 8;
@@ -560,13 +681,16 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
             for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
         }
         __syncthreads();
-        {
-            const int i = tid >> 4, j = tid & 15;
 #pragma unroll
-            for (int d = 1; d <= 3; ++d) {
-                float res[3];
+        for (int d = 1; d <= 3; ++d) {
+            // Block pairs (I, J) = (d + q, q); element e = q * 256 + i * 16 + j.
+            const int nel = (4 - d) * 256;
+            float res[2] = {0.f, 0.f};
 #pragma unroll
-                for (int q = 0; q < 4 - d; ++q) {
+            for (int r = 0; r < 2; ++r) {
+                const int e = tid + r * kThreads;
+                if (e < nel) {
+                    const int q = e >> 8, i = (e >> 4) & 15, j = e & 15;
                     const int I = d + q, J = q;
                     float acc = 0.f;
                     for (int M = J; M < I; ++M) {
@@ -575,26 +699,42 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
 #pragma unroll
                         for (int m = 0; m < 16; ++m) acc = fmaf(arow[m], tcol[m * AS], acc);
                     }
-                    res[q] = acc;
+                    res[r] = acc;
                 }
+            }
 #pragma unroll
-                for (int q = 0; q < 4 - d; ++q) Tm[(16 * (d + q) + i) * AS + 16 * q + j] = res[q];
-                __syncthreads();
+            for (int r = 0; r < 2; ++r) {
+                const int e = tid + r * kThreads;
+                if (e < nel) {
+                    const int q = e >> 8, i = (e >> 4) & 15, j = e & 15;
+                    Tm[(16 * (d + q) + i) * AS + 16 * q + j] = res[r];
+                }
+            }
+            __syncthreads();
 #pragma unroll
-                for (int q = 0; q < 4 - d; ++q) {
+            for (int r = 0; r < 2; ++r) {
+                const int e = tid + r * kThreads;
+                if (e < nel) {
+                    const int q = e >> 8, i = (e >> 4) & 15, j = e & 15;
                     const int I = d + q, J = q;
                     const float *trow = Tm + (16 * I + i) * AS + 16 * I;
                     const float *pcol = Tm + (16 * I) * AS + 16 * J + j;
                     float acc = 0.f;
 #pragma unroll
                     for (int m = 0; m < 16; ++m) acc = fmaf(trow[m], pcol[m * AS], acc);
-                    res[q] = -acc;
+                    res[r] = -acc;
                 }
-                __syncthreads();
-#pragma unroll
-                for (int q = 0; q < 4 - d; ++q) Tm[(16 * (d + q) + i) * AS + 16 * q + j] = res[q];
-                __syncthreads();
             }
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int e = tid + r * kThreads;
+                if (e < nel) {
+                    const int q = e >> 8, i = (e >> 4) & 15, j = e & 15;
+                    Tm[(16 * (d + q) + i) * AS + 16 * q + j] = res[r];
+                }
+            }
+            __syncthreads();
         }
 
         // ---- P5: TB = T diag(beta), lower triangle, split into hi/lo ----
@@ -606,6 +746,12 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
             split2(x0, x1, hi, lo);
             *reinterpret_cast<uint32_t *>(TBh + swz<BT>(j, jc)) = hi;
             *reinterpret_cast<uint32_t *>(TBl + swz<BT>(j, jc)) = lo;
+            // Aqk's strictly-upper 16x16 blocks are never computed but are read
+            // by the full-width tensor-core product: make them zero.
+            if ((jc >> 4) > (j >> 4)) {
+                *reinterpret_cast<uint32_t *>(AQh + swz<BT>(j, jc)) = 0u;
+                *reinterpret_cast<uint32_t *>(AQl + swz<BT>(j, jc)) = 0u;
+            }
         }
         __syncthreads();
 
@@ -616,21 +762,17 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
             load_beta(c + 1);
         }
 
-        // ---- P7: W = TB (kn e^{gc}); warp w owns key columns [16w, 16w+16) ----
-        float wacc[4][2][4] = {};
-        if (warp < D / 16) {
-            uint32_t kbh[4][2][2], kbl[4][2][2];
+        // ---- P7: W = TB (kn e^{gc}); warp w owns key columns [8w, 8w+8) ----
+        float wacc[4][4] = {};
+        if (warp < D / 8) {
+            uint32_t kbh[4][2], kbl[4][2];
+            const int kcol = 8 * warp + g;
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const int kcol = 16 * warp + 8 * nt + g;
-                    const int jr = 16 * ks + 2 * t4;
-                    const float e = vec[L::vEm + ks * D + kcol];
-                    split2(X[jr * FS + kcol] * e, X[(jr + 1) * FS + kcol] * e, kbh[ks][nt][0], kbl[ks][nt][0]);
-                    split2(X[(jr + 8) * FS + kcol] * e, X[(jr + 9) * FS + kcol] * e, kbh[ks][nt][1],
-                           kbl[ks][nt][1]);
-                }
+                const int jr = 16 * ks + 2 * t4;
+                const float e = vec[L::vEm + ks * D + kcol];
+                split2(X[jr * FS + kcol] * e, X[(jr + 1) * FS + kcol] * e, kbh[ks][0], kbl[ks][0]);
+                split2(X[(jr + 8) * FS + kcol] * e, X[(jr + 9) * FS + kcol] * e, kbh[ks][1], kbl[ks][1]);
             }
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) {
@@ -639,226 +781,253 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
                     uint32_t ah[4], al[4];
                     ldsm_x4(ah, s_base + L::kTBh + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
                     ldsm_x4(al, s_base + L::kTBl + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-                        mma3(wacc[mt][nt], ah, al, kbh[ks][nt][0], kbh[ks][nt][1], kbl[ks][nt][0], kbl[ks][nt][1]);
+                    mma3(wacc[mt], ah, al, kbh[ks][0], kbh[ks][1], kbl[ks][0], kbl[ks][1]);
                 }
             }
         }
         __syncthreads();   // X fully consumed: W replaces it
-        if (warp < D / 16) {
+        if (warp < D / 8) {
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        const int j = 16 * mt + g + 8 * hf;
-                        const int kcol = 16 * warp + 8 * nt + 2 * t4;
-                        uint32_t hi, lo;
-                        split2(wacc[mt][nt][2 * hf], wacc[mt][nt][2 * hf + 1], hi, lo);
-                        *reinterpret_cast<uint32_t *>(Wh + swz<D>(j, kcol)) = hi;
-                        *reinterpret_cast<uint32_t *>(Wl + swz<D>(j, kcol)) = lo;
-                    }
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int j = 16 * mt + g + 8 * hf;
+                    const int kcol = 8 * warp + 2 * t4;
+                    uint32_t hi, lo;
+                    split2(wacc[mt][2 * hf], wacc[mt][2 * hf + 1], hi, lo);
+                    *reinterpret_cast<uint32_t *>(Wh + f64(j, kcol)) = hi;
+                    *reinterpret_cast<uint32_t *>(Wl + f64(j, kcol)) = lo;
+                }
         }
 
         // ---- P8: QG = Y e^{m_I}, KD = Z e^{gl - m_J}, tracked K_r, in place ----
         {
             uint32_t stage[RPT];
-            const float etr_k = track_here ? vec[L::vGtr + kc] : 0.f;
+            if (elem) {
+                const float gtr_k = track_here ? vec[L::vGtr + kc] : 0.f;
+                const float em = vec[L::vEm + pt * D + kc];
+                const float etrm = track_here ? expf(gtr_k - vec[L::vM + pt * D + kc]) : 0.f;
 #pragma unroll
-            for (int i = 0; i < RPT; ++i) {
-                const int row = pt * RPT + i;
-                const int I = row / 16;
-                uint16_t hi, lo;
-                split1(Y[row * FS + kc] * vec[L::vEm + I * D + kc], hi, lo);
-                stage[i] = static_cast<uint32_t>(hi) | (static_cast<uint32_t>(lo) << 16);
-                if (track_here) {
-                    const float kr = (row < rtrack) ? Z[row * FS + kc] * expf(etr_k - vec[L::vM + I * D + kc]) : 0.f;
-                    split1(kr, hi, lo);
-                    KRh[swz<D>(row, kc)] = hi;
-                    KRl[swz<D>(row, kc)] = lo;
+                for (int i = 0; i < RPT; ++i) {
+                    const int row = pt * RPT + i;
+                    uint16_t hi, lo;
+                    split1(Y[row * FS + kc] * em, hi, lo);
+                    stage[i] = static_cast<uint32_t>(hi) | (static_cast<uint32_t>(lo) << 16);
+                    if (track_here) {
+                        const float kr = (row < rtrack) ? Z[row * FS + kc] * etrm : 0.f;
+                        split1(kr, hi, lo);
+                        KRh[f64(row, kc)] = hi;
+                        KRl[f64(row, kc)] = lo;
+                    }
                 }
             }
             __syncthreads();
+            if (elem) {
 #pragma unroll
-            for (int i = 0; i < RPT; ++i) {
-                const int row = pt * RPT + i;
-                QGh[swz<D>(row, kc)] = static_cast<uint16_t>(stage[i] & 0xffffu);
-                QGl[swz<D>(row, kc)] = static_cast<uint16_t>(stage[i] >> 16);
-            }
+                for (int i = 0; i < RPT; ++i) {
+                    const int row = pt * RPT + i;
+                    QGh[f64(row, kc)] = static_cast<uint16_t>(stage[i] & 0xffffu);
+                    QGl[f64(row, kc)] = static_cast<uint16_t>(stage[i] >> 16);
+                }
+                const float eg = vec[L::vEglm + pt * D + kc];
 #pragma unroll
-            for (int i = 0; i < RPT; ++i) {
-                const int row = pt * RPT + i;
-                uint16_t hi, lo;
-                split1(Z[row * FS + kc] * vec[L::vEglm + (row / 16) * D + kc], hi, lo);
-                stage[i] = static_cast<uint32_t>(hi) | (static_cast<uint32_t>(lo) << 16);
+                for (int i = 0; i < RPT; ++i) {
+                    const int row = pt * RPT + i;
+                    uint16_t hi, lo;
+                    split1(Z[row * FS + kc] * eg, hi, lo);
+                    stage[i] = static_cast<uint32_t>(hi) | (static_cast<uint32_t>(lo) << 16);
+                }
             }
             __syncthreads();
+            if (elem) {
 #pragma unroll
-            for (int i = 0; i < RPT; ++i) {
-                const int row = pt * RPT + i;
-                KDh[swz<D>(row, kc)] = static_cast<uint16_t>(stage[i] & 0xffffu);
-                KDl[swz<D>(row, kc)] = static_cast<uint16_t>(stage[i] >> 16);
+                for (int i = 0; i < RPT; ++i) {
+                    const int row = pt * RPT + i;
+                    KDh[f64(row, kc)] = static_cast<uint16_t>(stage[i] & 0xffffu);
+                    KDl[f64(row, kc)] = static_cast<uint16_t>(stage[i] >> 16);
+                }
             }
         }
+        fence_async_smem();   // tiles written by threads -> read by the tensor core
         __syncthreads();
 
-        // ---- P9: the scan, each warp on its 16 value rows ----
-        float U[8][4] = {};   // u^T, then -v'^T  (value rows x 64 chunk rows)
-        if (scan_warp) {
+        // ---- P9: the state scan on the 5th-gen tensor core (warpgroup 0) ----
+        if (wg0) {
+            const uint32_t ph = static_cast<uint32_t>(c & 1);
+            // S^T -> bf16 hi/lo A operand (unscaled chunk-start state).
 #pragma unroll
-            for (int np = 0; np < 4; ++np) {
+            for (int c32 = 0; c32 < D / 32; ++c32) {
+                uint32_t r[32], hi[16], lo[16];
+                tmem_ld32(tl + kColS + 32 * c32, r);
+                tmem_ld_wait();
 #pragma unroll
-                for (int ks = 0; ks <= np; ++ks) {
-                    uint32_t av[4], bh[4], bl[4];
-                    ldsm_x4_t(av, s_base + L::kV + 2 * lda_a_km<D>(lane, warp * 16, 16 * ks));
-                    ldsm_x4(bh, s_base + L::kTBh + 2 * lda_b_nk<BT>(lane, 16 * np, 16 * ks));
-                    ldsm_x4(bl, s_base + L::kTBl + 2 * lda_b_nk<BT>(lane, 16 * np, 16 * ks));
-                    mma16816(U[2 * np], av, bl[0], bl[1]);
-                    mma16816(U[2 * np], av, bh[0], bh[1]);
-                    mma16816(U[2 * np + 1], av, bl[2], bl[3]);
-                    mma16816(U[2 * np + 1], av, bh[2], bh[3]);
+                for (int e = 0; e < 16; ++e)
+                    split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+                tmem_st16(tl + kColSH + 16 * c32, hi);
+                tmem_st16(tl + kColSL + 16 * c32, lo);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            wg0_sync();
+            if (tid == 0) {
+                tc_fence_after();
+                constexpr uint32_t id_v = idesc_bf16(128, 64, true, false, true);     // -(v^T TB^T)
+                constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t a = sdesc(s_base + L::kV + kk * 2048, 8192, 1024);
+                    umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBh + kk * 32, 16, 1024), id_v, kk > 0 ? 1u : 0u);
+                    umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBl + kk * 32, 16, 1024), id_v, 1u);
                 }
-            }
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) U[nt][e] = -U[nt][e];
-        }
-        __syncthreads();   // the v tile is consumed: fetch the next one
-        if (has_next && !track_here) {
-            issue_v(c + 1);
-            cp_async_commit();
-        }
-        if (scan_warp) {
-            float O[8][4] = {};
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                uint32_t sh[4], sl[4];
-                split2(S[2 * ks][0], S[2 * ks][1], sh[0], sl[0]);
-                split2(S[2 * ks][2], S[2 * ks][3], sh[1], sl[1]);
-                split2(S[2 * ks + 1][0], S[2 * ks + 1][1], sh[2], sl[2]);
-                split2(S[2 * ks + 1][2], S[2 * ks + 1][3], sh[3], sl[3]);
-#pragma unroll
-                for (int np = 0; np < 4; ++np) {
-                    uint32_t bh[4], bl[4];
-                    ldsm_x4(bh, s_base + L::kX + 2 * lda_b_nk<D>(lane, 16 * np, 16 * ks));
-                    ldsm_x4(bl, s_base + L::kX + 2 * BT * D + 2 * lda_b_nk<D>(lane, 16 * np, 16 * ks));
-                    mma3(U[2 * np], sh, sl, bh[0], bh[1], bl[0], bl[1]);
-                    mma3(U[2 * np + 1], sh, sl, bh[2], bh[3], bl[2], bl[3]);
-                    ldsm_x4(bh, s_base + L::kY + 2 * lda_b_nk<D>(lane, 16 * np, 16 * ks));
-                    ldsm_x4(bl, s_base + L::kY + 2 * BT * D + 2 * lda_b_nk<D>(lane, 16 * np, 16 * ks));
-                    mma3(O[2 * np], sh, sl, bh[0], bh[1], bl[0], bl[1]);
-                    mma3(O[2 * np + 1], sh, sl, bh[2], bh[3], bl[2], bl[3]);
+                for (int kk = 0; kk < KS; ++kk) {
+                    const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
+                    const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
+                    const uint64_t wh = sdesc(s_base + L::kX + off, 16, 1024);
+                    const uint64_t wl = sdesc(s_base + L::kX + BT * D * 2 + off, 16, 1024);
+                    umma_ts(tmem + kColNU, al, wh, id_n64, 1u);
+                    umma_ts(tmem + kColNU, ah, wl, id_n64, 1u);
+                    umma_ts(tmem + kColNU, ah, wh, id_n64, 1u);
+                    const uint64_t qh = sdesc(s_base + L::kY + off, 16, 1024);
+                    const uint64_t ql = sdesc(s_base + L::kY + BT * D * 2 + off, 16, 1024);
+                    umma_ts(tmem + kColO, al, qh, id_n64, kk > 0 ? 1u : 0u);
+                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
                 }
+                umma_commit(&bars[0]);
             }
-            // v'^T fragments (A operand over the chunk rows j), from -U.
-            uint32_t vh[4][4], vl[4][4];
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                split2(-U[2 * ks][0], -U[2 * ks][1], vh[ks][0], vl[ks][0]);
-                split2(-U[2 * ks][2], -U[2 * ks][3], vh[ks][1], vl[ks][1]);
-                split2(-U[2 * ks + 1][0], -U[2 * ks + 1][1], vh[ks][2], vl[ks][2]);
-                split2(-U[2 * ks + 1][2], -U[2 * ks + 1][3], vh[ks][3], vl[ks][3]);
+            if (!mbar_wait(&bars[0], ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+            // The v tile is consumed: fetch the next one with this warpgroup.
+            if (has_next && !track_here) {
+                issue_v(c + 1, 128);
+                cp_async_commit();
             }
+            // -v'^T (fp32) -> v'^T hi/lo A operand.
 #pragma unroll
-            for (int np = 0; np < 4; ++np) {
+            for (int c32 = 0; c32 < 2; ++c32) {
+                uint32_t r[32], hi[16], lo[16];
+                tmem_ld32(tl + kColNU + 32 * c32, r);
+                tmem_ld_wait();
 #pragma unroll
-                for (int ks = 0; ks <= np; ++ks) {
-                    uint32_t bh[4], bl[4];
-                    ldsm_x4(bh, s_base + L::kAQh + 2 * lda_b_nk<BT>(lane, 16 * np, 16 * ks));
-                    ldsm_x4(bl, s_base + L::kAQl + 2 * lda_b_nk<BT>(lane, 16 * np, 16 * ks));
-                    mma3(O[2 * np], vh[ks], vl[ks], bh[0], bh[1], bl[0], bl[1]);
-                    mma3(O[2 * np + 1], vh[ks], vl[ks], bh[2], bh[3], bl[2], bl[3]);
+                for (int e = 0; e < 16; ++e)
+                    split2(-__uint_as_float(r[2 * e]), -__uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+                tmem_st16(tl + kColVH + 16 * c32, hi);
+                tmem_st16(tl + kColVL + 16 * c32, lo);
+            }
+            // S^T e^{gl} (the state the update accumulates into) and, for a
+            // tracked prefix, S^T e^{gc_{r-1}} in the freed hi/lo columns.
+#pragma unroll
+            for (int c32 = 0; c32 < D / 32; ++c32) {
+                uint32_t r[32], t[32];
+                tmem_ld32(tl + kColS + 32 * c32, r);
+                tmem_ld_wait();
+                if (track_here) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        t[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEtr + 32 * c32 + e]);
+                    tmem_st32(tl + kColTR + 32 * c32, t);
                 }
+#pragma unroll
+                for (int e = 0; e < 32; ++e)
+                    r[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEgl + 32 * c32 + e]);
+                tmem_st32(tl + kColS + 32 * c32, r);
             }
-            // Output rows of this chunk: o[t0 + i][h][v].
+            tmem_st_wait();
+            tc_fence_before();
+            wg0_sync();
+            if (tid == 0) {
+                tc_fence_after();
+                constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
+                constexpr uint32_t id_kd = idesc_bf16(128, D, false, true, false);
 #pragma unroll
-            for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int i = 8 * nt + 2 * t4 + (e & 1);
-                    const int v = vr + ((e & 2) ? 8 : 0);
-                    if (i < n) {
-                        const int64_t oi = ((t0 + i) * H + h) * D + v;
-                        if (p.out_fp32)
-                            static_cast<float *>(p.out)[oi] = O[nt][e];
-                        else
-                            static_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(O[nt][e]);
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
+                    const uint64_t qh = sdesc(s_base + L::kAQh + kk * 32, 16, 1024);
+                    const uint64_t ql = sdesc(s_base + L::kAQl + kk * 32, 16, 1024);
+                    umma_ts(tmem + kColO, al, qh, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
+                    const uint64_t dh = sdesc(s_base + L::kZ + kk * 2048, 8192, 1024);
+                    const uint64_t dl = sdesc(s_base + L::kZ + BT * D * 2 + kk * 2048, 8192, 1024);
+                    umma_ts(tmem + kColS, al, dh, id_kd, 1u);
+                    umma_ts(tmem + kColS, ah, dl, id_kd, 1u);
+                    umma_ts(tmem + kColS, ah, dh, id_kd, 1u);
+                    if (track_here) {
+                        const uint64_t rh = sdesc(s_base + L::kRawQ + kk * 2048, 8192, 1024);
+                        const uint64_t rl = sdesc(s_base + L::kRawK + kk * 2048, 8192, 1024);
+                        umma_ts(tmem + kColTR, al, rh, id_kd, 1u);
+                        umma_ts(tmem + kColTR, ah, rl, id_kd, 1u);
+                        umma_ts(tmem + kColTR, ah, rh, id_kd, 1u);
                     }
                 }
+                umma_commit(&bars[1]);
             }
-            // Tracked prefix: S_r^T = S^T e^{gc_{r-1}} + v'^T K_r, stored, S unchanged.
-            if (track_here) {
-                float *hs = p.state + tslot * s0 + h * s1;
+            if (!mbar_wait(&bars[1], ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+            // o rows of this chunk: lane = value row, column = chunk row i.
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    float R[D / 16][4];
+            for (int c32 = 0; c32 < 2; ++c32) {
+                uint32_t r[32];
+                tmem_ld32(tl + kColO + 32 * c32, r);
+                tmem_ld_wait();
+                if (vrow < D) {
 #pragma unroll
-                    for (int q = 0; q < D / 16; ++q) {
-                        const int nt = half * (D / 16) + q;
-                        const int k = nt * 8 + 2 * t4;
-                        const float e0 = vec[L::vEtr + k], e1 = vec[L::vEtr + k + 1];
-                        R[q][0] = S[nt][0] * e0;
-                        R[q][1] = S[nt][1] * e1;
-                        R[q][2] = S[nt][2] * e0;
-                        R[q][3] = S[nt][3] * e1;
-                    }
-#pragma unroll
-                    for (int np = 0; np < D / 32; ++np) {
-#pragma unroll
-                        for (int ks = 0; ks < 4; ++ks) {
-                            uint32_t bh[4], bl[4];
-                            const int n0 = half * (D / 2) + 16 * np;
-                            ldsm_x4_t(bh, s_base + L::kRawQ + 2 * lda_b_kn<D>(lane, 16 * ks, n0));
-                            ldsm_x4_t(bl, s_base + L::kRawK + 2 * lda_b_kn<D>(lane, 16 * ks, n0));
-                            mma3(R[2 * np], vh[ks], vl[ks], bh[0], bh[1], bl[0], bl[1]);
-                            mma3(R[2 * np + 1], vh[ks], vl[ks], bh[2], bh[3], bl[2], bl[3]);
+                    for (int e = 0; e < 32; ++e) {
+                        const int i = 32 * c32 + e;
+                        if (i < n) {
+                            const int64_t oi = ((t0 + i) * H + h) * D + vrow;
+                            if (p.out_fp32)
+                                static_cast<float *>(p.out)[oi] = __uint_as_float(r[e]);
+                            else
+                                static_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(__uint_as_float(r[e]));
                         }
                     }
-#pragma unroll
-                    for (int q = 0; q < D / 16; ++q) {
-                        const int k = (half * (D / 16) + q) * 8 + 2 * t4;
-                        hs[vr * sv + k * sk] = R[q][0];
-                        hs[vr * sv + (k + 1) * sk] = R[q][1];
-                        hs[(vr + 8) * sv + k * sk] = R[q][2];
-                        hs[(vr + 8) * sv + (k + 1) * sk] = R[q][3];
-                    }
                 }
             }
-            // State update: S^T = S^T e^{gl} + v'^T KD.
+            if (track_here) {
+                float *ts = p.state + tslot * s0 + h * s1;
 #pragma unroll
-            for (int nt = 0; nt < D / 8; ++nt) {
-                const int k = nt * 8 + 2 * t4;
-                const float e0 = vec[L::vEgl + k], e1 = vec[L::vEgl + k + 1];
-                S[nt][0] *= e0;
-                S[nt][1] *= e1;
-                S[nt][2] *= e0;
-                S[nt][3] *= e1;
-            }
+                for (int c32 = 0; c32 < D / 32; ++c32) {
+                    uint32_t r[32];
+                    tmem_ld32(tl + kColTR + 32 * c32, r);
+                    tmem_ld_wait();
+                    if (vrow < D) {
 #pragma unroll
-            for (int np = 0; np < D / 16; ++np) {
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                    uint32_t bh[4], bl[4];
-                    ldsm_x4_t(bh, s_base + L::kZ + 2 * lda_b_kn<D>(lane, 16 * ks, 16 * np));
-                    ldsm_x4_t(bl, s_base + L::kZ + 2 * BT * D + 2 * lda_b_kn<D>(lane, 16 * ks, 16 * np));
-                    mma3(S[2 * np], vh[ks], vl[ks], bh[0], bh[1], bl[0], bl[1]);
-                    mma3(S[2 * np + 1], vh[ks], vl[ks], bh[2], bh[3], bl[2], bl[3]);
+                        for (int e = 0; e < 32; ++e) ts[vrow * sv + (32 * c32 + e) * sk] = __uint_as_float(r[e]);
+                    }
                 }
             }
         }
         if (track_here && has_next) {
             __syncthreads();   // K_r (raw region) is consumed
             issue_qkg(c + 1);
-            issue_v(c + 1);
+            issue_v(c + 1, kThreads);
             cp_async_commit();
             load_beta(c + 1);
         }
     }
     cp_async_wait_all();
-    if (scan_warp && slot > 0) store_state(p.state + slot * s0 + h * s1);
+    // Final state S^T -> pool slot (padding slot 0 is never written).
+    if (wg0) {
+        float *hs = p.state + slot * s0 + h * s1;
+#pragma unroll
+        for (int c32 = 0; c32 < D / 32; ++c32) {
+            uint32_t r[32];
+            tmem_ld32(tl + kColS + 32 * c32, r);
+            tmem_ld_wait();
+            if (slot > 0 && vrow < D) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) hs[vrow * sv + (32 * c32 + e) * sk] = __uint_as_float(r[e]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
 }
 
 }  // namespace chunk
@@ -882,13 +1051,13 @@ static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
     dev = (dev >= 0 && dev < 64) ? dev : 0;
     if (!opted[dev]) {
         if (cudaFuncSetAttribute(chunk::chunk_kernel<D, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 L::kBytes) != cudaSuccess)
+                                 L::kAlloc) != cudaSuccess)
             return KDA_ERR_LAUNCH;
         opted[dev] = true;
     }
     if (order != nullptr) chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
     const int64_t grid = static_cast<int64_t>(a->num_req) * a->head_count;
-    chunk::chunk_kernel<D, MODE><<<static_cast<unsigned>(grid), chunk::kThreads, L::kBytes, st>>>(*a, order);
+    chunk::chunk_kernel<D, MODE><<<static_cast<unsigned>(grid), chunk::kThreads, L::kAlloc, st>>>(*a, order);
     return KDA_OK;
 }
 
