@@ -33,14 +33,16 @@
 //     intra-chunk results (W, QG, KD, TB, Aqk) are B operands in 128-byte
 //     swizzled shared-memory tiles. One thread issues the tcgen05.mma chain;
 //     warpgroup 0 converts accumulators and writes the output.
-//   * the next chunk's q/k/g (and v) are fetched with cp.async while the W
-//     product and the scan of this chunk run.
+//   * the next chunk's q/k/g (and v) tiles are fetched by TMA (one tensor
+//     map each, the v tile written in the 128-byte swizzle the tensor core
+//     reads) while the W product and the scan of this chunk run.
 //   * any sequence length: a partial last chunk is zero-filled (k = q = v =
 //     g = beta = 0), which leaves the state and the real rows unchanged.
 //   * every mbarrier wait is bounded; tensor memory is freed on every path.
 
 #include "kda_common.cuh"
 
+#include <cuda.h>
 #include <mutex>
 
 namespace kda {
@@ -179,6 +181,23 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
                  : "memory");
 }
 
+// Tiled TMA load of a 3-D box (x = key/value column, y = head, z = token)
+// into shared memory, completing on `bar`. No multicast.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Tensor maps of one launch: q, k, the gate (g fp32, or a bf16 for the raw
+// gate) as [T][H][D] boxes of 64 tokens x D, and v as 64-token x 64-column
+// boxes written with the 128-byte swizzle the tensor core reads.
+struct TmaMaps {
+    CUtensorMap q, k, g, v;
+};
+
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100
 // version bit. Byte offsets: lbo = leading (MN-block) stride, sbo = 8-row
 // group stride.
@@ -234,7 +253,7 @@ struct Smem {
     static constexpr int kTBl = kTBh + BT * BT * 2;
     static constexpr int kAQh = kTBl + BT * BT * 2;
     static constexpr int kAQl = kAQh + BT * BT * 2;
-    static constexpr int kBar = kAQl + BT * BT * 2;        // 2 mbarriers + tensor-memory base slot
+    static constexpr int kBar = kAQl + BT * BT * 2;        // 3 mbarriers + tensor-memory base slot
     static constexpr int kVec = kBar + 32;                 // fp32 vectors below
     // vector offsets in floats from kVec
     static constexpr int vRq = 0, vRk = 64, vBeta = 128;
@@ -304,7 +323,8 @@ __global__ void __launch_bounds__(1024) order_kernel(const KdaArgs p, int32_t *o
 }
 
 template <int D, int MODE>
-__global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, const int32_t *order) {
+__global__ void __launch_bounds__(kThreads, 1)
+    chunk_kernel(const KdaArgs p, const int32_t *order, const __grid_constant__ TmaMaps maps) {
     using L = Smem<D>;
     constexpr int KS = D / 16;              // k-steps over the key dim
     constexpr int ELEM = 4 * D;             // threads of the column-per-thread passes
@@ -335,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
     uint16_t *const AQh = reinterpret_cast<uint16_t *>(sm + L::kAQh);
     uint16_t *const AQl = reinterpret_cast<uint16_t *>(sm + L::kAQl);
     uint64_t *const bars = reinterpret_cast<uint64_t *>(sm + L::kBar);
-    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 16);
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 24);
     float *const vec = reinterpret_cast<float *>(sm + L::kVec);
     const uint32_t s_base = smem_addr(sm);
 
@@ -383,41 +403,23 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
         return static_cast<int>(eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT));
     };
-    auto issue_qkg = [&](int c) {
-        const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
-        const int n = chunk_rows(c);
-        constexpr int CPR = D / 8;
-        for (int e = tid; e < BT * CPR; e += kThreads) {
-            const int i = e / CPR, cc = e % CPR;
-            const bool ok = i < n;
-            const int64_t off = (ok ? ((t0 + i) * H + h) * D : 0) + cc * 8;
-            cp_async16(rawQ + i * D + cc * 8, static_cast<const uint16_t *>(p.q) + off, ok);
-            cp_async16(rawK + i * D + cc * 8, static_cast<const uint16_t *>(p.k) + off, ok);
-            if constexpr (MODE == KDA_GATE_RAW)
-                cp_async16(rawA + i * D + cc * 8, static_cast<const uint16_t *>(p.a) + off, ok);
-        }
-        if constexpr (MODE == KDA_GATE_LOG) {
-            constexpr int CPG = D / 4;
-            for (int e = tid; e < BT * CPG; e += kThreads) {
-                const int i = e / CPG, cc = e % CPG;
-                const bool ok = i < n;
-                const int64_t off = (ok ? ((t0 + i) * H + h) * D : 0) + cc * 4;
-                cp_async16(rawG + i * D + cc * 4, p.g + off, ok);
-            }
-        }
+    // Tiles of chunk c by TMA, issued by thread 0, all completing on bars[2]:
+    // q, k and the gate at once, v (the first scan product's A operand) either
+    // with them or once the previous chunk's product has consumed its tile.
+    constexpr uint32_t kTileBytes =
+        BT * D * 2 * 3 + BT * D * ((MODE == KDA_GATE_RAW) ? 2 : 4);
+    auto issue_v = [&](int c) {
+        const int t0c = static_cast<int>(bos + static_cast<int64_t>(c) * BT);
+#pragma unroll
+        for (int blk = 0; blk < D / 64; ++blk) tma_load_3d(Vt + blk * 4096, &maps.v, 64 * blk, h, t0c, &bars[2]);
     };
-    // v rows as the MN-major A tile [j][v] of the first scan product; issued
-    // by `nthreads` threads starting at thread 0.
-    auto issue_v = [&](int c, int nthreads) {
-        const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
-        const int n = chunk_rows(c);
-        constexpr int CPR = D / 8;
-        for (int e = tid; e < BT * CPR; e += nthreads) {
-            const int i = e / CPR, cc = e % CPR;
-            const bool ok = i < n;
-            const int64_t off = (ok ? ((t0 + i) * H + h) * D : 0) + cc * 8;
-            cp_async16(Vt + f64(i, cc * 8), static_cast<const uint16_t *>(p.v) + off, ok);
-        }
+    auto issue_tiles = [&](int c, bool with_v) {
+        const int t0c = static_cast<int>(bos + static_cast<int64_t>(c) * BT);
+        mbar_arrive_expect_tx(&bars[2], kTileBytes);
+        tma_load_3d(rawQ, &maps.q, 0, h, t0c, &bars[2]);
+        tma_load_3d(rawK, &maps.k, 0, h, t0c, &bars[2]);
+        tma_load_3d(rawG, &maps.g, 0, h, t0c, &bars[2]);
+        if (with_v) issue_v(c);
     };
     float bnext = 0.f;   // beta (or raw b) of row `tid` of the next chunk
     auto load_beta = [&](int c) {
@@ -435,6 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
     if (tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
+        mbar_init(&bars[2], 1);
         fence_mbar_init();
     }
     tc_fence_before();
@@ -444,6 +447,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
     const bool wg0 = tid < 128;                  // owns tensor-memory lane `tid` = value row
     const int vrow = tid;
     const uint32_t tl = tmem + (static_cast<uint32_t>(warp * 32) << 16);   // this warp's lane quadrant
+
+    if (nchunks > 0 && tid == 0) issue_tiles(0, true);
 
     // Initial state S^T row `vrow` -> tensor memory (zero for slot 0 and the
     // padding rows of D = 64); a length-0 prefix checkpoint is the initial state.
@@ -466,12 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         tmem_st_wait();
     }
 
-    if (nchunks > 0) {
-        issue_qkg(0);
-        issue_v(0, kThreads);
-        cp_async_commit();
-        load_beta(0);
-    }
+    if (nchunks > 0) load_beta(0);
 
     for (int c = 0; c < nchunks; ++c) {
         const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
@@ -479,8 +479,25 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         const int64_t rtrack = tlen - static_cast<int64_t>(c) * BT;
         const bool track_here = tslot > 0 && rtrack > 0 && rtrack <= BT;
         const bool has_next = c + 1 < nchunks;
-        cp_async_wait_all();
-        fence_async_smem();
+        if (!mbar_wait(&bars[2], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
+            report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+        if (n < BT) {
+            // The boxes cover 64 tokens; rows past this sequence's end hold the
+            // next sequence (or TMA's zero fill past T): clear them.
+            for (int e = n * (D / 8) + tid; e < BT * (D / 8); e += kThreads) {   // 8-element groups
+                reinterpret_cast<uint4 *>(rawQ)[e] = make_uint4(0u, 0u, 0u, 0u);
+                reinterpret_cast<uint4 *>(rawK)[e] = make_uint4(0u, 0u, 0u, 0u);
+                reinterpret_cast<uint4 *>(Vt)[((e / (D / 8)) * 8 + (e % 8)) + ((e % (D / 8)) / 8) * 512] =
+                    make_uint4(0u, 0u, 0u, 0u);
+                if constexpr (MODE == KDA_GATE_RAW) {
+                    reinterpret_cast<uint4 *>(rawA)[e] = make_uint4(0u, 0u, 0u, 0u);
+                } else {
+                    reinterpret_cast<float4 *>(rawG)[2 * e] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    reinterpret_cast<float4 *>(rawG)[2 * e + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            fence_async_smem();
+        }
         __syncthreads();
 
         // ---- P1: beta, row norms (scale folded into q), gate cumsum ----
@@ -753,12 +770,12 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
                 *reinterpret_cast<uint32_t *>(AQl + swz<BT>(j, jc)) = 0u;
             }
         }
+        fence_async_smem();   // A'/T (generic writes) are overwritten next by bulk copies
         __syncthreads();
 
         // ---- P6: the raw region is free: fetch the next chunk's q/k/g ----
         if (has_next && !track_here) {
-            issue_qkg(c + 1);
-            cp_async_commit();
+            if (tid == 0) issue_tiles(c + 1, false);
             load_beta(c + 1);
         }
 
@@ -854,17 +871,39 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         // ---- P9: the state scan on the 5th-gen tensor core (warpgroup 0) ----
         if (wg0) {
             const uint32_t ph = static_cast<uint32_t>(c & 1);
-            // S^T -> bf16 hi/lo A operand (unscaled chunk-start state).
+            // S^T -> bf16 hi/lo A operand (the unscaled chunk-start state, which
+            // the first product batch reads), and S^T <- S^T e^{gl} in place, the
+            // state the update accumulates into. On a tracked-prefix chunk the
+            // rescale waits until S^T e^{gc_{r-1}} has been taken as well.
 #pragma unroll
-            for (int c32 = 0; c32 < D / 32; ++c32) {
-                uint32_t r[32], hi[16], lo[16];
-                tmem_ld32(tl + kColS + 32 * c32, r);
+            for (int c64 = 0; c64 < D / 64; ++c64) {
+                uint32_t r0[32], r1[32];
+                tmem_ld32(tl + kColS + 64 * c64, r0);
+                tmem_ld32(tl + kColS + 64 * c64 + 32, r1);
                 tmem_ld_wait();
+                {
+                    uint32_t hi[16], lo[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
-                tmem_st16(tl + kColSH + 16 * c32, hi);
-                tmem_st16(tl + kColSL + 16 * c32, lo);
+                    for (int e = 0; e < 16; ++e)
+                        split2(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1]), hi[e], lo[e]);
+                    tmem_st16(tl + kColSH + 32 * c64, hi);
+                    tmem_st16(tl + kColSL + 32 * c64, lo);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        split2(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1]), hi[e], lo[e]);
+                    tmem_st16(tl + kColSH + 32 * c64 + 16, hi);
+                    tmem_st16(tl + kColSL + 32 * c64 + 16, lo);
+                }
+                if (!track_here) {
+                    const float *eg = vec + L::vEgl + 64 * c64;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        r0[e] = __float_as_uint(__uint_as_float(r0[e]) * eg[e]);
+                        r1[e] = __float_as_uint(__uint_as_float(r1[e]) * eg[32 + e]);
+                    }
+                    tmem_st32(tl + kColS + 64 * c64, r0);
+                    tmem_st32(tl + kColS + 64 * c64 + 32, r1);
+                }
             }
             tmem_st_wait();
             tc_fence_before();
@@ -898,40 +937,41 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
             }
             if (!mbar_wait(&bars[0], ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
-            // The v tile is consumed: fetch the next one with this warpgroup.
-            if (has_next && !track_here) {
-                issue_v(c + 1, 128);
-                cp_async_commit();
-            }
+            // The v tile is consumed: fetch the next one.
+            if (has_next && !track_here && tid == 0) issue_v(c + 1);
             // -v'^T (fp32) -> v'^T hi/lo A operand.
-#pragma unroll
-            for (int c32 = 0; c32 < 2; ++c32) {
-                uint32_t r[32], hi[16], lo[16];
-                tmem_ld32(tl + kColNU + 32 * c32, r);
+            {
+                uint32_t r0[32], r1[32], hi[16], lo[16];
+                tmem_ld32(tl + kColNU, r0);
+                tmem_ld32(tl + kColNU + 32, r1);
                 tmem_ld_wait();
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
-                    split2(-__uint_as_float(r[2 * e]), -__uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
-                tmem_st16(tl + kColVH + 16 * c32, hi);
-                tmem_st16(tl + kColVL + 16 * c32, lo);
+                    split2(-__uint_as_float(r0[2 * e]), -__uint_as_float(r0[2 * e + 1]), hi[e], lo[e]);
+                tmem_st16(tl + kColVH, hi);
+                tmem_st16(tl + kColVL, lo);
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    split2(-__uint_as_float(r1[2 * e]), -__uint_as_float(r1[2 * e + 1]), hi[e], lo[e]);
+                tmem_st16(tl + kColVH + 16, hi);
+                tmem_st16(tl + kColVL + 16, lo);
             }
-            // S^T e^{gl} (the state the update accumulates into) and, for a
-            // tracked prefix, S^T e^{gc_{r-1}} in the freed hi/lo columns.
+            // Tracked prefix: S^T e^{gc_{r-1}} into the freed hi/lo columns, then
+            // the deferred S^T e^{gl}.
+            if (track_here) {
 #pragma unroll
-            for (int c32 = 0; c32 < D / 32; ++c32) {
-                uint32_t r[32], t[32];
-                tmem_ld32(tl + kColS + 32 * c32, r);
-                tmem_ld_wait();
-                if (track_here) {
+                for (int c32 = 0; c32 < D / 32; ++c32) {
+                    uint32_t r[32], t[32];
+                    tmem_ld32(tl + kColS + 32 * c32, r);
+                    tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
+                    for (int e = 0; e < 32; ++e) {
                         t[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEtr + 32 * c32 + e]);
+                        r[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEgl + 32 * c32 + e]);
+                    }
                     tmem_st32(tl + kColTR + 32 * c32, t);
+                    tmem_st32(tl + kColS + 32 * c32, r);
                 }
-#pragma unroll
-                for (int e = 0; e < 32; ++e)
-                    r[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEgl + 32 * c32 + e]);
-                tmem_st32(tl + kColS + 32 * c32, r);
             }
             tmem_st_wait();
             tc_fence_before();
@@ -966,22 +1006,30 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
             if (!mbar_wait(&bars[1], ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
             // o rows of this chunk: lane = value row, column = chunk row i.
-#pragma unroll
-            for (int c32 = 0; c32 < 2; ++c32) {
-                uint32_t r[32];
-                tmem_ld32(tl + kColO + 32 * c32, r);
+            {
+                uint32_t r0[32], r1[32];
+                tmem_ld32(tl + kColO, r0);
+                tmem_ld32(tl + kColO + 32, r1);
                 tmem_ld_wait();
                 if (vrow < D) {
+                    const int64_t row_stride = static_cast<int64_t>(H) * D;
+                    const int64_t base = (t0 * H + h) * D + vrow;
+                    if (p.out_fp32) {
+                        float *o = static_cast<float *>(p.out) + base;
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const int i = 32 * c32 + e;
-                        if (i < n) {
-                            const int64_t oi = ((t0 + i) * H + h) * D + vrow;
-                            if (p.out_fp32)
-                                static_cast<float *>(p.out)[oi] = __uint_as_float(r[e]);
-                            else
-                                static_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(__uint_as_float(r[e]));
-                        }
+                        for (int e = 0; e < 32; ++e)
+                            if (e < n) o[e * row_stride] = __uint_as_float(r0[e]);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (32 + e < n) o[(32 + e) * row_stride] = __uint_as_float(r1[e]);
+                    } else {
+                        __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + base;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (e < n) o[e * row_stride] = __float2bfloat16_rn(__uint_as_float(r0[e]));
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (32 + e < n) o[(32 + e) * row_stride] = __float2bfloat16_rn(__uint_as_float(r1[e]));
                     }
                 }
             }
@@ -1001,13 +1049,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(const KdaArgs p, con
         }
         if (track_here && has_next) {
             __syncthreads();   // K_r (raw region) is consumed
-            issue_qkg(c + 1);
-            issue_v(c + 1, kThreads);
-            cp_async_commit();
+            if (tid == 0) issue_tiles(c + 1, true);
             load_beta(c + 1);
         }
     }
-    cp_async_wait_all();
     // Final state S^T -> pool slot (padding slot 0 is never written).
     if (wg0) {
         float *hs = p.state + slot * s0 + h * s1;
@@ -1042,9 +1087,54 @@ static size_t order_bytes(int32_t num_req) {
     return (static_cast<size_t>(num_req > 0 ? num_req : 1) * sizeof(int32_t) + 255) / 256 * 256;
 }
 
+// cuTensorMapEncodeTiled, resolved once through the runtime's driver entry
+// point (the library links the static runtime, not libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(ptr);
+    }();
+    return fn;
+}
+
+// A [T][H][D] tensor seen as (x = column, y = head, z = token), box of
+// `box_x` columns x 1 head x 64 tokens. Tokens past T read as zero.
+static bool encode_rows(CUtensorMap *map, const void *base, CUtensorMapDataType type, int elem_bytes, int D,
+                        int H, int64_t T, int box_x, CUtensorMapSwizzle swizzle) {
+    const EncodeTiledFn fn = encode_tiled();
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(H),
+                                static_cast<cuuint64_t>(T > 0 ? T : 1)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * elem_bytes,
+                                   static_cast<cuuint64_t>(D) * elem_bytes * H};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_x), 1u, static_cast<cuuint32_t>(chunk::BT)};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    return fn(map, type, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int D, int MODE>
 static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
     using L = chunk::Smem<D>;
+    chunk::TmaMaps maps;
+    const int H = a->num_heads;
+    const int64_t T = a->num_tokens;
+    const bool raw = MODE == KDA_GATE_RAW;
+    if (!encode_rows(&maps.q, a->q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_rows(&maps.k, a->k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_rows(&maps.g, raw ? a->a : a->g,
+                     raw ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, raw ? 2 : 4, D, H, T,
+                     D, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_rows(&maps.v, a->v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+        return KDA_ERR_LAUNCH;
     static bool opted[64];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1057,7 +1147,7 @@ static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
     }
     if (order != nullptr) chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
     const int64_t grid = static_cast<int64_t>(a->num_req) * a->head_count;
-    chunk::chunk_kernel<D, MODE><<<static_cast<unsigned>(grid), chunk::kThreads, L::kAlloc, st>>>(*a, order);
+    chunk::chunk_kernel<D, MODE><<<static_cast<unsigned>(grid), chunk::kThreads, L::kAlloc, st>>>(*a, order, maps);
     return KDA_OK;
 }
 
@@ -1091,7 +1181,8 @@ extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t wor
         return KDA_ERR_INVALID_ARGUMENT;
     if (args->gate_mode == KDA_GATE_LOG && (args->g == nullptr || args->beta == nullptr))
         return KDA_ERR_INVALID_ARGUMENT;
-    // cp.async moves 16-byte pieces of q/k/v/a/g rows.
+    // Tensor-map bases must be 16-byte aligned; the row strides (D elements)
+    // are multiples of 16 bytes for both head dims.
     const void *rows[] = {args->q, args->k, args->v, args->gate_mode == KDA_GATE_RAW ? args->a : args->g};
     for (const void *ptr : rows)
         if (!kda::chunk_aligned16(ptr)) return KDA_ERR_ALIGNMENT;
