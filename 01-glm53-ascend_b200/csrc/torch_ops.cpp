@@ -9,7 +9,9 @@
 //   *_v2                  sgl-glm53-ascend-ops/csrc/kda/recurrent_v2/kda_varlen_recurrent_v2.cpp:226-238
 //                         and chunk_v2/kda_varlen_chunk_v2.cpp (aliases of the real ops here)
 // plus two log-gate ops (`kda_varlen_recurrent_g`, `kda_varlen_chunk_g`) that
-// take the fp32 log-decay g and beta directly.
+// take the fp32 log-decay g and beta directly, and the speculative-decoding
+// commit `move_intermediate_cache_kda` (sgl_kernel_npu's function of that name,
+// which the reference's MTP test calls after a verify).
 //
 // Error messages keep the reference's wording where a caller matches on it
 // ("must be K-contiguous", "does not support", "expects ...",
@@ -386,6 +388,55 @@ void prepared_recurrent(const at::Tensor &qn, const at::Tensor &kn, const at::Te
     check_kda(kda_prepared_recurrent_launch(&a, current_stream(qn)), "prepared_recurrent");
 }
 
+// move_intermediate_cache_kda: the speculative-decoding commit, called as
+// sgl_kernel_npu's function of that name is at
+// sgl-glm53-ascend-ops/tests/integration/test_glm53_kda_mtp_state_view_ascendc.py:93-99:
+//   dst [layers, slots, H, D, D] (in place) <- src [layers, requests, steps, H, D, D]
+// entry i: dst[:, dst_indices[i]] = src[:, src_indices[i], step_indices[i]].
+// `h_block_size` is the original's heads-per-program tiling; it does not change
+// the result and is only range-checked.
+void move_intermediate_cache_kda(at::Tensor &dst, const at::Tensor &src, const at::Tensor &dst_indices,
+                                 const at::Tensor &src_indices, const at::Tensor &step_indices,
+                                 int64_t h_block_size) {
+    TORCH_CHECK(dst.is_cuda(), "dst must be a CUDA tensor");
+    TORCH_CHECK(src.device() == dst.device(), "src must be on the same device as dst");
+    TORCH_CHECK(dst.scalar_type() == at::kFloat && src.scalar_type() == at::kFloat, "dst and src must be fp32");
+    TORCH_CHECK(dst.dim() == 5, "dst must be [layers, slots, H, D, D], got ", dst.dim(), " dims");
+    TORCH_CHECK(src.dim() == 6, "src must be [layers, requests, steps, H, D, D], got ", src.dim(), " dims");
+    TORCH_CHECK(dst.size(3) == dst.size(4) && src.size(4) == dst.size(3) && src.size(5) == dst.size(4),
+                "dst and src must hold D x D blocks of the same D");
+    TORCH_CHECK(src.size(0) == dst.size(0) && src.size(3) == dst.size(2),
+                "dst and src must have the same layers and heads");
+    TORCH_CHECK(h_block_size >= 1, "h_block_size must be positive");
+    check_index("dst_indices", dst_indices, dst);
+    check_index("src_indices", src_indices, dst);
+    check_index("step_indices", step_indices, dst);
+    const int64_t n = dst_indices.numel();
+    TORCH_CHECK(src_indices.numel() == n && step_indices.numel() == n,
+                "dst_indices, src_indices and step_indices must have the same length");
+    c10::cuda::CUDAGuard guard(dst.device());
+    KdaCommitArgs a{};
+    a.dst = dst.data_ptr<float>();
+    a.src = src.data_ptr<float>();
+    for (int i = 0; i < 5; ++i) a.dst_stride[i] = dst.stride(i);
+    for (int i = 0; i < 6; ++i) a.src_stride[i] = src.stride(i);
+    a.dst_indices = dst_indices.data_ptr();
+    a.src_indices = src_indices.data_ptr();
+    a.step_indices = step_indices.data_ptr();
+    a.index_bytes[0] = index_bytes(dst_indices);
+    a.index_bytes[1] = index_bytes(src_indices);
+    a.index_bytes[2] = index_bytes(step_indices);
+    a.num_entries = static_cast<int32_t>(n);
+    a.num_layers = static_cast<int32_t>(dst.size(0));
+    a.num_heads = static_cast<int32_t>(dst.size(2));
+    a.head_dim = static_cast<int32_t>(dst.size(3));
+    a.num_slots = dst.size(1);
+    a.num_requests = static_cast<int32_t>(src.size(1));
+    a.num_steps = static_cast<int32_t>(src.size(2));
+    a.status = status_ptr(dst.device());
+    check_kda(kda_commit_intermediate_launch(&a, current_stream(dst)), "move_intermediate_cache_kda");
+}
+
 // Registers (or clears, with an undefined tensor) an int32 device word that
 // the kernels on that device report KDA_DEVICE_ERR_* codes into.
 void kda_set_status_buffer(int64_t device, const c10::optional<at::Tensor> &buf) {
@@ -426,6 +477,8 @@ TORCH_LIBRARY(sgl_glm53_ascend, m) {
     m.def("kda_varlen_chunk_g(*, Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, "
           "Tensor(a!) initial_state_source, Tensor initial_state_indices, Tensor cu_seqlens, float scale, "
           "bool prefill=False, Tensor? track_state_indices=None, Tensor? track_state_lens=None) -> Tensor");
+    m.def("move_intermediate_cache_kda(Tensor(a!) dst, Tensor src, Tensor dst_indices, Tensor src_indices, "
+          "Tensor step_indices, int h_block_size=1) -> ()");
     m.def("kda_set_status_buffer(int device, Tensor? buf) -> ()");
     m.def("kda_abi_version() -> int");
     m.impl("kda_set_status_buffer", &kda_set_status_buffer);
@@ -440,4 +493,5 @@ TORCH_LIBRARY_IMPL(sgl_glm53_ascend, CUDA, m) {
     m.impl("prepared_recurrent", &prepared_recurrent);
     m.impl("kda_varlen_recurrent_g", &kda_varlen_recurrent_g);
     m.impl("kda_varlen_chunk_g", &kda_varlen_chunk_g);
+    m.impl("move_intermediate_cache_kda", &move_intermediate_cache_kda);
 }

@@ -30,6 +30,7 @@ EXPORTED = (
     "kda_chunk_launch",
     "kda_prepared_recurrent_launch",
     "kda_chunk_launch_no_alloc",
+    "kda_commit_intermediate_launch",
 )
 
 
@@ -69,6 +70,27 @@ class KdaArgs(ctypes.Structure):
     ]
 
 
+class KdaCommitArgs(ctypes.Structure):
+    _fields_ = [
+        ("dst", ctypes.c_void_p),
+        ("src", ctypes.c_void_p),
+        ("dst_stride", ctypes.c_int64 * 5),
+        ("src_stride", ctypes.c_int64 * 6),
+        ("dst_indices", ctypes.c_void_p),
+        ("src_indices", ctypes.c_void_p),
+        ("step_indices", ctypes.c_void_p),
+        ("index_bytes", ctypes.c_int32 * 3),
+        ("num_entries", ctypes.c_int32),
+        ("num_layers", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("num_slots", ctypes.c_int64),
+        ("num_requests", ctypes.c_int32),
+        ("num_steps", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 
 
@@ -88,6 +110,8 @@ def lib() -> ctypes.CDLL:
         L.kda_chunk_workspace_bytes.argtypes = [ctypes.c_int32] * 4
         L.kda_chunk_launch_no_alloc.restype = ctypes.c_int
         L.kda_chunk_launch_no_alloc.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p]
+        L.kda_commit_intermediate_launch.restype = ctypes.c_int
+        L.kda_commit_intermediate_launch.argtypes = [ctypes.POINTER(KdaCommitArgs), ctypes.c_void_p]
         L.kda_chunk_launch.restype = ctypes.c_int
         L.kda_chunk_launch.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
                                        ctypes.c_void_p]
@@ -167,6 +191,29 @@ def chunk_launch(args: KdaArgs, workspace: Optional[torch.Tensor], workspace_byt
 def chunk_launch_no_alloc(args: KdaArgs, stream: Optional[torch.cuda.Stream] = None) -> int:
     """kda_chunk_launch without a caller workspace (scratch inside the library)."""
     return lib().kda_chunk_launch_no_alloc(ctypes.byref(args), stream_handle(stream))
+
+
+def commit_args_from_tensors(dst, src, dst_indices, src_indices, step_indices,
+                             status: Optional[torch.Tensor] = None) -> KdaCommitArgs:
+    """dst [layers, slots, H, D, D] fp32, src [layers, requests, steps, H, D, D] fp32."""
+    x = KdaCommitArgs()
+    x.dst, x.src = dst.data_ptr(), src.data_ptr()
+    for i in range(5):
+        x.dst_stride[i] = dst.stride(i)
+    for i in range(6):
+        x.src_stride[i] = src.stride(i)
+    x.dst_indices, x.src_indices, x.step_indices = (t.data_ptr() for t in (dst_indices, src_indices, step_indices))
+    for i, t in enumerate((dst_indices, src_indices, step_indices)):
+        x.index_bytes[i] = _ibytes(t)
+    x.num_entries = dst_indices.numel()
+    x.num_layers, x.num_slots, x.num_heads, x.head_dim = dst.shape[0], dst.shape[1], dst.shape[2], dst.shape[3]
+    x.num_requests, x.num_steps = src.shape[1], src.shape[2]
+    x.status = _ptr(status)
+    return x
+
+
+def commit_launch(args: KdaCommitArgs, stream: Optional[torch.cuda.Stream] = None) -> int:
+    return lib().kda_commit_intermediate_launch(ctypes.byref(args), stream_handle(stream))
 
 
 def status_string(code: int) -> str:

@@ -5,6 +5,7 @@ from .kda import (
     kda_varlen_recurrent,
     kda_varlen_recurrent_g,
     kda_varlen_recurrent_v2,
+    move_intermediate_cache_kda,
     prepared_recurrent,
 )
 
@@ -15,5 +16,6 @@ __all__ = [
     "kda_varlen_recurrent",
     "kda_varlen_recurrent_g",
     "kda_varlen_recurrent_v2",
+    "move_intermediate_cache_kda",
     "prepared_recurrent",
 ]

@@ -230,3 +230,21 @@ def kda_varlen_chunk_g(
         prefill=prefill, track_state_indices=track_state_indices,
         track_state_lens=track_state_lens,
     )
+
+
+def move_intermediate_cache_kda(
+    dst: torch.Tensor,
+    src: torch.Tensor,
+    dst_indices: torch.Tensor,
+    src_indices: torch.Tensor,
+    step_indices: torch.Tensor,
+    h_block_size: int = 1,
+) -> None:
+    """Speculative-decoding commit: ``dst[:, dst_indices[i]] =
+    src[:, src_indices[i], step_indices[i]]`` in place, with ``dst`` the pool
+    ``[layers, slots, H, D, D]`` and ``src`` the verify checkpoints
+    ``[layers, requests, steps, H, D, D]``; a negative step copies nothing.
+    Same positional call as sgl_kernel_npu's function of this name in the
+    reference's MTP test (test_glm53_kda_mtp_state_view_ascendc.py:93-99)."""
+    torch.ops.sgl_glm53_ascend.move_intermediate_cache_kda(
+        dst, src, dst_indices, src_indices, step_indices, h_block_size)

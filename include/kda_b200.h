@@ -22,6 +22,9 @@
  *       (kda_varlen_chunk.h:143-144; launched at kda_varlen_chunk.cpp:190-191)
  *   kda_prepared_recurrent_launch   <- the prepared_recurrent_kernel_* launches
  *       (sgl-glm53-ascend-ops/csrc/kda/prepared_recurrent.cpp:684-710)
+ *   kda_commit_intermediate_launch  <- sgl_kernel_npu move_intermediate_cache_kda,
+ *       the speculative commit called at
+ *       sgl-glm53-ascend-ops/tests/integration/test_glm53_kda_mtp_state_view_ascendc.py:93-99
  *
  * Layouts (all row-major, element strides):
  *   q, k, v, a, g, out : [T, H, D]   (the torch [1, T, H, D] contiguous tensor)
@@ -161,6 +164,40 @@ int kda_chunk_launch_no_alloc(const KdaArgs *args, void *stream);
  * KDA_GATE_PREPARED). Replaces the prepared_recurrent_kernel_* launches
  * (prepared_recurrent.cpp:578-604, 684-710). */
 int kda_prepared_recurrent_launch(const KdaArgs *args, void *stream);
+
+/* Speculative-decoding commit. A verify pass (kda_recurrent_launch with
+ * `intermediate`) leaves one checkpoint per draft step; once the number of
+ * accepted tokens is known, entry i copies, for every layer l and head h,
+ *     dst[l, dst_indices[i], h] <- src[l, src_indices[i], step_indices[i], h]
+ * (each a D x D fp32 block, element (r, c) at r*s[...-2] + c*s[...-1]).
+ * Replaces sgl_kernel_npu's move_intermediate_cache_kda, the commit the
+ * reference's MTP test runs after a verify
+ * (sgl-glm53-ascend-ops/tests/integration/test_glm53_kda_mtp_state_view_ascendc.py:87-99).
+ *   - An entry whose step index is negative (no token accepted) copies nothing.
+ *   - A slot, request or step index past its dimension copies nothing and
+ *     writes KDA_DEVICE_ERR_BAD_SLOT into *status (when status is non-NULL).
+ *   - Entries must name distinct destinations; the copy order among entries
+ *     is unspecified. */
+typedef struct KdaCommitArgs {
+    float *dst;                   /* pool: [layers][slots][H][D][D] by dst_stride */
+    const float *src;             /* checkpoints: [layers][requests][steps][H][D][D] */
+    int64_t dst_stride[5];        /* layer, slot, head, row, column (elements) */
+    int64_t src_stride[6];        /* layer, request, step, head, row, column */
+    const void *dst_indices;      /* [num_entries] pool slot */
+    const void *src_indices;      /* [num_entries] request row of src */
+    const void *step_indices;     /* [num_entries] accepted draft step, or < 0 */
+    int32_t index_bytes[3];       /* 4 or 8 each */
+    int32_t num_entries;
+    int32_t num_layers;
+    int32_t num_heads;
+    int32_t head_dim;             /* D, any value >= 1 */
+    int64_t num_slots;            /* dst slots */
+    int32_t num_requests;         /* src requests */
+    int32_t num_steps;            /* src steps */
+    int32_t *status;              /* optional device word for KDA_DEVICE_ERR_* */
+} KdaCommitArgs;
+
+int kda_commit_intermediate_launch(const KdaCommitArgs *args, void *stream);
 
 #ifdef __cplusplus
 }

@@ -23,6 +23,8 @@ fixes and extensions the B200 operator needs:
 * ``prepared_recurrent`` restates the recurrence on host-prepared fp32 inputs
   (sgl-glm53-ascend-ops/csrc/kda/prepared_recurrent.cpp:610-713 and the Triton
   twin bench/_prepared_recurrent/bench_prepared_recurrent.py:62-127).
+* ``move_intermediate_cache_kda`` restates the speculative-decoding commit the
+  reference's MTP test runs after a verify (a gather of accepted checkpoints).
 
 Parity is pinned against the reference's own code: ``tests/golden/make_golden.py``
 runs ``kda_chunk_torch``, ``kda_recur_torch`` (one sequence per call, where it
@@ -276,6 +278,31 @@ def prepared_recurrent(qn, kn, v, gdecay, beta, out, state, indices, starts,
                 o[i, h] = (qn[i, h] @ S).to(o.dtype)
             if slot > 0:
                 state[slot, h].copy_(S)
+
+
+# ---------------------------------------------------------------------------
+# Speculative-decoding commit (move_intermediate_cache_kda)
+# ---------------------------------------------------------------------------
+
+def move_intermediate_cache_kda(dst, src, dst_indices, src_indices, step_indices,
+                                h_block_size: int = 1) -> None:
+    """The commit after a verify pass, as the reference's MTP test calls it
+    (sgl-glm53-ascend-ops/tests/integration/test_glm53_kda_mtp_state_view_ascendc.py:93-99):
+    ``dst[:, dst_indices[i]] = src[:, src_indices[i], step_indices[i]]`` for
+    every entry i, with dst ``[layers, slots, H, D, D]`` and src
+    ``[layers, requests, steps, H, D, D]`` (any strides; elements are matched by
+    logical index). The function itself (sgl_kernel_npu) is not in the
+    reference tree; this restates the copy its call site implies. An entry with
+    a negative step copies nothing; an index past its dimension raises.
+    ``h_block_size`` is the original's heads-per-program tiling and does not
+    change the result."""
+    assert h_block_size >= 1
+    for slot, req, step in zip(_ints(dst_indices), _ints(src_indices), _ints(step_indices)):
+        if step < 0:
+            continue
+        if not (0 <= slot < dst.shape[1] and 0 <= req < src.shape[1] and step < src.shape[2]):
+            raise IndexError(f"commit entry ({slot}, {req}, {step}) out of range")
+        dst[:, slot].copy_(src[:, req, step])
 
 
 # ---------------------------------------------------------------------------

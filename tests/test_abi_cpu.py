@@ -42,11 +42,13 @@ def test_header_functions_are_exported(abi):
     assert lib.kda_abi_version() == 1
 
 
-def test_struct_layout_matches_header(abi, tmp_path):
-    fields = [f[0] for f in abi.KdaArgs._fields_]
+@pytest.mark.parametrize("struct", ["KdaArgs", "KdaCommitArgs"])
+def test_struct_layout_matches_header(abi, tmp_path, struct):
+    cls = getattr(abi, struct)
+    fields = [f[0] for f in cls._fields_]
     src = ["#include <stdio.h>", "#include <stddef.h>", '#include "kda_b200.h"', "int main(void){",
-           'printf("%zu\\n", sizeof(KdaArgs));']
-    src += [f'printf("%zu\\n", offsetof(KdaArgs, {f}));' for f in fields]
+           f'printf("%zu\\n", sizeof({struct}));']
+    src += [f'printf("%zu\\n", offsetof({struct}, {f}));' for f in fields]
     src += ["return 0;}"]
     c = tmp_path / "layout.c"
     c.write_text("\n".join(src))
@@ -54,9 +56,9 @@ def test_struct_layout_matches_header(abi, tmp_path):
     subprocess.run(["gcc", "-I", str(ROOT / "include"), str(c), "-o", str(exe)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True,
                                            text=True).stdout.split()]
-    assert vals[0] == ctypes.sizeof(abi.KdaArgs)
+    assert vals[0] == ctypes.sizeof(cls)
     for f, off in zip(fields, vals[1:]):
-        assert getattr(abi.KdaArgs, f).offset == off, f"offset of {f}"
+        assert getattr(cls, f).offset == off, f"offset of {f}"
 
 
 def test_invalid_arguments_rejected_without_launch(abi):
@@ -79,6 +81,21 @@ def test_invalid_arguments_rejected_without_launch(abi):
     a.head_count = 1
     assert lib.kda_recurrent_launch(ctypes.byref(a), None) == 1   # null pointers
     assert abi.status_string(0x102).startswith("device: state slot")
+
+
+def test_commit_arguments_rejected_without_launch(abi):
+    lib = abi.lib()
+    assert lib.kda_commit_intermediate_launch(None, None) == 1
+    c = abi.KdaCommitArgs()
+    c.index_bytes[:] = [4, 4, 4]
+    assert lib.kda_commit_intermediate_launch(ctypes.byref(c), None) == 0     # no entries: nothing to do
+    c.num_entries, c.num_layers, c.num_heads, c.head_dim = 2, 1, 4, 128
+    assert lib.kda_commit_intermediate_launch(ctypes.byref(c), None) == 1     # null pointers
+    c.index_bytes[2] = 2
+    assert lib.kda_commit_intermediate_launch(ctypes.byref(c), None) == 1     # bad index width
+    c.index_bytes[2] = 4
+    c.num_layers = -1
+    assert lib.kda_commit_intermediate_launch(ctypes.byref(c), None) == 1
 
 
 def test_workspace_size_is_queryable(abi):
@@ -116,3 +133,6 @@ def test_ops_registered_with_reference_schemas():
     for name in ("kda_varlen_recurrent_v2", "kda_varlen_chunk_v2", "kda_varlen_recurrent_g",
                  "kda_varlen_chunk_g"):
         assert hasattr(ns, name)
+    commit = str(ns.move_intermediate_cache_kda.default._schema)
+    assert commit == ("sgl_glm53_ascend::move_intermediate_cache_kda(Tensor(a!) dst, Tensor src, "
+                      "Tensor dst_indices, Tensor src_indices, Tensor step_indices, int h_block_size=1) -> ()")
