@@ -139,8 +139,6 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// Named barrier for warpgroup 0 (the 128 threads that own the tensor-memory lanes).
-__device__ __forceinline__ void wg0_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // D[tmem] (+)= A[smem desc] x B[smem desc]
 __device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -181,6 +179,47 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
                  : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+// N consecutive fp32 columns of this warp's 32 lanes (N = 16 or 32).
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
+    if constexpr (N == 32) tmem_ld32(taddr, r); else tmem_ld16(taddr, r);
+}
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) {
+    if constexpr (N == 32) tmem_st32(taddr, r);
+    else if constexpr (N == 16) tmem_st16(taddr, r);
+    else tmem_st8(taddr, r);
+}
+
+// Tiled TMA store of a 3-D box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_addr(src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+// Linear bulk copy shared -> global (16-byte aligned ends, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_s2g(void *gdst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_addr(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... and finished writing global memory.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // Tiled TMA load of a 3-D box (x = key/value column, y = head, z = token)
 // into shared memory, completing on `bar`. No multicast.
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
@@ -192,10 +231,11 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
 }
 
 // Tensor maps of one launch: q, k, the gate (g fp32, or a bf16 for the raw
-// gate) as [T][H][D] boxes of 64 tokens x D, and v as 64-token x 64-column
-// boxes written with the 128-byte swizzle the tensor core reads.
+// gate) as [T][H][D] boxes of 64 tokens x D, v as 64-token x 64-column
+// boxes written with the 128-byte swizzle the tensor core reads, and the bf16
+// output as 64-token x D boxes (stores of whole chunks).
 struct TmaMaps {
-    CUtensorMap q, k, g, v;
+    CUtensorMap q, k, g, v, o;
 };
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100
@@ -354,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint16_t *const TBl = reinterpret_cast<uint16_t *>(sm + L::kTBl);
     uint16_t *const AQh = reinterpret_cast<uint16_t *>(sm + L::kAQh);
     uint16_t *const AQl = reinterpret_cast<uint16_t *>(sm + L::kAQl);
+    __nv_bfloat16 *const Ostage = reinterpret_cast<__nv_bfloat16 *>(sm + L::kX);   // o tile, after W is consumed
     uint64_t *const bars = reinterpret_cast<uint64_t *>(sm + L::kBar);
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 24);
     float *const vec = reinterpret_cast<float *>(sm + L::kVec);
@@ -444,30 +485,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const bool wg0 = tid < 128;                  // owns tensor-memory lane `tid` = value row
-    const int vrow = tid;
-    const uint32_t tl = tmem + (static_cast<uint32_t>(warp * 32) << 16);   // this warp's lane quadrant
+    // Tensor-memory slices: warp w reaches lanes [32 (w % 4), +32) (value
+    // rows) and takes column slice w / 4 of every conversion.
+    const int q4 = warp & 3, cs = warp >> 2;
+    const int srow = 32 * q4 + lane;                 // value row of this thread
+    const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+    constexpr int SC = D / 4;                        // state columns per slice
 
     if (nchunks > 0 && tid == 0) issue_tiles(0, true);
 
-    // Initial state S^T row `vrow` -> tensor memory (zero for slot 0 and the
-    // padding rows of D = 64); a length-0 prefix checkpoint is the initial state.
-    if (wg0) {
+    // Initial state S^T -> tensor memory (zero for slot 0 and the padding rows
+    // of D = 64); a length-0 prefix checkpoint is the initial state.
+    {
         const float *hs = p.state + slot * s0 + h * s1;
         float *ts = p.state + tslot * s0 + h * s1;
-        const bool row_ok = vrow < D;
+        const bool row_ok = srow < D;
+        uint32_t r[SC];
 #pragma unroll
-        for (int c32 = 0; c32 < D / 32; ++c32) {
-            uint32_t r[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const int k = c32 * 32 + e;
-                const float x = (slot > 0 && row_ok) ? hs[vrow * sv + k * sk] : 0.f;
-                r[e] = __float_as_uint(x);
-                if (row_ok && tslot > 0 && tlen == 0) ts[vrow * sv + k * sk] = x;
-            }
-            tmem_st32(tl + kColS + 32 * c32, r);
+        for (int e = 0; e < SC; ++e) {
+            const int k = SC * cs + e;
+            const float x = (slot > 0 && row_ok) ? hs[srow * sv + k * sk] : 0.f;
+            r[e] = __float_as_uint(x);
+            if (row_ok && tslot > 0 && tlen == 0) ts[srow * sv + k * sk] = x;
         }
+        tmem_st<SC>(tq + kColS + SC * cs, r);
         tmem_st_wait();
     }
 
@@ -481,6 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool has_next = c + 1 < nchunks;
         if (!mbar_wait(&bars[2], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
             report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+        if (tid == 0) bulk_wait_read();   // the previous o tile has left the W region
         if (n < BT) {
             // The boxes cover 64 tokens; rows past this sequence's end hold the
             // next sequence (or TMA's zero fill past T): clear them.
@@ -868,50 +910,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_async_smem();   // tiles written by threads -> read by the tensor core
         __syncthreads();
 
-        // ---- P9: the state scan on the 5th-gen tensor core (warpgroup 0) ----
-        if (wg0) {
+        // ---- P9: the state scan on the 5th-gen tensor core ----
+        // Every warp converts a slice of tensor memory: warp w reaches lanes
+        // [32 (w % 4), +32) (value rows) and takes column slice w / 4.
+        {
             const uint32_t ph = static_cast<uint32_t>(c & 1);
             // S^T -> bf16 hi/lo A operand (the unscaled chunk-start state, which
             // the first product batch reads), and S^T <- S^T e^{gl} in place, the
             // state the update accumulates into. On a tracked-prefix chunk the
             // rescale waits until S^T e^{gc_{r-1}} has been taken as well.
-#pragma unroll
-            for (int c64 = 0; c64 < D / 64; ++c64) {
-                uint32_t r0[32], r1[32];
-                tmem_ld32(tl + kColS + 64 * c64, r0);
-                tmem_ld32(tl + kColS + 64 * c64 + 32, r1);
+            {
+                uint32_t r[SC], hi[SC / 2], lo[SC / 2];
+                tmem_ld<SC>(tq + kColS + SC * cs, r);
                 tmem_ld_wait();
-                {
-                    uint32_t hi[16], lo[16];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        split2(__uint_as_float(r0[2 * e]), __uint_as_float(r0[2 * e + 1]), hi[e], lo[e]);
-                    tmem_st16(tl + kColSH + 32 * c64, hi);
-                    tmem_st16(tl + kColSL + 32 * c64, lo);
-#pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        split2(__uint_as_float(r1[2 * e]), __uint_as_float(r1[2 * e + 1]), hi[e], lo[e]);
-                    tmem_st16(tl + kColSH + 32 * c64 + 16, hi);
-                    tmem_st16(tl + kColSL + 32 * c64 + 16, lo);
-                }
+                for (int e = 0; e < SC / 2; ++e)
+                    split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+                tmem_st<SC / 2>(tq + kColSH + (SC / 2) * cs, hi);
+                tmem_st<SC / 2>(tq + kColSL + (SC / 2) * cs, lo);
                 if (!track_here) {
-                    const float *eg = vec + L::vEgl + 64 * c64;
+                    const float *eg = vec + L::vEgl + SC * cs;
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        r0[e] = __float_as_uint(__uint_as_float(r0[e]) * eg[e]);
-                        r1[e] = __float_as_uint(__uint_as_float(r1[e]) * eg[32 + e]);
-                    }
-                    tmem_st32(tl + kColS + 64 * c64, r0);
-                    tmem_st32(tl + kColS + 64 * c64 + 32, r1);
+                    for (int e = 0; e < SC; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * eg[e]);
+                    tmem_st<SC>(tq + kColS + SC * cs, r);
                 }
             }
             tmem_st_wait();
             tc_fence_before();
-            wg0_sync();
+            __syncthreads();
             if (tid == 0) {
                 tc_fence_after();
                 constexpr uint32_t id_v = idesc_bf16(128, 64, true, false, true);     // -(v^T TB^T)
                 constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
+                // NU = -(u - W S)^T = -v'^T, the operand the rest of the scan waits for.
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t a = sdesc(s_base + L::kV + kk * 2048, 8192, 1024);
@@ -927,55 +958,58 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_ts(tmem + kColNU, al, wh, id_n64, 1u);
                     umma_ts(tmem + kColNU, ah, wl, id_n64, 1u);
                     umma_ts(tmem + kColNU, ah, wh, id_n64, 1u);
-                    const uint64_t qh = sdesc(s_base + L::kY + off, 16, 1024);
-                    const uint64_t ql = sdesc(s_base + L::kY + BT * D * 2 + off, 16, 1024);
-                    umma_ts(tmem + kColO, al, qh, id_n64, kk > 0 ? 1u : 0u);
-                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
-                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
                 }
+                // O = (QG S)^T: only the output needs it, so it runs while v' is
+                // converted -- except on a tracked chunk, whose conversion
+                // reuses the S hi/lo columns and must find them consumed.
+                auto issue_qs = [&] {
+#pragma unroll
+                    for (int kk = 0; kk < KS; ++kk) {
+                        const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
+                        const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
+                        const uint64_t qh = sdesc(s_base + L::kY + off, 16, 1024);
+                        const uint64_t ql = sdesc(s_base + L::kY + BT * D * 2 + off, 16, 1024);
+                        umma_ts(tmem + kColO, al, qh, id_n64, kk > 0 ? 1u : 0u);
+                        umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
+                        umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
+                    }
+                };
+                if (track_here) issue_qs();
                 umma_commit(&bars[0]);
+                if (!track_here) issue_qs();
             }
-            if (!mbar_wait(&bars[0], ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (!mbar_wait(&bars[0], ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
             // The v tile is consumed: fetch the next one.
             if (has_next && !track_here && tid == 0) issue_v(c + 1);
-            // -v'^T (fp32) -> v'^T hi/lo A operand.
+            // -v'^T (fp32) -> v'^T hi/lo A operand, 16 columns per warp.
             {
-                uint32_t r0[32], r1[32], hi[16], lo[16];
-                tmem_ld32(tl + kColNU, r0);
-                tmem_ld32(tl + kColNU + 32, r1);
+                uint32_t r[16], hi[8], lo[8];
+                tmem_ld16(tq + kColNU + 16 * cs, r);
                 tmem_ld_wait();
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    split2(-__uint_as_float(r0[2 * e]), -__uint_as_float(r0[2 * e + 1]), hi[e], lo[e]);
-                tmem_st16(tl + kColVH, hi);
-                tmem_st16(tl + kColVL, lo);
-#pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    split2(-__uint_as_float(r1[2 * e]), -__uint_as_float(r1[2 * e + 1]), hi[e], lo[e]);
-                tmem_st16(tl + kColVH + 16, hi);
-                tmem_st16(tl + kColVL + 16, lo);
+                for (int e = 0; e < 8; ++e)
+                    split2(-__uint_as_float(r[2 * e]), -__uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+                tmem_st8(tq + kColVH + 8 * cs, hi);
+                tmem_st8(tq + kColVL + 8 * cs, lo);
             }
             // Tracked prefix: S^T e^{gc_{r-1}} into the freed hi/lo columns, then
             // the deferred S^T e^{gl}.
             if (track_here) {
+                uint32_t r[SC], t[SC];
+                tmem_ld<SC>(tq + kColS + SC * cs, r);
+                tmem_ld_wait();
 #pragma unroll
-                for (int c32 = 0; c32 < D / 32; ++c32) {
-                    uint32_t r[32], t[32];
-                    tmem_ld32(tl + kColS + 32 * c32, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        t[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEtr + 32 * c32 + e]);
-                        r[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEgl + 32 * c32 + e]);
-                    }
-                    tmem_st32(tl + kColTR + 32 * c32, t);
-                    tmem_st32(tl + kColS + 32 * c32, r);
+                for (int e = 0; e < SC; ++e) {
+                    t[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEtr + SC * cs + e]);
+                    r[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEgl + SC * cs + e]);
                 }
+                tmem_st<SC>(tq + kColTR + SC * cs, t);
+                tmem_st<SC>(tq + kColS + SC * cs, r);
             }
             tmem_st_wait();
             tc_fence_before();
-            wg0_sync();
+            __syncthreads();
             if (tid == 0) {
                 tc_fence_after();
                 constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
@@ -983,16 +1017,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
-                    const uint64_t qh = sdesc(s_base + L::kAQh + kk * 32, 16, 1024);
-                    const uint64_t ql = sdesc(s_base + L::kAQl + kk * 32, 16, 1024);
-                    umma_ts(tmem + kColO, al, qh, id_n64, 1u);
-                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
-                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
                     const uint64_t dh = sdesc(s_base + L::kZ + kk * 2048, 8192, 1024);
                     const uint64_t dl = sdesc(s_base + L::kZ + BT * D * 2 + kk * 2048, 8192, 1024);
                     umma_ts(tmem + kColS, al, dh, id_kd, 1u);
                     umma_ts(tmem + kColS, ah, dl, id_kd, 1u);
                     umma_ts(tmem + kColS, ah, dh, id_kd, 1u);
+                    const uint64_t qh = sdesc(s_base + L::kAQh + kk * 32, 16, 1024);
+                    const uint64_t ql = sdesc(s_base + L::kAQl + kk * 32, 16, 1024);
+                    umma_ts(tmem + kColO, al, qh, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
                     if (track_here) {
                         const uint64_t rh = sdesc(s_base + L::kRawQ + kk * 2048, 8192, 1024);
                         const uint64_t rl = sdesc(s_base + L::kRawK + kk * 2048, 8192, 1024);
@@ -1003,47 +1037,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 umma_commit(&bars[1]);
             }
-            if (!mbar_wait(&bars[1], ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (!mbar_wait(&bars[1], ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
-            // o rows of this chunk: lane = value row, column = chunk row i.
+            // o rows of this chunk: lane = value row, column = chunk row. Each
+            // warp converts 16 rows; the bf16 tile is staged row-major in the
+            // W region (consumed by the first batch) and leaves by TMA.
             {
-                uint32_t r0[32], r1[32];
-                tmem_ld32(tl + kColO, r0);
-                tmem_ld32(tl + kColO + 32, r1);
+                uint32_t r[16];
+                tmem_ld16(tq + kColO + 16 * cs, r);
                 tmem_ld_wait();
-                if (vrow < D) {
-                    const int64_t row_stride = static_cast<int64_t>(H) * D;
-                    const int64_t base = (t0 * H + h) * D + vrow;
-                    if (p.out_fp32) {
-                        float *o = static_cast<float *>(p.out) + base;
+                if (p.out_fp32) {
+                    if (srow < D) {
+                        float *o = static_cast<float *>(p.out) + (t0 * H + h) * D + srow;
+                        const int64_t row_stride = static_cast<int64_t>(H) * D;
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (e < n) o[e * row_stride] = __uint_as_float(r0[e]);
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (32 + e < n) o[(32 + e) * row_stride] = __uint_as_float(r1[e]);
-                    } else {
-                        __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + base;
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (e < n) o[e * row_stride] = __float2bfloat16_rn(__uint_as_float(r0[e]));
-#pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (32 + e < n) o[(32 + e) * row_stride] = __float2bfloat16_rn(__uint_as_float(r1[e]));
+                        for (int e = 0; e < 16; ++e)
+                            if (16 * cs + e < n) o[(16 * cs + e) * row_stride] = __uint_as_float(r[e]);
                     }
+                } else {
+                    if (srow < D) {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            Ostage[(16 * cs + e) * D + srow] = __float2bfloat16_rn(__uint_as_float(r[e]));
+                    }
+                    fence_async_smem();
                 }
+            }
+            __syncthreads();
+            if (!p.out_fp32 && tid == 0) {
+                if (n == BT) {
+                    tma_store_3d(&maps.o, Ostage, 0, h, static_cast<int>(t0));
+                } else {
+                    __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (t0 * H + h) * D;
+                    for (int rw = 0; rw < n; ++rw)
+                        bulk_s2g(o + static_cast<int64_t>(rw) * H * D, Ostage + rw * D, D * 2);
+                }
+                bulk_commit();
             }
             if (track_here) {
                 float *ts = p.state + tslot * s0 + h * s1;
+                uint32_t r[SC];
+                tmem_ld<SC>(tq + kColTR + SC * cs, r);
+                tmem_ld_wait();
+                if (srow < D) {
 #pragma unroll
-                for (int c32 = 0; c32 < D / 32; ++c32) {
-                    uint32_t r[32];
-                    tmem_ld32(tl + kColTR + 32 * c32, r);
-                    tmem_ld_wait();
-                    if (vrow < D) {
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) ts[vrow * sv + (32 * c32 + e) * sk] = __uint_as_float(r[e]);
-                    }
+                    for (int e = 0; e < SC; ++e) ts[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
                 }
             }
         }
@@ -1054,19 +1092,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     // Final state S^T -> pool slot (padding slot 0 is never written).
-    if (wg0) {
+    {
         float *hs = p.state + slot * s0 + h * s1;
+        uint32_t r[SC];
+        tmem_ld<SC>(tq + kColS + SC * cs, r);
+        tmem_ld_wait();
+        if (slot > 0 && srow < D) {
 #pragma unroll
-        for (int c32 = 0; c32 < D / 32; ++c32) {
-            uint32_t r[32];
-            tmem_ld32(tl + kColS + 32 * c32, r);
-            tmem_ld_wait();
-            if (slot > 0 && vrow < D) {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) hs[vrow * sv + (32 * c32 + e) * sk] = __uint_as_float(r[e]);
-            }
+            for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
         }
     }
+    if (tid == 0) bulk_wait_all();   // output stores complete before the CTA exits
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -1133,7 +1169,8 @@ static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
         !encode_rows(&maps.g, raw ? a->a : a->g,
                      raw ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, raw ? 2 : 4, D, H, T,
                      D, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_rows(&maps.v, a->v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, 64, CU_TENSOR_MAP_SWIZZLE_128B))
+        !encode_rows(&maps.v, a->v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_rows(&maps.o, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE))
         return KDA_ERR_LAUNCH;
     static bool opted[64];
     int dev = 0;
@@ -1183,7 +1220,7 @@ extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t wor
         return KDA_ERR_INVALID_ARGUMENT;
     // Tensor-map bases must be 16-byte aligned; the row strides (D elements)
     // are multiples of 16 bytes for both head dims.
-    const void *rows[] = {args->q, args->k, args->v, args->gate_mode == KDA_GATE_RAW ? args->a : args->g};
+    const void *rows[] = {args->q, args->k, args->v, args->gate_mode == KDA_GATE_RAW ? args->a : args->g, args->out};
     for (const void *ptr : rows)
         if (!kda::chunk_aligned16(ptr)) return KDA_ERR_ALIGNMENT;
     const size_t need = kda_chunk_workspace_bytes(args->num_req, args->num_tokens, args->num_heads, args->head_dim);
