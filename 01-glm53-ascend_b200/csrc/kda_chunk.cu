@@ -285,7 +285,9 @@ struct Smem {
     // the tracked-prefix operand K_r (hi at kRawQ, lo at kRawK) as well.
     static constexpr int kAp = 0;
     static constexpr int kT = kAp + BT * AS * 4;
-    static constexpr int kV = r1k(kRawEnd > kT + BT * AS * 4 ? kRawEnd : kT + BT * AS * 4);  // bf16 f64 tile [j][v]
+    static constexpr int kP = kT + BT * AS * 4;            // fp32 [3][16][16] inverse partial products
+    static constexpr int kPEnd = kP + 3 * 256 * 4;
+    static constexpr int kV = r1k(kRawEnd > kPEnd ? kRawEnd : kPEnd);   // bf16 f64 tile [j][v]
     static constexpr int kX = r1k(kV + BT * D * 2);        // fp32 [64][FS]  X, then W hi/lo (f64 tiles)
     static constexpr int kY = r1k(kX + BT * FS * 4);       // fp32 [64][FS]  Y, then QG hi/lo
     static constexpr int kZ = r1k(kY + BT * FS * 4);       // fp32 [64][FS]  Z, then KD hi/lo
@@ -378,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint16_t *const rawA = reinterpret_cast<uint16_t *>(sm + L::kRawG);
     float *const Ap = reinterpret_cast<float *>(sm + L::kAp);
     float *const Tm = reinterpret_cast<float *>(sm + L::kT);
+    float *const Pp = reinterpret_cast<float *>(sm + L::kP);
     uint16_t *const Vt = reinterpret_cast<uint16_t *>(sm + L::kV);
     float *const X = reinterpret_cast<float *>(sm + L::kX);
     float *const Y = reinterpret_cast<float *>(sm + L::kY);
@@ -724,74 +727,71 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncthreads();
 
         // ---- P4: T = (I + A')^-1, blocked forward substitution in fp32 ----
-        if (warp < 4 && lane < 16) {
-            const int I = warp, j = lane;
+        // Diagonal 16x16 blocks: lane (I, j) of warps 0-1 solves column j of
+        // block I (entries above the diagonal of the column stay 0, so the
+        // unpredicated sums are exact); two partial sums halve the FMA chain.
+        if (warp < 2) {
+            const int I = 2 * warp + (lane >> 4), j = lane & 15;
             float col[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-                float acc = (i == j) ? 1.f : 0.f;
                 const float *arow = Ap + (16 * I + i) * AS + 16 * I;
+                float s0a = 0.f, s1a = 0.f;
 #pragma unroll
-                for (int m = 0; m < i; ++m)
-                    if (m >= j) acc -= arow[m] * col[m];
-                col[i] = (i >= j) ? acc : 0.f;
+                for (int m = 0; m + 1 < i; m += 2) {
+                    s0a = fmaf(arow[m], col[m], s0a);
+                    s1a = fmaf(arow[m + 1], col[m + 1], s1a);
+                }
+                if (i & 1) s0a = fmaf(arow[i - 1], col[i - 1], s0a);
+                col[i] = (i == j) ? 1.f : (i > j ? -(s0a + s1a) : 0.f);
             }
 #pragma unroll
             for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
         }
         __syncthreads();
+        // Off-diagonal blocks by distance d = I - J, all pairs of one distance
+        // at once: P = sum_{M=J}^{I-1} A'_IM T_MJ, then T_IJ = -T_II P. A
+        // thread computes two adjacent columns of one row.
 #pragma unroll
         for (int d = 1; d <= 3; ++d) {
-            // Block pairs (I, J) = (d + q, q); element e = q * 256 + i * 16 + j.
-            const int nel = (4 - d) * 256;
-            float res[2] = {0.f, 0.f};
+            const int njob = (4 - d) * 128;               // (pair, row, column pair)
+            const int q = tid >> 7, i = (tid >> 3) & 15, j = (tid & 7) * 2;
+            const int I = d + q, J = q;
+            if (tid < njob) {
+                float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+                const float *arow = Ap + (16 * I + i) * AS;
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int e = tid + r * kThreads;
-                if (e < nel) {
-                    const int q = e >> 8, i = (e >> 4) & 15, j = e & 15;
-                    const int I = d + q, J = q;
-                    float acc = 0.f;
-                    for (int M = J; M < I; ++M) {
-                        const float *arow = Ap + (16 * I + i) * AS + 16 * M;
-                        const float *tcol = Tm + (16 * M) * AS + 16 * J + j;
+                for (int M = 0; M < d; ++M) {
+                    const int k0 = 16 * (J + M);
 #pragma unroll
-                        for (int m = 0; m < 16; ++m) acc = fmaf(arow[m], tcol[m * AS], acc);
+                    for (int m = 0; m < 16; m += 2) {
+                        const float x0 = arow[k0 + m], x1 = arow[k0 + m + 1];
+                        const float2 t0 = *reinterpret_cast<const float2 *>(Tm + (k0 + m) * AS + 16 * J + j);
+                        const float2 t1 = *reinterpret_cast<const float2 *>(Tm + (k0 + m + 1) * AS + 16 * J + j);
+                        a0.x = fmaf(x0, t0.x, a0.x);
+                        a0.y = fmaf(x0, t0.y, a0.y);
+                        a1.x = fmaf(x1, t1.x, a1.x);
+                        a1.y = fmaf(x1, t1.y, a1.y);
                     }
-                    res[r] = acc;
                 }
-            }
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int e = tid + r * kThreads;
-                if (e < nel) {
-                    const int q = e >> 8, i = (e >> 4) & 15, j = e & 15;
-                    Tm[(16 * (d + q) + i) * AS + 16 * q + j] = res[r];
-                }
+                *reinterpret_cast<float2 *>(Pp + q * 256 + i * 16 + j) = make_float2(a0.x + a1.x, a0.y + a1.y);
             }
             __syncthreads();
+            if (tid < njob) {
+                float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+                const float *trow = Tm + (16 * I + i) * AS + 16 * I;
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int e = tid + r * kThreads;
-                if (e < nel) {
-                    const int q = e >> 8, i = (e >> 4) & 15, j = e & 15;
-                    const int I = d + q, J = q;
-                    const float *trow = Tm + (16 * I + i) * AS + 16 * I;
-                    const float *pcol = Tm + (16 * I) * AS + 16 * J + j;
-                    float acc = 0.f;
-#pragma unroll
-                    for (int m = 0; m < 16; ++m) acc = fmaf(trow[m], pcol[m * AS], acc);
-                    res[r] = -acc;
+                for (int m = 0; m < 16; m += 2) {
+                    const float x0 = trow[m], x1 = trow[m + 1];
+                    const float2 p0 = *reinterpret_cast<const float2 *>(Pp + q * 256 + m * 16 + j);
+                    const float2 p1 = *reinterpret_cast<const float2 *>(Pp + q * 256 + (m + 1) * 16 + j);
+                    a0.x = fmaf(x0, p0.x, a0.x);
+                    a0.y = fmaf(x0, p0.y, a0.y);
+                    a1.x = fmaf(x1, p1.x, a1.x);
+                    a1.y = fmaf(x1, p1.y, a1.y);
                 }
-            }
-            __syncthreads();
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                const int e = tid + r * kThreads;
-                if (e < nel) {
-                    const int q = e >> 8, i = (e >> 4) & 15, j = e & 15;
-                    Tm[(16 * (d + q) + i) * AS + 16 * q + j] = res[r];
-                }
+                *reinterpret_cast<float2 *>(Tm + (16 * I + i) * AS + 16 * J + j) =
+                    make_float2(-(a0.x + a1.x), -(a0.y + a1.y));
             }
             __syncthreads();
         }
