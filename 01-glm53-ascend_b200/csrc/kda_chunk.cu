@@ -50,6 +50,8 @@ namespace chunk {
 
 constexpr int BT = 64;
 constexpr int kThreads = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 
 // ---------------------------------------------------------------------------
 // mma.sync / ldmatrix / cp.async primitives
@@ -82,6 +84,26 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(addr));
+}
+
+// 2^x on the special-function unit (relative error ~2^-22, flushes denormals).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// bf16x2 product; exact when one factor is a power of two and nothing leaves
+// the normal range (an underflow flushes a vanishing term to zero).
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
@@ -275,11 +297,11 @@ __device__ __forceinline__ int f64(int r, int c) { return ((c >> 6) << 12) + swz
 
 template <int D>
 struct Smem {
-    static constexpr int FS = D + 8;                       // fp32 tile row stride (conflict-free float2)
     static constexpr int AS = BT + 4;                      // fp32 64x64 tile row stride
     static constexpr int kRawQ = 0;                        // bf16 [64][D]   q of the chunk (plain rows)
     static constexpr int kRawK = kRawQ + BT * D * 2;       // bf16 [64][D]   k
-    static constexpr int kRawG = kRawK + BT * D * 2;       // fp32 [64][D]   g (bf16 a for the raw gate)
+    static constexpr int kRawG = kRawK + BT * D * 2;       // fp32 [64][D]   g (bf16 a for the raw gate),
+                                                           //                then x = gc - m (in place)
     static constexpr int kRawEnd = kRawG + BT * D * 4;
     // A' and T (fp32 [64][AS]) alias the raw region once X/Y/Z are built;
     // the tracked-prefix operand K_r (hi at kRawQ, lo at kRawK) as well.
@@ -288,23 +310,26 @@ struct Smem {
     static constexpr int kP = kT + BT * AS * 4;            // fp32 [3][16][16] inverse partial products
     static constexpr int kPEnd = kP + 3 * 256 * 4;
     static constexpr int kV = r1k(kRawEnd > kPEnd ? kRawEnd : kPEnd);   // bf16 f64 tile [j][v]
-    static constexpr int kX = r1k(kV + BT * D * 2);        // fp32 [64][FS]  X, then W hi/lo (f64 tiles)
-    static constexpr int kY = r1k(kX + BT * FS * 4);       // fp32 [64][FS]  Y, then QG hi/lo
-    static constexpr int kZ = r1k(kY + BT * FS * 4);       // fp32 [64][FS]  Z, then KD hi/lo
-    static constexpr int kTBh = r1k(kZ + BT * FS * 4);     // bf16 [64][64] swizzled
+    // bf16 hi/lo f64 tiles (hi at the base, lo BT*D*2 bytes later):
+    static constexpr int kX = r1k(kV + BT * D * 2);        // X, then W
+    static constexpr int kY = kX + BT * D * 4;             // Y, then QG (in place)
+    static constexpr int kZ = kY + BT * D * 4;             // Z, then KD (in place)
+    static constexpr int kTBh = kZ + BT * D * 4;           // bf16 [64][64] swizzled
     static constexpr int kTBl = kTBh + BT * BT * 2;
     static constexpr int kAQh = kTBl + BT * BT * 2;
     static constexpr int kAQl = kAQh + BT * BT * 2;
     static constexpr int kBar = kAQl + BT * BT * 2;        // 3 mbarriers + tensor-memory base slot
-    static constexpr int kVec = kBar + 32;                 // fp32 vectors below
-    // vector offsets in floats from kVec
+    static constexpr int kVec = kBar + 32;                 // vectors below
+    // vector offsets in 4-byte words from kVec; per (16-row block I, column k)
+    // tables are [4][D]
     static constexpr int vRq = 0, vRk = 64, vBeta = 128;
-    static constexpr int vM = 192;                         // [4][D] anchors m_I
-    static constexpr int vEm = vM + 4 * D;                 // [4][D] e^{m_I}
-    static constexpr int vF = vEm + 4 * D;                 // [6][D] e^{m_I - m_J}, J < I
-    static constexpr int vTot = vF;                        // [4][D] cumsum partial totals (before vF)
-    static constexpr int vEglm = vF + 6 * D;               // [4][D] e^{gl - m_J}
-    static constexpr int vEgl = vEglm + 4 * D;             // [D]    e^{gl}
+    static constexpr int vM = 192;                         // [4][D] anchors m_I (multiples of ln 2)
+    static constexpr int vTot = vM + 4 * D;                // [4][D] cumsum block totals
+    static constexpr int vS = vTot + 4 * D;                // bf16 [4][D] 2^{m_I / ln 2} = e^{m_I}
+    static constexpr int vFb = vS + 2 * D;                 // bf16 [6][D] e^{m_I - m_J}, J < I
+    static constexpr int vEglm = vFb + 3 * D;              // [4][D] e^{gl - m_J}
+    static constexpr int vEtrm = vEglm + 4 * D;            // [4][D] e^{gtr - m_J} (tracked chunk)
+    static constexpr int vEgl = vEtrm + 4 * D;             // [D]    e^{gl}
     static constexpr int vGl = vEgl + D;                   // [D]    gl = gc of the last row
     static constexpr int vGtr = vGl + D;                   // [D]    gc of the tracked row
     static constexpr int vEtr = vGtr + D;                  // [D]    e^{gtr}
@@ -347,6 +372,20 @@ __device__ __forceinline__ int lda_a_km(int lane, int m0, int k0) {
     return swz<C>(k0 + r + ((q >> 1) << 3), m0 + ((q & 1) << 3));
 }
 
+// The same lane addresses for the 64-row f64 tiles (64-column blocks; a
+// 16-column span never crosses a block).
+__device__ __forceinline__ int fa_a(int lane, int m0, int k0) {
+    return f64(m0 + (lane & 15), k0 + ((lane >> 4) << 3));
+}
+__device__ __forceinline__ int fb_nk(int lane, int n0, int k0) {
+    const int q = lane >> 3, r = lane & 7;
+    return f64(n0 + r + ((q >> 1) << 3), k0 + ((q & 1) << 3));
+}
+// B fragments (16 k x 8 n) from a [k][n] f64 tile at (k0, n0), with .trans (x2).
+__device__ __forceinline__ int fb_kn8(int lane, int k0, int n0) {
+    return f64(k0 + (lane & 7) + (((lane >> 3) & 1) << 3), n0);
+}
+
 // Ranks requests by length, longest first, so the longest chunk chains start
 // first (one block; order[rank] = request).
 __global__ void __launch_bounds__(1024) order_kernel(const KdaArgs p, int32_t *order) {
@@ -371,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int KS = D / 16;              // k-steps over the key dim
     constexpr int ELEM = 4 * D;             // threads of the column-per-thread passes
     constexpr int RPT = 16;                 // rows per thread in those passes (one 16-row block)
-    constexpr int FS = L::FS, AS = L::AS;
+    constexpr int AS = L::AS;
     extern __shared__ __align__(1024) unsigned char sm_raw[];
     unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
     uint16_t *const rawQ = reinterpret_cast<uint16_t *>(sm + L::kRawQ);
@@ -382,9 +421,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     float *const Tm = reinterpret_cast<float *>(sm + L::kT);
     float *const Pp = reinterpret_cast<float *>(sm + L::kP);
     uint16_t *const Vt = reinterpret_cast<uint16_t *>(sm + L::kV);
-    float *const X = reinterpret_cast<float *>(sm + L::kX);
-    float *const Y = reinterpret_cast<float *>(sm + L::kY);
-    float *const Z = reinterpret_cast<float *>(sm + L::kZ);
+    float *const xg = reinterpret_cast<float *>(sm + L::kRawG);   // x = gc - m, in place of the gate
+    uint16_t *const Xh = reinterpret_cast<uint16_t *>(sm + L::kX);
+    uint16_t *const Xl = Xh + BT * D;
+    uint16_t *const Yh = reinterpret_cast<uint16_t *>(sm + L::kY);
+    uint16_t *const Yl = Yh + BT * D;
+    uint16_t *const Zh = reinterpret_cast<uint16_t *>(sm + L::kZ);
+    uint16_t *const Zl = Zh + BT * D;
     uint16_t *const Wh = reinterpret_cast<uint16_t *>(sm + L::kX);
     uint16_t *const Wl = Wh + BT * D;
     uint16_t *const QGh = reinterpret_cast<uint16_t *>(sm + L::kY);
@@ -557,30 +600,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             vec[L::vBeta + tid] = bt;
         }
         {
-            const int grp = tid >> 4, l16 = tid & 15;
-            constexpr int EPL = D / 16;             // elements per lane of a row
+            // Four threads per row of q (rows 0..63) or k (64..127); part p
+            // reads the row's 16-byte groups 4i + p, with i mirrored on odd
+            // rows so the two rows of a quarter-warp hit distinct banks.
+            constexpr int GPT = D / 32;                       // groups per thread
+            const int rowid = tid >> 2, part = tid & 3, row = rowid & 63;
+            const uint4 *src = reinterpret_cast<const uint4 *>((rowid >= 64 ? rawK : rawQ) + row * D);
+            float sa = 0.f, sb = 0.f;
 #pragma unroll
-            for (int it = 0; it < 4; ++it) {
-                const int rowid = grp + 32 * it;   // 0..63 q rows, 64..127 k rows
-                const int row = rowid & 63;
-                const uint16_t *src = (rowid >= 64 ? rawK : rawQ) + row * D + l16 * EPL;
-                float ss = 0.f;
+            for (int i = 0; i < GPT; ++i) {
+                const uint4 u = src[4 * (i ^ (row & 1)) + part];
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                for (int e = 0; e < EPL; ++e) {
-                    const float x = __uint_as_float(static_cast<uint32_t>(src[e]) << 16);
-                    ss = fmaf(x, x, ss);
+                for (int e = 0; e < 4; ++e) {
+                    const float lo = bf16_lo(w[e]), hi = bf16_hi(w[e]);
+                    sa = fmaf(lo, lo, sa);
+                    sb = fmaf(hi, hi, sb);
                 }
-                ss += __shfl_xor_sync(0xffffffffu, ss, 8);
-                ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-                if (l16 == 0) {
-                    const float inv = 1.0f / sqrtf(ss + kNormEps);
-                    if (rowid >= 64)
-                        vec[L::vRk + row] = inv;
-                    else
-                        vec[L::vRq + row] = p.scale * inv;
-                }
+            }
+            float ss = sa + sb;
+            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+            if (part == 0) {
+                const float inv = 1.0f / sqrtf(ss + kNormEps);
+                if (rowid >= 64)
+                    vec[L::vRk + row] = inv;
+                else
+                    vec[L::vRq + row] = p.scale * inv;
             }
         }
         float gcr[RPT];
@@ -602,108 +648,120 @@ __global__ void __launch_bounds__(kThreads, 1)
                 gcr[i] = acc;
                 gtr = (row == trow) ? acc : gtr;
             }
-            if (pt < 3) vec[L::vTot + pt * D + kc] = acc;
+            vec[L::vTot + pt * D + kc] = acc;
         }
-        __syncthreads();
+        __syncthreads();   // block totals, norms, beta; every raw gate value has been read
         if (elem) {
             float off = 0.f;
-            for (int q = 0; q < pt; ++q) off += vec[L::vTot + q * D + kc];
+#pragma unroll
+            for (int q = 0; q < 3; ++q)
+                if (q < pt) off += vec[L::vTot + q * D + kc];
 #pragma unroll
             for (int i = 0; i < RPT; ++i) gcr[i] += off;
             gtr += off;
-        }
-        __syncthreads();   // vTot is read; vF (its alias) is written below
-
-        // ---- P2a: anchors, last/tracked gate rows, X/Y/Z ----
-        if (elem) {
-            const float m = gcr[8];
+            // Anchor of block pt: the midpoint row's gc rounded to a multiple of
+            // ln 2, so every ratio of anchors is an exact power of two. Then
+            // x = gc - m in place of the gate (|x| <= 8|g| + ln2/2).
+            const float nI = rintf(gcr[8] * kLog2e);
+            const float m = nI * kLn2;
             vec[L::vM + pt * D + kc] = m;
+            reinterpret_cast<uint16_t *>(vec + L::vS)[pt * D + kc] =
+                nI >= -126.f ? static_cast<uint16_t>((static_cast<int>(nI) + 127) << 7) : static_cast<uint16_t>(0);
+#pragma unroll
+            for (int i = 0; i < RPT; ++i) xg[(pt * RPT + i) * D + kc] = gcr[i] - m;
             if (pt == 3) vec[L::vGl + kc] = gcr[RPT - 1];
             if (trow >= 0 && trow / RPT == pt) vec[L::vGtr + kc] = gtr;
-#pragma unroll
-            for (int i = 0; i < RPT; ++i) {
-                const int row = pt * RPT + i;
-                const float x = gcr[i] - m;
-                const float E = expf(x), Ei = expf(-x);
-                const float kn =
-                    __uint_as_float(static_cast<uint32_t>(rawK[row * D + kc]) << 16) * vec[L::vRk + row];
-                const float qn =
-                    __uint_as_float(static_cast<uint32_t>(rawQ[row * D + kc]) << 16) * vec[L::vRq + row];
-                X[row * FS + kc] = kn * E;
-                Y[row * FS + kc] = qn * E;
-                Z[row * FS + kc] = kn * Ei;
-            }
         }
         __syncthreads();
 
-        // ---- P2b: per-(block, column) factors ----
+        // ---- P2: factor tables; X = kn e^x, Y = qn e^x, Z = kn e^-x as bf16 hi/lo tiles ----
         for (int e = tid; e < 16 * D; e += kThreads) {
             const int r = e / D, k = e % D;
-            if (r < 4) {
-                vec[L::vEm + r * D + k] = expf(vec[L::vM + r * D + k]);
+            if (r < 6) {
+                int I = (r < 1) ? 1 : (r < 3) ? 2 : 3;
+                const int J = r - I * (I - 1) / 2;
+                const float d = rintf((vec[L::vM + I * D + k] - vec[L::vM + J * D + k]) * kLog2e);   // <= 0
+                reinterpret_cast<uint16_t *>(vec + L::vFb)[r * D + k] =
+                    d >= -126.f ? static_cast<uint16_t>((static_cast<int>(d) + 127) << 7) : static_cast<uint16_t>(0);
             } else if (r < 10) {
-                const int s = r - 4;
-                const int I = (s < 1) ? 1 : (s < 3) ? 2 : 3;
-                const int J = s - I * (I - 1) / 2;
-                vec[L::vF + s * D + k] = expf(vec[L::vM + I * D + k] - vec[L::vM + J * D + k]);
-            } else if (r < 14) {
-                const int J = r - 10;
-                vec[L::vEglm + J * D + k] = expf(vec[L::vGl + k] - vec[L::vM + J * D + k]);
-            } else if (r == 14) {
-                vec[L::vEgl + k] = expf(vec[L::vGl + k]);
-            } else {
-                vec[L::vEtr + k] = track_here ? expf(vec[L::vGtr + k]) : 0.f;
+                const int J = r - 6;
+                vec[L::vEglm + J * D + k] = ex2((vec[L::vGl + k] - vec[L::vM + J * D + k]) * kLog2e);
+            } else if (r == 10) {
+                vec[L::vEgl + k] = ex2(vec[L::vGl + k] * kLog2e);
+            } else if (track_here) {
+                if (r == 11) {
+                    vec[L::vEtr + k] = ex2(vec[L::vGtr + k] * kLog2e);
+                } else {
+                    const int J = r - 12;
+                    vec[L::vEtrm + J * D + k] = ex2((vec[L::vGtr + k] - vec[L::vM + J * D + k]) * kLog2e);
+                }
             }
+        }
+        for (int j = tid; j < BT * D / 8; j += kThreads) {
+            const int row = j / (D / 8), c = 8 * (j % (D / 8));
+            const float4 x0 = *reinterpret_cast<const float4 *>(xg + row * D + c);
+            const float4 x1 = *reinterpret_cast<const float4 *>(xg + row * D + c + 4);
+            const uint4 qq = *reinterpret_cast<const uint4 *>(rawQ + row * D + c);
+            const uint4 kk = *reinterpret_cast<const uint4 *>(rawK + row * D + c);
+            const float rq = vec[L::vRq + row], rk = vec[L::vRk + row];
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            const uint32_t qw[4] = {qq.x, qq.y, qq.z, qq.w}, kw[4] = {kk.x, kk.y, kk.z, kk.w};
+            uint32_t xh[4], xl[4], yh[4], yl[4], zh[4], zl[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float t0 = xv[2 * e] * kLog2e, t1 = xv[2 * e + 1] * kLog2e;
+                const float E0 = ex2(t0), E1 = ex2(t1), F0 = ex2(-t0), F1 = ex2(-t1);
+                const float k0 = bf16_lo(kw[e]) * rk, k1 = bf16_hi(kw[e]) * rk;
+                const float q0 = bf16_lo(qw[e]) * rq, q1 = bf16_hi(qw[e]) * rq;
+                split2(k0 * E0, k1 * E1, xh[e], xl[e]);
+                split2(q0 * E0, q1 * E1, yh[e], yl[e]);
+                split2(k0 * F0, k1 * F1, zh[e], zl[e]);
+            }
+            const int o = f64(row, c);
+            *reinterpret_cast<uint4 *>(Xh + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+            *reinterpret_cast<uint4 *>(Xl + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+            *reinterpret_cast<uint4 *>(Yh + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+            *reinterpret_cast<uint4 *>(Yl + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
+            *reinterpret_cast<uint4 *>(Zh + o) = make_uint4(zh[0], zh[1], zh[2], zh[3]);
+            *reinterpret_cast<uint4 *>(Zl + o) = make_uint4(zl[0], zl[1], zl[2], zl[3]);
         }
         __syncthreads();
 
         // ---- P3: A' and Aqk, one 16x16 block pair per warp ----
+        // Block (I, J) = X_I diag(e^{m_I - m_J}) Z_J^T: the factor is a power
+        // of two, applied exactly to Z's bf16 hi/lo fragments.
         if (warp < 10) {
             int I, J;
             pair_ij(warp, I, J);
-            const float *F = (J < I) ? vec + L::vF + fslot(I, J) * D : nullptr;
+            const uint32_t *Fp =
+                (J < I) ? reinterpret_cast<const uint32_t *>(vec + L::vFb) + fslot(I, J) * (D / 2) : nullptr;
             float akk[2][4] = {}, aqk[2][4] = {};
-            const int ra = 16 * I + g, rb = ra + 8;
-#pragma unroll 2
-            for (int ks = 0; ks < KS; ++ks) {
-                const int c0 = ks * 16 + 2 * t4;
-                float2 f0 = make_float2(1.f, 1.f), f1 = make_float2(1.f, 1.f);
-                if (F != nullptr) {
-                    f0 = *reinterpret_cast<const float2 *>(F + c0);
-                    f1 = *reinterpret_cast<const float2 *>(F + c0 + 8);
-                }
-                uint32_t xh[4], xl[4], yh[4], yl[4];
-                {
-                    const float2 a0 = *reinterpret_cast<const float2 *>(X + ra * FS + c0);
-                    const float2 a1 = *reinterpret_cast<const float2 *>(X + rb * FS + c0);
-                    const float2 a2 = *reinterpret_cast<const float2 *>(X + ra * FS + c0 + 8);
-                    const float2 a3 = *reinterpret_cast<const float2 *>(X + rb * FS + c0 + 8);
-                    split2(a0.x * f0.x, a0.y * f0.y, xh[0], xl[0]);
-                    split2(a1.x * f0.x, a1.y * f0.y, xh[1], xl[1]);
-                    split2(a2.x * f1.x, a2.y * f1.y, xh[2], xl[2]);
-                    split2(a3.x * f1.x, a3.y * f1.y, xh[3], xl[3]);
-                }
-                {
-                    const float2 a0 = *reinterpret_cast<const float2 *>(Y + ra * FS + c0);
-                    const float2 a1 = *reinterpret_cast<const float2 *>(Y + rb * FS + c0);
-                    const float2 a2 = *reinterpret_cast<const float2 *>(Y + ra * FS + c0 + 8);
-                    const float2 a3 = *reinterpret_cast<const float2 *>(Y + rb * FS + c0 + 8);
-                    split2(a0.x * f0.x, a0.y * f0.y, yh[0], yl[0]);
-                    split2(a1.x * f0.x, a1.y * f0.y, yh[1], yl[1]);
-                    split2(a2.x * f1.x, a2.y * f1.y, yh[2], yl[2]);
-                    split2(a3.x * f1.x, a3.y * f1.y, yh[3], yl[3]);
-                }
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const int j = 16 * J + 8 * nt + g;
-                    const float2 z0 = *reinterpret_cast<const float2 *>(Z + j * FS + c0);
-                    const float2 z1 = *reinterpret_cast<const float2 *>(Z + j * FS + c0 + 8);
-                    uint32_t bh0, bl0, bh1, bl1;
-                    split2(z0.x, z0.y, bh0, bl0);
-                    split2(z1.x, z1.y, bh1, bl1);
-                    mma3(akk[nt], xh, xl, bh0, bh1, bl0, bl1);
-                    mma3(aqk[nt], yh, yl, bh0, bh1, bl0, bl1);
+            for (int ks = 0; ks < KS; ++ks) {
+                const int k0 = 16 * ks;
+                uint32_t xh[4], xl[4], yh[4], yl[4], zh[4], zl[4];
+                const uint32_t oa = 2 * fa_a(lane, 16 * I, k0), ob = 2 * fb_nk(lane, 16 * J, k0);
+                ldsm_x4(xh, s_base + L::kX + oa);
+                ldsm_x4(xl, s_base + L::kX + BT * D * 2 + oa);
+                ldsm_x4(yh, s_base + L::kY + oa);
+                ldsm_x4(yl, s_base + L::kY + BT * D * 2 + oa);
+                ldsm_x4(zh, s_base + L::kZ + ob);
+                ldsm_x4(zl, s_base + L::kZ + BT * D * 2 + ob);
+                if (Fp != nullptr) {
+                    const uint32_t f0 = Fp[(k0 >> 1) + t4], f1 = Fp[(k0 >> 1) + 4 + t4];
+                    zh[0] = bmul2(zh[0], f0);
+                    zh[1] = bmul2(zh[1], f1);
+                    zh[2] = bmul2(zh[2], f0);
+                    zh[3] = bmul2(zh[3], f1);
+                    zl[0] = bmul2(zl[0], f0);
+                    zl[1] = bmul2(zl[1], f1);
+                    zl[2] = bmul2(zl[2], f0);
+                    zl[3] = bmul2(zl[3], f1);
                 }
+                mma3(akk[0], xh, xl, zh[0], zh[1], zl[0], zl[1]);
+                mma3(akk[1], xh, xl, zh[2], zh[3], zl[2], zl[3]);
+                mma3(aqk[0], yh, yl, zh[0], zh[1], zl[0], zl[1]);
+                mma3(aqk[1], yh, yl, zh[2], zh[3], zl[2], zl[3]);
             }
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
@@ -822,16 +880,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 
         // ---- P7: W = TB (kn e^{gc}); warp w owns key columns [8w, 8w+8) ----
+        // kn e^{gc} = X e^{m_I}: X's bf16 hi/lo fragments scaled exactly by 2^{m_I / ln 2}.
         float wacc[4][4] = {};
         if (warp < D / 8) {
             uint32_t kbh[4][2], kbl[4][2];
             const int kcol = 8 * warp + g;
+            const uint16_t *sv16 = reinterpret_cast<const uint16_t *>(vec + L::vS);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-                const int jr = 16 * ks + 2 * t4;
-                const float e = vec[L::vEm + ks * D + kcol];
-                split2(X[jr * FS + kcol] * e, X[(jr + 1) * FS + kcol] * e, kbh[ks][0], kbl[ks][0]);
-                split2(X[(jr + 8) * FS + kcol] * e, X[(jr + 9) * FS + kcol] * e, kbh[ks][1], kbl[ks][1]);
+                const uint32_t ob = 2 * fb_kn8(lane, 16 * ks, 8 * warp);
+                ldsm_x2_t(kbh[ks], s_base + L::kX + ob);
+                ldsm_x2_t(kbl[ks], s_base + L::kX + BT * D * 2 + ob);
+                const uint32_t sc = static_cast<uint32_t>(sv16[ks * D + kcol]) * 0x10001u;
+                kbh[ks][0] = bmul2(kbh[ks][0], sc);
+                kbh[ks][1] = bmul2(kbh[ks][1], sc);
+                kbl[ks][0] = bmul2(kbl[ks][0], sc);
+                kbl[ks][1] = bmul2(kbl[ks][1], sc);
             }
 #pragma unroll
             for (int mt = 0; mt < 4; ++mt) {
@@ -841,6 +905,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ldsm_x4(ah, s_base + L::kTBh + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
                     ldsm_x4(al, s_base + L::kTBl + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
                     mma3(wacc[mt], ah, al, kbh[ks][0], kbh[ks][1], kbl[ks][0], kbl[ks][1]);
+                }
+            }
+        }
+
+        // ---- P8: QG = Y e^{m_I} (exact), KD = Z e^{gl - m_J}, tracked K_r; in place ----
+        {
+            const uint16_t *sv16 = reinterpret_cast<const uint16_t *>(vec + L::vS);
+            for (int j = tid; j < BT * D / 8; j += kThreads) {
+                const int row = j / (D / 8), c = 8 * (j % (D / 8)), blk = row >> 4;
+                const int o = f64(row, c);
+                const uint4 sc = *reinterpret_cast<const uint4 *>(sv16 + blk * D + c);
+                uint4 h = *reinterpret_cast<const uint4 *>(QGh + o), l = *reinterpret_cast<const uint4 *>(QGl + o);
+                *reinterpret_cast<uint4 *>(QGh + o) =
+                    make_uint4(bmul2(h.x, sc.x), bmul2(h.y, sc.y), bmul2(h.z, sc.z), bmul2(h.w, sc.w));
+                *reinterpret_cast<uint4 *>(QGl + o) =
+                    make_uint4(bmul2(l.x, sc.x), bmul2(l.y, sc.y), bmul2(l.z, sc.z), bmul2(l.w, sc.w));
+                h = *reinterpret_cast<const uint4 *>(KDh + o);
+                l = *reinterpret_cast<const uint4 *>(KDl + o);
+                const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
+                const float *eg = vec + L::vEglm + blk * D + c;
+                float z[8];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    z[2 * e] = bf16_lo(hw[e]) + bf16_lo(lw[e]);
+                    z[2 * e + 1] = bf16_hi(hw[e]) + bf16_hi(lw[e]);
+                }
+                uint32_t dh[4], dl[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) split2(z[2 * e] * eg[2 * e], z[2 * e + 1] * eg[2 * e + 1], dh[e], dl[e]);
+                *reinterpret_cast<uint4 *>(KDh + o) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
+                *reinterpret_cast<uint4 *>(KDl + o) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
+                if (track_here) {
+                    const float *et = vec + L::vEtrm + blk * D + c;
+                    const bool live = row < rtrack;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        split2(live ? z[2 * e] * et[2 * e] : 0.f, live ? z[2 * e + 1] * et[2 * e + 1] : 0.f, dh[e],
+                               dl[e]);
+                    *reinterpret_cast<uint4 *>(KRh + o) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
+                    *reinterpret_cast<uint4 *>(KRl + o) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
                 }
             }
         }
@@ -857,55 +961,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<uint32_t *>(Wh + f64(j, kcol)) = hi;
                     *reinterpret_cast<uint32_t *>(Wl + f64(j, kcol)) = lo;
                 }
-        }
-
-        // ---- P8: QG = Y e^{m_I}, KD = Z e^{gl - m_J}, tracked K_r, in place ----
-        {
-            uint32_t stage[RPT];
-            if (elem) {
-                const float gtr_k = track_here ? vec[L::vGtr + kc] : 0.f;
-                const float em = vec[L::vEm + pt * D + kc];
-                const float etrm = track_here ? expf(gtr_k - vec[L::vM + pt * D + kc]) : 0.f;
-#pragma unroll
-                for (int i = 0; i < RPT; ++i) {
-                    const int row = pt * RPT + i;
-                    uint16_t hi, lo;
-                    split1(Y[row * FS + kc] * em, hi, lo);
-                    stage[i] = static_cast<uint32_t>(hi) | (static_cast<uint32_t>(lo) << 16);
-                    if (track_here) {
-                        const float kr = (row < rtrack) ? Z[row * FS + kc] * etrm : 0.f;
-                        split1(kr, hi, lo);
-                        KRh[f64(row, kc)] = hi;
-                        KRl[f64(row, kc)] = lo;
-                    }
-                }
-            }
-            __syncthreads();
-            if (elem) {
-#pragma unroll
-                for (int i = 0; i < RPT; ++i) {
-                    const int row = pt * RPT + i;
-                    QGh[f64(row, kc)] = static_cast<uint16_t>(stage[i] & 0xffffu);
-                    QGl[f64(row, kc)] = static_cast<uint16_t>(stage[i] >> 16);
-                }
-                const float eg = vec[L::vEglm + pt * D + kc];
-#pragma unroll
-                for (int i = 0; i < RPT; ++i) {
-                    const int row = pt * RPT + i;
-                    uint16_t hi, lo;
-                    split1(Z[row * FS + kc] * eg, hi, lo);
-                    stage[i] = static_cast<uint32_t>(hi) | (static_cast<uint32_t>(lo) << 16);
-                }
-            }
-            __syncthreads();
-            if (elem) {
-#pragma unroll
-                for (int i = 0; i < RPT; ++i) {
-                    const int row = pt * RPT + i;
-                    KDh[f64(row, kc)] = static_cast<uint16_t>(stage[i] & 0xffffu);
-                    KDl[f64(row, kc)] = static_cast<uint16_t>(stage[i] >> 16);
-                }
-            }
         }
         fence_async_smem();   // tiles written by threads -> read by the tensor core
         __syncthreads();
