@@ -155,6 +155,10 @@ __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
 __device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols) : "memory");
 }
+// Named barrier `id` over `count` threads (whole warps).
+__device__ __forceinline__ void nbar(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 // Generic-proxy shared-memory writes -> visible to the tensor core (async proxy).
@@ -308,8 +312,11 @@ struct Smem {
     static constexpr int kAp = 0;
     static constexpr int kT = kAp + BT * AS * 4;
     static constexpr int kP = kT + BT * AS * 4;            // fp32 [3][16][16] inverse partial products
-    static constexpr int kPEnd = kP + 3 * 256 * 4;
-    static constexpr int kV = r1k(kRawEnd > kPEnd ? kRawEnd : kPEnd);   // bf16 f64 tile [j][v]
+    // bf16 [64][D] o tile of the previous chunk, staged for its TMA store
+    // while A', T and P occupy the front of the raw region.
+    static constexpr int kOst = r1k(kP + 3 * 256 * 4);
+    static constexpr int kOstEnd = kOst + BT * D * 2;
+    static constexpr int kV = r1k(kRawEnd > kOstEnd ? kRawEnd : kOstEnd);   // bf16 f64 tile [j][v]
     // bf16 hi/lo f64 tiles (hi at the base, lo BT*D*2 bytes later):
     static constexpr int kX = r1k(kV + BT * D * 2);        // X, then W
     static constexpr int kY = kX + BT * D * 4;             // Y, then QG (in place)
@@ -318,8 +325,8 @@ struct Smem {
     static constexpr int kTBl = kTBh + BT * BT * 2;
     static constexpr int kAQh = kTBl + BT * BT * 2;
     static constexpr int kAQl = kAQh + BT * BT * 2;
-    static constexpr int kBar = kAQl + BT * BT * 2;        // 3 mbarriers + tensor-memory base slot
-    static constexpr int kVec = kBar + 32;                 // vectors below
+    static constexpr int kBar = kAQl + BT * BT * 2;        // 8 mbarriers + tensor-memory base slot
+    static constexpr int kVec = kBar + 128;                // vectors below
     // vector offsets in 4-byte words from kVec; per (16-row block I, column k)
     // tables are [4][D]
     static constexpr int vRq = 0, vRk = 64, vBeta = 128;
@@ -404,7 +411,7 @@ __global__ void __launch_bounds__(1024) order_kernel(const KdaArgs p, int32_t *o
 }
 
 template <int D, int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads + 32, 1)
     chunk_kernel(const KdaArgs p, const int32_t *order, const __grid_constant__ TmaMaps maps) {
     using L = Smem<D>;
     constexpr int KS = D / 16;              // k-steps over the key dim
@@ -440,9 +447,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint16_t *const TBl = reinterpret_cast<uint16_t *>(sm + L::kTBl);
     uint16_t *const AQh = reinterpret_cast<uint16_t *>(sm + L::kAQh);
     uint16_t *const AQl = reinterpret_cast<uint16_t *>(sm + L::kAQl);
-    __nv_bfloat16 *const Ostage = reinterpret_cast<__nv_bfloat16 *>(sm + L::kX);   // o tile, after W is consumed
+    // o tile staging: in the W region at the end of a tracked chunk and after
+    // the last chunk, in the raw region during the next chunk's inverse
+    __nv_bfloat16 *const OstX = reinterpret_cast<__nv_bfloat16 *>(sm + L::kX);
+    __nv_bfloat16 *const OstR = reinterpret_cast<__nv_bfloat16 *>(sm + L::kOst);
     uint64_t *const bars = reinterpret_cast<uint64_t *>(sm + L::kBar);
-    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 24);
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 64);
     float *const vec = reinterpret_cast<float *>(sm + L::kVec);
     const uint32_t s_base = smem_addr(sm);
 
@@ -520,11 +530,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     // ---- tensor memory, mbarriers ----
+    // bars: 0 = W S done (v' ready), 1 = state update done, 2 = chunk tiles
+    // landed, 3 = o^T done, 4 = u product done (v tile free). sig: consumer ->
+    // producer, 0 = TB/QG/S-split ready, 1 = W/KD ready, 2 = v' hi/lo ready.
+    uint64_t *const sig = bars + 5;
     if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
     if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
-        mbar_init(&bars[2], 1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
     }
     tc_fence_before();
@@ -538,472 +551,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q4) << 16);
     constexpr int SC = D / 4;                        // state columns per slice
 
-    if (nchunks > 0 && tid == 0) issue_tiles(0, true);
-
-    // Initial state S^T -> tensor memory (zero for slot 0 and the padding rows
-    // of D = 64); a length-0 prefix checkpoint is the initial state.
-    {
-        const float *hs = p.state + slot * s0 + h * s1;
-        float *ts = p.state + tslot * s0 + h * s1;
-        const bool row_ok = srow < D;
-        uint32_t r[SC];
-#pragma unroll
-        for (int e = 0; e < SC; ++e) {
-            const int k = SC * cs + e;
-            const float x = (slot > 0 && row_ok) ? hs[srow * sv + k * sk] : 0.f;
-            r[e] = __float_as_uint(x);
-            if (row_ok && tslot > 0 && tlen == 0) ts[srow * sv + k * sk] = x;
-        }
-        tmem_st<SC>(tq + kColS + SC * cs, r);
-        tmem_st_wait();
-    }
-
-    if (nchunks > 0) load_beta(0);
-
-    for (int c = 0; c < nchunks; ++c) {
-        const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
-        const int n = chunk_rows(c);
-        const int64_t rtrack = tlen - static_cast<int64_t>(c) * BT;
-        const bool track_here = tslot > 0 && rtrack > 0 && rtrack <= BT;
-        const bool has_next = c + 1 < nchunks;
-        if (!mbar_wait(&bars[2], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
-            report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
-        if (tid == 0) bulk_wait_read();   // the previous o tile has left the W region
-        if (n < BT) {
-            // The boxes cover 64 tokens; rows past this sequence's end hold the
-            // next sequence (or TMA's zero fill past T): clear them.
-            for (int e = n * (D / 8) + tid; e < BT * (D / 8); e += kThreads) {   // 8-element groups
-                reinterpret_cast<uint4 *>(rawQ)[e] = make_uint4(0u, 0u, 0u, 0u);
-                reinterpret_cast<uint4 *>(rawK)[e] = make_uint4(0u, 0u, 0u, 0u);
-                reinterpret_cast<uint4 *>(Vt)[((e / (D / 8)) * 8 + (e % 8)) + ((e % (D / 8)) / 8) * 512] =
-                    make_uint4(0u, 0u, 0u, 0u);
-                if constexpr (MODE == KDA_GATE_RAW) {
-                    reinterpret_cast<uint4 *>(rawA)[e] = make_uint4(0u, 0u, 0u, 0u);
-                } else {
-                    reinterpret_cast<float4 *>(rawG)[2 * e] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    reinterpret_cast<float4 *>(rawG)[2 * e + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-            }
-            fence_async_smem();
-        }
-        __syncthreads();
-
-        // ---- P1: beta, row norms (scale folded into q), gate cumsum ----
-        if (tid < BT) {
-            float bt = 0.f;
-            if (tid < n) {
-                if constexpr (MODE == KDA_GATE_RAW)
-                    bt = sigmoidf_(bnext);
-                else
-                    bt = bnext;
-            }
-            vec[L::vBeta + tid] = bt;
-        }
-        {
-            // Four threads per row of q (rows 0..63) or k (64..127); part p
-            // reads the row's 16-byte groups 4i + p, with i mirrored on odd
-            // rows so the two rows of a quarter-warp hit distinct banks.
-            constexpr int GPT = D / 32;                       // groups per thread
-            const int rowid = tid >> 2, part = tid & 3, row = rowid & 63;
-            const uint4 *src = reinterpret_cast<const uint4 *>((rowid >= 64 ? rawK : rawQ) + row * D);
-            float sa = 0.f, sb = 0.f;
-#pragma unroll
-            for (int i = 0; i < GPT; ++i) {
-                const uint4 u = src[4 * (i ^ (row & 1)) + part];
-                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float lo = bf16_lo(w[e]), hi = bf16_hi(w[e]);
-                    sa = fmaf(lo, lo, sa);
-                    sb = fmaf(hi, hi, sb);
-                }
-            }
-            float ss = sa + sb;
-            ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-            ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-            if (part == 0) {
-                const float inv = 1.0f / sqrtf(ss + kNormEps);
-                if (rowid >= 64)
-                    vec[L::vRk + row] = inv;
-                else
-                    vec[L::vRq + row] = p.scale * inv;
-            }
-        }
-        float gcr[RPT];
-        const int trow = track_here ? static_cast<int>(rtrack) - 1 : -1;   // gc row of the checkpoint
-        float gtr = 0.f;
-        if (elem) {
-            float acc = 0.f;
-#pragma unroll
-            for (int i = 0; i < RPT; ++i) {
-                const int row = pt * RPT + i;
-                float gv;
-                if constexpr (MODE == KDA_GATE_RAW) {
-                    const float av = __uint_as_float(static_cast<uint32_t>(rawA[row * D + kc]) << 16);
-                    gv = row < n ? p.lower_bound * sigmoidf_(expA * (av + dtb)) : 0.f;
-                } else {
-                    gv = rawG[row * D + kc];
-                }
-                acc += gv;
-                gcr[i] = acc;
-                gtr = (row == trow) ? acc : gtr;
-            }
-            vec[L::vTot + pt * D + kc] = acc;
-        }
-        __syncthreads();   // block totals, norms, beta; every raw gate value has been read
-        if (elem) {
-            float off = 0.f;
-#pragma unroll
-            for (int q = 0; q < 3; ++q)
-                if (q < pt) off += vec[L::vTot + q * D + kc];
-#pragma unroll
-            for (int i = 0; i < RPT; ++i) gcr[i] += off;
-            gtr += off;
-            // Anchor of block pt: the midpoint row's gc rounded to a multiple of
-            // ln 2, so every ratio of anchors is an exact power of two. Then
-            // x = gc - m in place of the gate (|x| <= 8|g| + ln2/2).
-            const float nI = rintf(gcr[8] * kLog2e);
-            const float m = nI * kLn2;
-            vec[L::vM + pt * D + kc] = m;
-            reinterpret_cast<uint16_t *>(vec + L::vS)[pt * D + kc] =
-                nI >= -126.f ? static_cast<uint16_t>((static_cast<int>(nI) + 127) << 7) : static_cast<uint16_t>(0);
-#pragma unroll
-            for (int i = 0; i < RPT; ++i) xg[(pt * RPT + i) * D + kc] = gcr[i] - m;
-            if (pt == 3) vec[L::vGl + kc] = gcr[RPT - 1];
-            if (trow >= 0 && trow / RPT == pt) vec[L::vGtr + kc] = gtr;
-        }
-        __syncthreads();
-
-        // ---- P2: factor tables; X = kn e^x, Y = qn e^x, Z = kn e^-x as bf16 hi/lo tiles ----
-        for (int e = tid; e < 16 * D; e += kThreads) {
-            const int r = e / D, k = e % D;
-            if (r < 6) {
-                int I = (r < 1) ? 1 : (r < 3) ? 2 : 3;
-                const int J = r - I * (I - 1) / 2;
-                const float d = rintf((vec[L::vM + I * D + k] - vec[L::vM + J * D + k]) * kLog2e);   // <= 0
-                reinterpret_cast<uint16_t *>(vec + L::vFb)[r * D + k] =
-                    d >= -126.f ? static_cast<uint16_t>((static_cast<int>(d) + 127) << 7) : static_cast<uint16_t>(0);
-            } else if (r < 10) {
-                const int J = r - 6;
-                vec[L::vEglm + J * D + k] = ex2((vec[L::vGl + k] - vec[L::vM + J * D + k]) * kLog2e);
-            } else if (r == 10) {
-                vec[L::vEgl + k] = ex2(vec[L::vGl + k] * kLog2e);
-            } else if (track_here) {
-                if (r == 11) {
-                    vec[L::vEtr + k] = ex2(vec[L::vGtr + k] * kLog2e);
-                } else {
-                    const int J = r - 12;
-                    vec[L::vEtrm + J * D + k] = ex2((vec[L::vGtr + k] - vec[L::vM + J * D + k]) * kLog2e);
-                }
-            }
-        }
-        for (int j = tid; j < BT * D / 8; j += kThreads) {
-            const int row = j / (D / 8), c = 8 * (j % (D / 8));
-            const float4 x0 = *reinterpret_cast<const float4 *>(xg + row * D + c);
-            const float4 x1 = *reinterpret_cast<const float4 *>(xg + row * D + c + 4);
-            const uint4 qq = *reinterpret_cast<const uint4 *>(rawQ + row * D + c);
-            const uint4 kk = *reinterpret_cast<const uint4 *>(rawK + row * D + c);
-            const float rq = vec[L::vRq + row], rk = vec[L::vRk + row];
-            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            const uint32_t qw[4] = {qq.x, qq.y, qq.z, qq.w}, kw[4] = {kk.x, kk.y, kk.z, kk.w};
-            uint32_t xh[4], xl[4], yh[4], yl[4], zh[4], zl[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float t0 = xv[2 * e] * kLog2e, t1 = xv[2 * e + 1] * kLog2e;
-                const float E0 = ex2(t0), E1 = ex2(t1), F0 = ex2(-t0), F1 = ex2(-t1);
-                const float k0 = bf16_lo(kw[e]) * rk, k1 = bf16_hi(kw[e]) * rk;
-                const float q0 = bf16_lo(qw[e]) * rq, q1 = bf16_hi(qw[e]) * rq;
-                split2(k0 * E0, k1 * E1, xh[e], xl[e]);
-                split2(q0 * E0, q1 * E1, yh[e], yl[e]);
-                split2(k0 * F0, k1 * F1, zh[e], zl[e]);
-            }
-            const int o = f64(row, c);
-            *reinterpret_cast<uint4 *>(Xh + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
-            *reinterpret_cast<uint4 *>(Xl + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
-            *reinterpret_cast<uint4 *>(Yh + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
-            *reinterpret_cast<uint4 *>(Yl + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
-            *reinterpret_cast<uint4 *>(Zh + o) = make_uint4(zh[0], zh[1], zh[2], zh[3]);
-            *reinterpret_cast<uint4 *>(Zl + o) = make_uint4(zl[0], zl[1], zl[2], zl[3]);
-        }
-        __syncthreads();
-
-        // ---- P3: A' and Aqk, one 16x16 block pair per warp ----
-        // Block (I, J) = X_I diag(e^{m_I - m_J}) Z_J^T: the factor is a power
-        // of two, applied exactly to Z's bf16 hi/lo fragments.
-        if (warp < 10) {
-            int I, J;
-            pair_ij(warp, I, J);
-            const uint32_t *Fp =
-                (J < I) ? reinterpret_cast<const uint32_t *>(vec + L::vFb) + fslot(I, J) * (D / 2) : nullptr;
-            float akk[2][4] = {}, aqk[2][4] = {};
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                const int k0 = 16 * ks;
-                uint32_t xh[4], xl[4], yh[4], yl[4], zh[4], zl[4];
-                const uint32_t oa = 2 * fa_a(lane, 16 * I, k0), ob = 2 * fb_nk(lane, 16 * J, k0);
-                ldsm_x4(xh, s_base + L::kX + oa);
-                ldsm_x4(xl, s_base + L::kX + BT * D * 2 + oa);
-                ldsm_x4(yh, s_base + L::kY + oa);
-                ldsm_x4(yl, s_base + L::kY + BT * D * 2 + oa);
-                ldsm_x4(zh, s_base + L::kZ + ob);
-                ldsm_x4(zl, s_base + L::kZ + BT * D * 2 + ob);
-                if (Fp != nullptr) {
-                    const uint32_t f0 = Fp[(k0 >> 1) + t4], f1 = Fp[(k0 >> 1) + 4 + t4];
-                    zh[0] = bmul2(zh[0], f0);
-                    zh[1] = bmul2(zh[1], f1);
-                    zh[2] = bmul2(zh[2], f0);
-                    zh[3] = bmul2(zh[3], f1);
-                    zl[0] = bmul2(zl[0], f0);
-                    zl[1] = bmul2(zl[1], f1);
-                    zl[2] = bmul2(zl[2], f0);
-                    zl[3] = bmul2(zl[3], f1);
-                }
-                mma3(akk[0], xh, xl, zh[0], zh[1], zl[0], zl[1]);
-                mma3(akk[1], xh, xl, zh[2], zh[3], zl[2], zl[3]);
-                mma3(aqk[0], yh, yl, zh[0], zh[1], zl[0], zl[1]);
-                mma3(aqk[1], yh, yl, zh[2], zh[3], zl[2], zl[3]);
-            }
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int i = 16 * I + g + 8 * hf;
-                    const int j0 = 16 * J + 8 * nt + 2 * t4;
-                    const float bi = vec[L::vBeta + i];
-                    const float a0 = (j0 < i) ? akk[nt][2 * hf] * bi : 0.f;
-                    const float a1 = (j0 + 1 < i) ? akk[nt][2 * hf + 1] * bi : 0.f;
-                    *reinterpret_cast<float2 *>(Ap + i * AS + j0) = make_float2(a0, a1);
-                    const float q0 = (j0 <= i) ? aqk[nt][2 * hf] : 0.f;
-                    const float q1 = (j0 + 1 <= i) ? aqk[nt][2 * hf + 1] : 0.f;
-                    uint32_t qh, ql;
-                    split2(q0, q1, qh, ql);
-                    *reinterpret_cast<uint32_t *>(AQh + swz<BT>(i, j0)) = qh;
-                    *reinterpret_cast<uint32_t *>(AQl + swz<BT>(i, j0)) = ql;
-                }
-            }
-        }
-        __syncthreads();
-
-        // ---- P4: T = (I + A')^-1, blocked forward substitution in fp32 ----
-        // Diagonal 16x16 blocks: lane (I, j) of warps 0-1 solves column j of
-        // block I (entries above the diagonal of the column stay 0, so the
-        // unpredicated sums are exact); two partial sums halve the FMA chain.
-        if (warp < 2) {
-            const int I = 2 * warp + (lane >> 4), j = lane & 15;
-            float col[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const float *arow = Ap + (16 * I + i) * AS + 16 * I;
-                float s0a = 0.f, s1a = 0.f;
-#pragma unroll
-                for (int m = 0; m + 1 < i; m += 2) {
-                    s0a = fmaf(arow[m], col[m], s0a);
-                    s1a = fmaf(arow[m + 1], col[m + 1], s1a);
-                }
-                if (i & 1) s0a = fmaf(arow[i - 1], col[i - 1], s0a);
-                col[i] = (i == j) ? 1.f : (i > j ? -(s0a + s1a) : 0.f);
-            }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
-        }
-        __syncthreads();
-        // Off-diagonal blocks by distance d = I - J, all pairs of one distance
-        // at once: P = sum_{M=J}^{I-1} A'_IM T_MJ, then T_IJ = -T_II P. A
-        // thread computes two adjacent columns of one row.
-#pragma unroll
-        for (int d = 1; d <= 3; ++d) {
-            const int njob = (4 - d) * 128;               // (pair, row, column pair)
-            const int q = tid >> 7, i = (tid >> 3) & 15, j = (tid & 7) * 2;
-            const int I = d + q, J = q;
-            if (tid < njob) {
-                float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
-                const float *arow = Ap + (16 * I + i) * AS;
-#pragma unroll
-                for (int M = 0; M < d; ++M) {
-                    const int k0 = 16 * (J + M);
-#pragma unroll
-                    for (int m = 0; m < 16; m += 2) {
-                        const float x0 = arow[k0 + m], x1 = arow[k0 + m + 1];
-                        const float2 t0 = *reinterpret_cast<const float2 *>(Tm + (k0 + m) * AS + 16 * J + j);
-                        const float2 t1 = *reinterpret_cast<const float2 *>(Tm + (k0 + m + 1) * AS + 16 * J + j);
-                        a0.x = fmaf(x0, t0.x, a0.x);
-                        a0.y = fmaf(x0, t0.y, a0.y);
-                        a1.x = fmaf(x1, t1.x, a1.x);
-                        a1.y = fmaf(x1, t1.y, a1.y);
-                    }
-                }
-                *reinterpret_cast<float2 *>(Pp + q * 256 + i * 16 + j) = make_float2(a0.x + a1.x, a0.y + a1.y);
-            }
-            __syncthreads();
-            if (tid < njob) {
-                float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
-                const float *trow = Tm + (16 * I + i) * AS + 16 * I;
-#pragma unroll
-                for (int m = 0; m < 16; m += 2) {
-                    const float x0 = trow[m], x1 = trow[m + 1];
-                    const float2 p0 = *reinterpret_cast<const float2 *>(Pp + q * 256 + m * 16 + j);
-                    const float2 p1 = *reinterpret_cast<const float2 *>(Pp + q * 256 + (m + 1) * 16 + j);
-                    a0.x = fmaf(x0, p0.x, a0.x);
-                    a0.y = fmaf(x0, p0.y, a0.y);
-                    a1.x = fmaf(x1, p1.x, a1.x);
-                    a1.y = fmaf(x1, p1.y, a1.y);
-                }
-                *reinterpret_cast<float2 *>(Tm + (16 * I + i) * AS + 16 * J + j) =
-                    make_float2(-(a0.x + a1.x), -(a0.y + a1.y));
-            }
-            __syncthreads();
-        }
-
-        // ---- P5: TB = T diag(beta), lower triangle, split into hi/lo ----
-        for (int e = tid; e < BT * (BT / 2); e += kThreads) {
-            const int j = e / (BT / 2), jc = (e % (BT / 2)) * 2;
-            const float x0 = (jc <= j) ? Tm[j * AS + jc] * vec[L::vBeta + jc] : 0.f;
-            const float x1 = (jc + 1 <= j) ? Tm[j * AS + jc + 1] * vec[L::vBeta + jc + 1] : 0.f;
-            uint32_t hi, lo;
-            split2(x0, x1, hi, lo);
-            *reinterpret_cast<uint32_t *>(TBh + swz<BT>(j, jc)) = hi;
-            *reinterpret_cast<uint32_t *>(TBl + swz<BT>(j, jc)) = lo;
-            // Aqk's strictly-upper 16x16 blocks are never computed but are read
-            // by the full-width tensor-core product: make them zero.
-            if ((jc >> 4) > (j >> 4)) {
-                *reinterpret_cast<uint32_t *>(AQh + swz<BT>(j, jc)) = 0u;
-                *reinterpret_cast<uint32_t *>(AQl + swz<BT>(j, jc)) = 0u;
-            }
-        }
-        fence_async_smem();   // A'/T (generic writes) are overwritten next by bulk copies
-        __syncthreads();
-
-        // ---- P6: the raw region is free: fetch the next chunk's q/k/g ----
-        if (has_next && !track_here) {
-            if (tid == 0) issue_tiles(c + 1, false);
-            load_beta(c + 1);
-        }
-
-        // ---- P7: W = TB (kn e^{gc}); warp w owns key columns [8w, 8w+8) ----
-        // kn e^{gc} = X e^{m_I}: X's bf16 hi/lo fragments scaled exactly by 2^{m_I / ln 2}.
-        float wacc[4][4] = {};
-        if (warp < D / 8) {
-            uint32_t kbh[4][2], kbl[4][2];
-            const int kcol = 8 * warp + g;
-            const uint16_t *sv16 = reinterpret_cast<const uint16_t *>(vec + L::vS);
-#pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-                const uint32_t ob = 2 * fb_kn8(lane, 16 * ks, 8 * warp);
-                ldsm_x2_t(kbh[ks], s_base + L::kX + ob);
-                ldsm_x2_t(kbl[ks], s_base + L::kX + BT * D * 2 + ob);
-                const uint32_t sc = static_cast<uint32_t>(sv16[ks * D + kcol]) * 0x10001u;
-                kbh[ks][0] = bmul2(kbh[ks][0], sc);
-                kbh[ks][1] = bmul2(kbh[ks][1], sc);
-                kbl[ks][0] = bmul2(kbl[ks][0], sc);
-                kbl[ks][1] = bmul2(kbl[ks][1], sc);
-            }
-#pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-#pragma unroll
-                for (int ks = 0; ks <= mt; ++ks) {
-                    uint32_t ah[4], al[4];
-                    ldsm_x4(ah, s_base + L::kTBh + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
-                    ldsm_x4(al, s_base + L::kTBl + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
-                    mma3(wacc[mt], ah, al, kbh[ks][0], kbh[ks][1], kbl[ks][0], kbl[ks][1]);
-                }
-            }
-        }
-
-        // ---- P8: QG = Y e^{m_I} (exact), KD = Z e^{gl - m_J}, tracked K_r; in place ----
-        {
-            const uint16_t *sv16 = reinterpret_cast<const uint16_t *>(vec + L::vS);
-            for (int j = tid; j < BT * D / 8; j += kThreads) {
-                const int row = j / (D / 8), c = 8 * (j % (D / 8)), blk = row >> 4;
-                const int o = f64(row, c);
-                const uint4 sc = *reinterpret_cast<const uint4 *>(sv16 + blk * D + c);
-                uint4 h = *reinterpret_cast<const uint4 *>(QGh + o), l = *reinterpret_cast<const uint4 *>(QGl + o);
-                *reinterpret_cast<uint4 *>(QGh + o) =
-                    make_uint4(bmul2(h.x, sc.x), bmul2(h.y, sc.y), bmul2(h.z, sc.z), bmul2(h.w, sc.w));
-                *reinterpret_cast<uint4 *>(QGl + o) =
-                    make_uint4(bmul2(l.x, sc.x), bmul2(l.y, sc.y), bmul2(l.z, sc.z), bmul2(l.w, sc.w));
-                h = *reinterpret_cast<const uint4 *>(KDh + o);
-                l = *reinterpret_cast<const uint4 *>(KDl + o);
-                const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
-                const float *eg = vec + L::vEglm + blk * D + c;
-                float z[8];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    z[2 * e] = bf16_lo(hw[e]) + bf16_lo(lw[e]);
-                    z[2 * e + 1] = bf16_hi(hw[e]) + bf16_hi(lw[e]);
-                }
-                uint32_t dh[4], dl[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) split2(z[2 * e] * eg[2 * e], z[2 * e + 1] * eg[2 * e + 1], dh[e], dl[e]);
-                *reinterpret_cast<uint4 *>(KDh + o) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
-                *reinterpret_cast<uint4 *>(KDl + o) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
-                if (track_here) {
-                    const float *et = vec + L::vEtrm + blk * D + c;
-                    const bool live = row < rtrack;
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        split2(live ? z[2 * e] * et[2 * e] : 0.f, live ? z[2 * e + 1] * et[2 * e + 1] : 0.f, dh[e],
-                               dl[e]);
-                    *reinterpret_cast<uint4 *>(KRh + o) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
-                    *reinterpret_cast<uint4 *>(KRl + o) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
-                }
-            }
-        }
-        __syncthreads();   // X fully consumed: W replaces it
-        if (warp < D / 8) {
-#pragma unroll
-            for (int mt = 0; mt < 4; ++mt)
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int j = 16 * mt + g + 8 * hf;
-                    const int kcol = 8 * warp + 2 * t4;
-                    uint32_t hi, lo;
-                    split2(wacc[mt][2 * hf], wacc[mt][2 * hf + 1], hi, lo);
-                    *reinterpret_cast<uint32_t *>(Wh + f64(j, kcol)) = hi;
-                    *reinterpret_cast<uint32_t *>(Wl + f64(j, kcol)) = lo;
-                }
-        }
-        fence_async_smem();   // tiles written by threads -> read by the tensor core
-        __syncthreads();
-
-        // ---- P9: the state scan on the 5th-gen tensor core ----
-        // Every warp converts a slice of tensor memory: warp w reaches lanes
-        // [32 (w % 4), +32) (value rows) and takes column slice w / 4.
-        {
-            const uint32_t ph = static_cast<uint32_t>(c & 1);
-            // S^T -> bf16 hi/lo A operand (the unscaled chunk-start state, which
-            // the first product batch reads), and S^T <- S^T e^{gl} in place, the
-            // state the update accumulates into. On a tracked-prefix chunk the
-            // rescale waits until S^T e^{gc_{r-1}} has been taken as well.
-            {
-                uint32_t r[SC], hi[SC / 2], lo[SC / 2];
-                tmem_ld<SC>(tq + kColS + SC * cs, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < SC / 2; ++e)
-                    split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
-                tmem_st<SC / 2>(tq + kColSH + (SC / 2) * cs, hi);
-                tmem_st<SC / 2>(tq + kColSL + (SC / 2) * cs, lo);
-                if (!track_here) {
-                    const float *eg = vec + L::vEgl + SC * cs;
-#pragma unroll
-                    for (int e = 0; e < SC; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * eg[e]);
-                    tmem_st<SC>(tq + kColS + SC * cs, r);
-                }
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            __syncthreads();
-            if (tid == 0) {
+    if (warp == kThreads / 32) {
+        // ===== producer warp: one thread issues every tensor-core product and
+        // every TMA load, in the order the consumers' signals allow =====
+        if (lane == 0 && nchunks > 0) {
+            constexpr uint32_t id_v = idesc_bf16(128, 64, true, false, true);      // -(v^T TB^T)
+            constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
+            constexpr uint32_t id_kd = idesc_bf16(128, D, false, true, false);
+            auto pwait = [&](uint64_t *b, uint32_t ph) {
+                if (!mbar_wait(b, ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            };
+            issue_tiles(0, true);
+            for (int c = 0; c < nchunks; ++c) {
+                const uint32_t ph = static_cast<uint32_t>(c & 1);
+                const int64_t rt = tlen - static_cast<int64_t>(c) * BT;
+                const bool trk = tslot > 0 && rt > 0 && rt <= BT;
+                const bool nxt = c + 1 < nchunks;
+                pwait(&sig[0], ph);
                 tc_fence_after();
-                constexpr uint32_t id_v = idesc_bf16(128, 64, true, false, true);     // -(v^T TB^T)
-                constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
-                // NU = -(u - W S)^T = -v'^T, the operand the rest of the scan waits for.
+                if (nxt && !trk) issue_tiles(c + 1, false);   // the raw region is free
+                // NU = -u^T = -(TB v)^T (needs neither S nor v')
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t a = sdesc(s_base + L::kV + kk * 2048, 8192, 1024);
                     umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBh + kk * 32, 16, 1024), id_v, kk > 0 ? 1u : 0u);
                     umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBl + kk * 32, 16, 1024), id_v, 1u);
                 }
+                umma_commit(&bars[4]);
+                if (nxt && !trk) {
+                    pwait(&bars[4], ph);   // the v tile is consumed
+                    issue_v(c + 1);
+                }
+                pwait(&sig[1], ph);
+                tc_fence_after();
+                // NU += (W S)^T  ->  -v'^T
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
                     const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
@@ -1014,47 +595,592 @@ __global__ void __launch_bounds__(kThreads, 1)
                     umma_ts(tmem + kColNU, ah, wl, id_n64, 1u);
                     umma_ts(tmem + kColNU, ah, wh, id_n64, 1u);
                 }
-                // O = (QG S)^T: only the output needs it, so it runs while v' is
-                // converted -- except on a tracked chunk, whose conversion
-                // reuses the S hi/lo columns and must find them consumed.
-                auto issue_qs = [&] {
+                if (!trk) umma_commit(&bars[0]);
+                // o^T = (QG S)^T, while the consumers convert v' (on a tracked
+                // chunk before bars[0]: the conversion reuses the S hi/lo columns)
 #pragma unroll
-                    for (int kk = 0; kk < KS; ++kk) {
-                        const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
-                        const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
-                        const uint64_t qh = sdesc(s_base + L::kY + off, 16, 1024);
-                        const uint64_t ql = sdesc(s_base + L::kY + BT * D * 2 + off, 16, 1024);
-                        umma_ts(tmem + kColO, al, qh, id_n64, kk > 0 ? 1u : 0u);
-                        umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
-                        umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
+                for (int kk = 0; kk < KS; ++kk) {
+                    const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
+                    const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
+                    const uint64_t qh = sdesc(s_base + L::kY + off, 16, 1024);
+                    const uint64_t ql = sdesc(s_base + L::kY + BT * D * 2 + off, 16, 1024);
+                    umma_ts(tmem + kColO, al, qh, id_n64, kk > 0 ? 1u : 0u);
+                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
+                }
+                if (trk) umma_commit(&bars[0]);
+                pwait(&sig[2], ph);
+                tc_fence_after();
+                // S^T += v'^T KD (and the tracked prefix), then o^T += v'^T Aqk^T.
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
+                    const uint64_t dh = sdesc(s_base + L::kZ + kk * 2048, 8192, 1024);
+                    const uint64_t dl = sdesc(s_base + L::kZ + BT * D * 2 + kk * 2048, 8192, 1024);
+                    umma_ts(tmem + kColS, al, dh, id_kd, 1u);
+                    umma_ts(tmem + kColS, ah, dl, id_kd, 1u);
+                    umma_ts(tmem + kColS, ah, dh, id_kd, 1u);
+                    if (trk) {
+                        const uint64_t rh = sdesc(s_base + L::kRawQ + kk * 2048, 8192, 1024);
+                        const uint64_t rl = sdesc(s_base + L::kRawK + kk * 2048, 8192, 1024);
+                        umma_ts(tmem + kColTR, al, rh, id_kd, 1u);
+                        umma_ts(tmem + kColTR, ah, rl, id_kd, 1u);
+                        umma_ts(tmem + kColTR, ah, rh, id_kd, 1u);
                     }
-                };
-                if (track_here) issue_qs();
-                umma_commit(&bars[0]);
-                if (!track_here) issue_qs();
+                }
+                umma_commit(&bars[1]);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
+                    const uint64_t qh = sdesc(s_base + L::kAQh + kk * 32, 16, 1024);
+                    const uint64_t ql = sdesc(s_base + L::kAQl + kk * 32, 16, 1024);
+                    umma_ts(tmem + kColO, al, qh, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
+                }
+                umma_commit(&bars[3]);
+                if (nxt && trk) {
+                    pwait(&bars[1], ph);   // K_r (raw region) and the v tile are consumed
+                    issue_tiles(c + 1, true);
+                }
             }
-            if (!mbar_wait(&bars[0], ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+        }
+    } else {
+        // ===== consumer warps 0..15 =====
+        auto cbar = [] { nbar(1, kThreads); };
+        // o^T columns [c0, c0 + ncol) of this warp's lanes -> bf16 staging tile
+        // (row-major [64][D]), or straight to `out` for fp32 verification output.
+        auto o_cols = [&](__nv_bfloat16 *ost, int64_t ot0, int on, int c0, int ncol) {
+            for (int cc = c0; cc < c0 + ncol; cc += 16) {
+                uint32_t r[16];
+                tmem_ld16(tq + kColO + cc, r);
+                tmem_ld_wait();
+                if (srow < D) {
+                    if (p.out_fp32) {
+                        float *o = static_cast<float *>(p.out) + (ot0 * H + h) * D + srow;
+                        const int64_t row_stride = static_cast<int64_t>(H) * D;
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            if (cc + e < on) o[(cc + e) * row_stride] = __uint_as_float(r[e]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) ost[(cc + e) * D + srow] = __float2bfloat16_rn(__uint_as_float(r[e]));
+                    }
+                }
+            }
+        };
+        // A staged o tile -> `out`: one TMA tile store for a whole chunk, row
+        // copies for a partial one (rows past the sequence belong to the next).
+        auto o_store = [&](const __nv_bfloat16 *ost, int64_t ot0, int on) {
+            if (p.out_fp32) return;
+            if (on == BT) {
+                tma_store_3d(&maps.o, ost, 0, h, static_cast<int>(ot0));
+            } else {
+                __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (ot0 * H + h) * D;
+                for (int rw = 0; rw < on; ++rw)
+                    bulk_s2g(o + static_cast<int64_t>(rw) * H * D, ost + rw * D, D * 2);
+            }
+            bulk_commit();
+        };
+
+        // Initial state S^T -> tensor memory (zero for slot 0 and the padding rows
+        // of D = 64); a length-0 prefix checkpoint is the initial state.
+        {
+            const float *hs = p.state + slot * s0 + h * s1;
+            float *ts = p.state + tslot * s0 + h * s1;
+            const bool row_ok = srow < D;
+            uint32_t r[SC];
+#pragma unroll
+            for (int e = 0; e < SC; ++e) {
+                const int k = SC * cs + e;
+                const float x = (slot > 0 && row_ok) ? hs[srow * sv + k * sk] : 0.f;
+                r[e] = __float_as_uint(x);
+                if (row_ok && tslot > 0 && tlen == 0) ts[srow * sv + k * sk] = x;
+            }
+            tmem_st<SC>(tq + kColS + SC * cs, r);
+            tmem_st_wait();
+        }
+        if (nchunks > 0) load_beta(0);
+
+        bool o_pending = false;   // the previous chunk's o^T waits in tensor memory
+        int64_t o_t0 = 0;
+        int o_n = 0;
+        for (int c = 0; c < nchunks; ++c) {
+            const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
+            const int n = chunk_rows(c);
+            const int64_t rtrack = tlen - static_cast<int64_t>(c) * BT;
+            const bool track_here = tslot > 0 && rtrack > 0 && rtrack <= BT;
+            const bool has_next = c + 1 < nchunks;
+            if (!mbar_wait(&bars[2], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
+                report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (tid == 0) bulk_wait_read();   // a tracked chunk's o tile has left the W region
+            if (n < BT) {
+                // The boxes cover 64 tokens; rows past this sequence's end hold the
+                // next sequence (or TMA's zero fill past T): clear them.
+                for (int e = n * (D / 8) + tid; e < BT * (D / 8); e += kThreads) {   // 8-element groups
+                    reinterpret_cast<uint4 *>(rawQ)[e] = make_uint4(0u, 0u, 0u, 0u);
+                    reinterpret_cast<uint4 *>(rawK)[e] = make_uint4(0u, 0u, 0u, 0u);
+                    reinterpret_cast<uint4 *>(Vt)[((e / (D / 8)) * 8 + (e % 8)) + ((e % (D / 8)) / 8) * 512] =
+                        make_uint4(0u, 0u, 0u, 0u);
+                    if constexpr (MODE == KDA_GATE_RAW) {
+                        reinterpret_cast<uint4 *>(rawA)[e] = make_uint4(0u, 0u, 0u, 0u);
+                    } else {
+                        reinterpret_cast<float4 *>(rawG)[2 * e] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        reinterpret_cast<float4 *>(rawG)[2 * e + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+                fence_async_smem();
+            }
+            cbar();
+
+            // ---- P1: beta, row norms (scale folded into q), gate cumsum ----
+            if (tid < BT) {
+                float bt = 0.f;
+                if (tid < n) {
+                    if constexpr (MODE == KDA_GATE_RAW)
+                        bt = sigmoidf_(bnext);
+                    else
+                        bt = bnext;
+                }
+                vec[L::vBeta + tid] = bt;
+            }
+            {
+                // Four threads per row of q (rows 0..63) or k (64..127); part p
+                // reads the row's 16-byte groups 4i + p, with i mirrored on odd
+                // rows so the two rows of a quarter-warp hit distinct banks.
+                constexpr int GPT = D / 32;                       // groups per thread
+                const int rowid = tid >> 2, part = tid & 3, row = rowid & 63;
+                const uint4 *src = reinterpret_cast<const uint4 *>((rowid >= 64 ? rawK : rawQ) + row * D);
+                float sa = 0.f, sb = 0.f;
+    #pragma unroll
+                for (int i = 0; i < GPT; ++i) {
+                    const uint4 u = src[4 * (i ^ (row & 1)) + part];
+                    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    #pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float lo = bf16_lo(w[e]), hi = bf16_hi(w[e]);
+                        sa = fmaf(lo, lo, sa);
+                        sb = fmaf(hi, hi, sb);
+                    }
+                }
+                float ss = sa + sb;
+                ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+                ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+                if (part == 0) {
+                    const float inv = 1.0f / sqrtf(ss + kNormEps);
+                    if (rowid >= 64)
+                        vec[L::vRk + row] = inv;
+                    else
+                        vec[L::vRq + row] = p.scale * inv;
+                }
+            }
+            float gcr[RPT];
+            const int trow = track_here ? static_cast<int>(rtrack) - 1 : -1;   // gc row of the checkpoint
+            float gtr = 0.f;
+            if (elem) {
+                float acc = 0.f;
+    #pragma unroll
+                for (int i = 0; i < RPT; ++i) {
+                    const int row = pt * RPT + i;
+                    float gv;
+                    if constexpr (MODE == KDA_GATE_RAW) {
+                        const float av = __uint_as_float(static_cast<uint32_t>(rawA[row * D + kc]) << 16);
+                        gv = row < n ? p.lower_bound * sigmoidf_(expA * (av + dtb)) : 0.f;
+                    } else {
+                        gv = rawG[row * D + kc];
+                    }
+                    acc += gv;
+                    gcr[i] = acc;
+                    gtr = (row == trow) ? acc : gtr;
+                }
+                vec[L::vTot + pt * D + kc] = acc;
+            }
+            cbar();   // block totals, norms, beta; every raw gate value has been read
+            if (elem) {
+                float off = 0.f;
+    #pragma unroll
+                for (int q = 0; q < 3; ++q)
+                    if (q < pt) off += vec[L::vTot + q * D + kc];
+    #pragma unroll
+                for (int i = 0; i < RPT; ++i) gcr[i] += off;
+                gtr += off;
+                // Anchor of block pt: the midpoint row's gc rounded to a multiple of
+                // ln 2, so every ratio of anchors is an exact power of two. Then
+                // x = gc - m in place of the gate (|x| <= 8|g| + ln2/2).
+                const float nI = rintf(gcr[8] * kLog2e);
+                const float m = nI * kLn2;
+                vec[L::vM + pt * D + kc] = m;
+                reinterpret_cast<uint16_t *>(vec + L::vS)[pt * D + kc] =
+                    nI >= -126.f ? static_cast<uint16_t>((static_cast<int>(nI) + 127) << 7) : static_cast<uint16_t>(0);
+    #pragma unroll
+                for (int i = 0; i < RPT; ++i) xg[(pt * RPT + i) * D + kc] = gcr[i] - m;
+                if (pt == 3) vec[L::vGl + kc] = gcr[RPT - 1];
+                if (trow >= 0 && trow / RPT == pt) vec[L::vGtr + kc] = gtr;
+            }
+            cbar();
+
+            // ---- P2: factor tables; X = kn e^x, Y = qn e^x, Z = kn e^-x as bf16 hi/lo tiles ----
+            for (int e = tid; e < 16 * D; e += kThreads) {
+                const int r = e / D, k = e % D;
+                if (r < 6) {
+                    int I = (r < 1) ? 1 : (r < 3) ? 2 : 3;
+                    const int J = r - I * (I - 1) / 2;
+                    const float d = rintf((vec[L::vM + I * D + k] - vec[L::vM + J * D + k]) * kLog2e);   // <= 0
+                    reinterpret_cast<uint16_t *>(vec + L::vFb)[r * D + k] =
+                        d >= -126.f ? static_cast<uint16_t>((static_cast<int>(d) + 127) << 7) : static_cast<uint16_t>(0);
+                } else if (r < 10) {
+                    const int J = r - 6;
+                    vec[L::vEglm + J * D + k] = ex2((vec[L::vGl + k] - vec[L::vM + J * D + k]) * kLog2e);
+                } else if (r == 10) {
+                    vec[L::vEgl + k] = ex2(vec[L::vGl + k] * kLog2e);
+                } else if (track_here) {
+                    if (r == 11) {
+                        vec[L::vEtr + k] = ex2(vec[L::vGtr + k] * kLog2e);
+                    } else {
+                        const int J = r - 12;
+                        vec[L::vEtrm + J * D + k] = ex2((vec[L::vGtr + k] - vec[L::vM + J * D + k]) * kLog2e);
+                    }
+                }
+            }
+            for (int j = tid; j < BT * D / 8; j += kThreads) {
+                const int row = j / (D / 8), c = 8 * (j % (D / 8));
+                const float4 x0 = *reinterpret_cast<const float4 *>(xg + row * D + c);
+                const float4 x1 = *reinterpret_cast<const float4 *>(xg + row * D + c + 4);
+                const uint4 qq = *reinterpret_cast<const uint4 *>(rawQ + row * D + c);
+                const uint4 kk = *reinterpret_cast<const uint4 *>(rawK + row * D + c);
+                const float rq = vec[L::vRq + row], rk = vec[L::vRk + row];
+                const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                const uint32_t qw[4] = {qq.x, qq.y, qq.z, qq.w}, kw[4] = {kk.x, kk.y, kk.z, kk.w};
+                uint32_t xh[4], xl[4], yh[4], yl[4], zh[4], zl[4];
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float t0 = xv[2 * e] * kLog2e, t1 = xv[2 * e + 1] * kLog2e;
+                    const float E0 = ex2(t0), E1 = ex2(t1), F0 = ex2(-t0), F1 = ex2(-t1);
+                    const float k0 = bf16_lo(kw[e]) * rk, k1 = bf16_hi(kw[e]) * rk;
+                    const float q0 = bf16_lo(qw[e]) * rq, q1 = bf16_hi(qw[e]) * rq;
+                    split2(k0 * E0, k1 * E1, xh[e], xl[e]);
+                    split2(q0 * E0, q1 * E1, yh[e], yl[e]);
+                    split2(k0 * F0, k1 * F1, zh[e], zl[e]);
+                }
+                const int o = f64(row, c);
+                *reinterpret_cast<uint4 *>(Xh + o) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+                *reinterpret_cast<uint4 *>(Xl + o) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+                *reinterpret_cast<uint4 *>(Yh + o) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+                *reinterpret_cast<uint4 *>(Yl + o) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
+                *reinterpret_cast<uint4 *>(Zh + o) = make_uint4(zh[0], zh[1], zh[2], zh[3]);
+                *reinterpret_cast<uint4 *>(Zl + o) = make_uint4(zl[0], zl[1], zl[2], zl[3]);
+            }
+            cbar();
+
+            // ---- P3: A' and Aqk, one 16x16 block pair per warp ----
+            // Block (I, J) = X_I diag(e^{m_I - m_J}) Z_J^T: the factor is a power
+            // of two, applied exactly to Z's bf16 hi/lo fragments.
+            if (warp < 10) {
+                int I, J;
+                pair_ij(warp, I, J);
+                const uint32_t *Fp =
+                    (J < I) ? reinterpret_cast<const uint32_t *>(vec + L::vFb) + fslot(I, J) * (D / 2) : nullptr;
+                float akk[2][4] = {}, aqk[2][4] = {};
+    #pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+                    const int k0 = 16 * ks;
+                    uint32_t xh[4], xl[4], yh[4], yl[4], zh[4], zl[4];
+                    const uint32_t oa = 2 * fa_a(lane, 16 * I, k0), ob = 2 * fb_nk(lane, 16 * J, k0);
+                    ldsm_x4(xh, s_base + L::kX + oa);
+                    ldsm_x4(xl, s_base + L::kX + BT * D * 2 + oa);
+                    ldsm_x4(yh, s_base + L::kY + oa);
+                    ldsm_x4(yl, s_base + L::kY + BT * D * 2 + oa);
+                    ldsm_x4(zh, s_base + L::kZ + ob);
+                    ldsm_x4(zl, s_base + L::kZ + BT * D * 2 + ob);
+                    if (Fp != nullptr) {
+                        const uint32_t f0 = Fp[(k0 >> 1) + t4], f1 = Fp[(k0 >> 1) + 4 + t4];
+                        zh[0] = bmul2(zh[0], f0);
+                        zh[1] = bmul2(zh[1], f1);
+                        zh[2] = bmul2(zh[2], f0);
+                        zh[3] = bmul2(zh[3], f1);
+                        zl[0] = bmul2(zl[0], f0);
+                        zl[1] = bmul2(zl[1], f1);
+                        zl[2] = bmul2(zl[2], f0);
+                        zl[3] = bmul2(zl[3], f1);
+                    }
+                    mma3(akk[0], xh, xl, zh[0], zh[1], zl[0], zl[1]);
+                    mma3(akk[1], xh, xl, zh[2], zh[3], zl[2], zl[3]);
+                    mma3(aqk[0], yh, yl, zh[0], zh[1], zl[0], zl[1]);
+                    mma3(aqk[1], yh, yl, zh[2], zh[3], zl[2], zl[3]);
+                }
+    #pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+    #pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const int i = 16 * I + g + 8 * hf;
+                        const int j0 = 16 * J + 8 * nt + 2 * t4;
+                        const float bi = vec[L::vBeta + i];
+                        const float a0 = (j0 < i) ? akk[nt][2 * hf] * bi : 0.f;
+                        const float a1 = (j0 + 1 < i) ? akk[nt][2 * hf + 1] * bi : 0.f;
+                        *reinterpret_cast<float2 *>(Ap + i * AS + j0) = make_float2(a0, a1);
+                        const float q0 = (j0 <= i) ? aqk[nt][2 * hf] : 0.f;
+                        const float q1 = (j0 + 1 <= i) ? aqk[nt][2 * hf + 1] : 0.f;
+                        uint32_t qh, ql;
+                        split2(q0, q1, qh, ql);
+                        *reinterpret_cast<uint32_t *>(AQh + swz<BT>(i, j0)) = qh;
+                        *reinterpret_cast<uint32_t *>(AQl + swz<BT>(i, j0)) = ql;
+                    }
+                }
+            } else if (o_pending) {
+                // Warps 10..15, beside the block products: the previous chunk's
+                // o tile leaves through the raw region's staging area (quadrants 0
+                // and 1 have one warp each, 2 and 3 two).
+                if (!mbar_wait(&bars[3], static_cast<uint32_t>((c - 1) & 1), p.status) && lane == 0)
+                    report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                tc_fence_after();
+                const bool pair = q4 >= 2;
+                const int half = (warp >= 14) ? 1 : 0;
+                o_cols(OstR, o_t0, o_n, pair ? 32 * half : 0, pair ? 32 : BT);
+                fence_async_smem();
+                nbar(3, 192);
+                if (tid == 384) {
+                    o_store(OstR, o_t0, o_n);
+                    bulk_wait_read();   // before the next chunk's tiles land on the raw region
+                }
+            }
+            cbar();
+
+                // Warps 12..15 (one per lane quadrant), beside the inverse: this
+            // chunk's S^T is split into the bf16 hi/lo A operand and rescaled
+            // by e^{gl} (deferred on a tracked chunk).
+            auto p4_side = [&] {
+                if (c > 0) {
+                    if (!mbar_wait(&bars[1], static_cast<uint32_t>((c - 1) & 1), p.status) && lane == 0)
+                        report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                    tc_fence_after();
+                }
+#pragma unroll
+                for (int c32 = 0; c32 < D / 32; ++c32) {
+                    uint32_t r[32], hi[16], lo[16];
+                    tmem_ld32(tq + kColS + 32 * c32, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+                    tmem_st16(tq + kColSH + 16 * c32, hi);
+                    tmem_st16(tq + kColSL + 16 * c32, lo);
+                    if (!track_here) {
+                        const float *eg = vec + L::vEgl + 32 * c32;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * eg[e]);
+                        tmem_st32(tq + kColS + 32 * c32, r);
+                    }
+                }
+                tmem_st_wait();
+                tc_fence_before();
+            };
+            // ---- P4: T = (I + A')^-1, blocked forward substitution in fp32 (warps 0-11) ----
+            if (warp < 12) {
+            // Diagonal 16x16 blocks: lane (I, j) of warps 0-1 solves column j of
+            // block I (entries above the diagonal of the column stay 0, so the
+            // unpredicated sums are exact); two partial sums halve the FMA chain.
+            if (warp < 2) {
+                const int I = 2 * warp + (lane >> 4), j = lane & 15;
+                float col[16];
+    #pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float *arow = Ap + (16 * I + i) * AS + 16 * I;
+                    float s0a = 0.f, s1a = 0.f;
+    #pragma unroll
+                    for (int m = 0; m + 1 < i; m += 2) {
+                        s0a = fmaf(arow[m], col[m], s0a);
+                        s1a = fmaf(arow[m + 1], col[m + 1], s1a);
+                    }
+                    if (i & 1) s0a = fmaf(arow[i - 1], col[i - 1], s0a);
+                    col[i] = (i == j) ? 1.f : (i > j ? -(s0a + s1a) : 0.f);
+                }
+    #pragma unroll
+                for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
+            }
+            nbar(2, 384);
+            // Off-diagonal blocks by distance d = I - J, all pairs of one distance
+            // at once: P = sum_{M=J}^{I-1} A'_IM T_MJ, then T_IJ = -T_II P. A
+            // thread computes two adjacent columns of one row.
+    #pragma unroll
+            for (int d = 1; d <= 3; ++d) {
+                const int njob = (4 - d) * 128;               // (pair, row, column pair)
+                const int q = tid >> 7, i = (tid >> 3) & 15, j = (tid & 7) * 2;
+                const int I = d + q, J = q;
+                if (tid < njob) {
+                    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+                    const float *arow = Ap + (16 * I + i) * AS;
+    #pragma unroll
+                    for (int M = 0; M < d; ++M) {
+                        const int k0 = 16 * (J + M);
+    #pragma unroll
+                        for (int m = 0; m < 16; m += 2) {
+                            const float x0 = arow[k0 + m], x1 = arow[k0 + m + 1];
+                            const float2 t0 = *reinterpret_cast<const float2 *>(Tm + (k0 + m) * AS + 16 * J + j);
+                            const float2 t1 = *reinterpret_cast<const float2 *>(Tm + (k0 + m + 1) * AS + 16 * J + j);
+                            a0.x = fmaf(x0, t0.x, a0.x);
+                            a0.y = fmaf(x0, t0.y, a0.y);
+                            a1.x = fmaf(x1, t1.x, a1.x);
+                            a1.y = fmaf(x1, t1.y, a1.y);
+                        }
+                    }
+                    *reinterpret_cast<float2 *>(Pp + q * 256 + i * 16 + j) = make_float2(a0.x + a1.x, a0.y + a1.y);
+                }
+                nbar(2, 384);
+                if (tid < njob) {
+                    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
+                    const float *trow = Tm + (16 * I + i) * AS + 16 * I;
+    #pragma unroll
+                    for (int m = 0; m < 16; m += 2) {
+                        const float x0 = trow[m], x1 = trow[m + 1];
+                        const float2 p0 = *reinterpret_cast<const float2 *>(Pp + q * 256 + m * 16 + j);
+                        const float2 p1 = *reinterpret_cast<const float2 *>(Pp + q * 256 + (m + 1) * 16 + j);
+                        a0.x = fmaf(x0, p0.x, a0.x);
+                        a0.y = fmaf(x0, p0.y, a0.y);
+                        a1.x = fmaf(x1, p1.x, a1.x);
+                        a1.y = fmaf(x1, p1.y, a1.y);
+                    }
+                    *reinterpret_cast<float2 *>(Tm + (16 * I + i) * AS + 16 * J + j) =
+                        make_float2(-(a0.x + a1.x), -(a0.y + a1.y));
+                }
+                nbar(2, 384);
+            }
+            } else {
+                p4_side();
+            }
+            cbar();
+
+            // ---- P5: TB = T diag(beta) hi/lo; Aqk's upper blocks zeroed ----
+            for (int e = tid; e < BT * (BT / 2); e += kThreads) {
+                const int j = e / (BT / 2), jc = (e % (BT / 2)) * 2;
+                const float x0 = (jc <= j) ? Tm[j * AS + jc] * vec[L::vBeta + jc] : 0.f;
+                const float x1 = (jc + 1 <= j) ? Tm[j * AS + jc + 1] * vec[L::vBeta + jc + 1] : 0.f;
+                uint32_t hi, lo;
+                split2(x0, x1, hi, lo);
+                *reinterpret_cast<uint32_t *>(TBh + swz<BT>(j, jc)) = hi;
+                *reinterpret_cast<uint32_t *>(TBl + swz<BT>(j, jc)) = lo;
+                // Aqk's strictly-upper 16x16 blocks are never computed but are read
+                // by the full-width tensor-core product: make them zero.
+                if ((jc >> 4) > (j >> 4)) {
+                    *reinterpret_cast<uint32_t *>(AQh + swz<BT>(j, jc)) = 0u;
+                    *reinterpret_cast<uint32_t *>(AQl + swz<BT>(j, jc)) = 0u;
+                }
+            }
+            fence_async_smem();   // tiles written by threads -> read by the tensor core
+            cbar();
+            if (tid == 0) mbar_arrive(&sig[0]);   // u = TB v may start
+            if (has_next) load_beta(c + 1);
+
+            // ---- P7: W = TB (kn e^{gc}); warp w owns key columns [8w, 8w+8) ----
+            // kn e^{gc} = X e^{m_I}: X's bf16 hi/lo fragments scaled exactly by 2^{m_I / ln 2}.
+            float wacc[4][4] = {};
+            if (warp < D / 8) {
+                uint32_t kbh[4][2], kbl[4][2];
+                const int kcol = 8 * warp + g;
+                const uint16_t *sv16 = reinterpret_cast<const uint16_t *>(vec + L::vS);
+    #pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    const uint32_t ob = 2 * fb_kn8(lane, 16 * ks, 8 * warp);
+                    ldsm_x2_t(kbh[ks], s_base + L::kX + ob);
+                    ldsm_x2_t(kbl[ks], s_base + L::kX + BT * D * 2 + ob);
+                    const uint32_t sc = static_cast<uint32_t>(sv16[ks * D + kcol]) * 0x10001u;
+                    kbh[ks][0] = bmul2(kbh[ks][0], sc);
+                    kbh[ks][1] = bmul2(kbh[ks][1], sc);
+                    kbl[ks][0] = bmul2(kbl[ks][0], sc);
+                    kbl[ks][1] = bmul2(kbl[ks][1], sc);
+                }
+    #pragma unroll
+                for (int mt = 0; mt < 4; ++mt) {
+    #pragma unroll
+                    for (int ks = 0; ks <= mt; ++ks) {
+                        uint32_t ah[4], al[4];
+                        ldsm_x4(ah, s_base + L::kTBh + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
+                        ldsm_x4(al, s_base + L::kTBl + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
+                        mma3(wacc[mt], ah, al, kbh[ks][0], kbh[ks][1], kbl[ks][0], kbl[ks][1]);
+                    }
+                }
+            }
+
+            // ---- P8: QG = Y e^{m_I} (exact), KD = Z e^{gl - m_J}, tracked K_r; in place ----
+            {
+                for (int j = tid; j < BT * D / 8; j += kThreads) {
+                    const int row = j / (D / 8), c = 8 * (j % (D / 8)), blk = row >> 4;
+                    const int o = f64(row, c);
+                    {
+                        const uint4 sc = *reinterpret_cast<const uint4 *>(
+                            reinterpret_cast<const uint16_t *>(vec + L::vS) + blk * D + c);
+                        const uint4 hq = *reinterpret_cast<const uint4 *>(QGh + o);
+                        const uint4 lq = *reinterpret_cast<const uint4 *>(QGl + o);
+                        *reinterpret_cast<uint4 *>(QGh + o) =
+                            make_uint4(bmul2(hq.x, sc.x), bmul2(hq.y, sc.y), bmul2(hq.z, sc.z), bmul2(hq.w, sc.w));
+                        *reinterpret_cast<uint4 *>(QGl + o) =
+                            make_uint4(bmul2(lq.x, sc.x), bmul2(lq.y, sc.y), bmul2(lq.z, sc.z), bmul2(lq.w, sc.w));
+                    }
+                    uint4 h = *reinterpret_cast<const uint4 *>(KDh + o);
+                    uint4 l = *reinterpret_cast<const uint4 *>(KDl + o);
+                    const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
+                    const float *eg = vec + L::vEglm + blk * D + c;
+                    float z[8];
+    #pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        z[2 * e] = bf16_lo(hw[e]) + bf16_lo(lw[e]);
+                        z[2 * e + 1] = bf16_hi(hw[e]) + bf16_hi(lw[e]);
+                    }
+                    uint32_t dh[4], dl[4];
+    #pragma unroll
+                    for (int e = 0; e < 4; ++e) split2(z[2 * e] * eg[2 * e], z[2 * e + 1] * eg[2 * e + 1], dh[e], dl[e]);
+                    *reinterpret_cast<uint4 *>(KDh + o) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
+                    *reinterpret_cast<uint4 *>(KDl + o) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
+                    if (track_here) {
+                        const float *et = vec + L::vEtrm + blk * D + c;
+                        const bool live = row < rtrack;
+    #pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            split2(live ? z[2 * e] * et[2 * e] : 0.f, live ? z[2 * e + 1] * et[2 * e + 1] : 0.f, dh[e],
+                                   dl[e]);
+                        *reinterpret_cast<uint4 *>(KRh + o) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
+                        *reinterpret_cast<uint4 *>(KRl + o) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
+                    }
+                }
+            }
+            cbar();   // X fully consumed: W replaces it
+            if (warp < D / 8) {
+    #pragma unroll
+                for (int mt = 0; mt < 4; ++mt)
+    #pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const int j = 16 * mt + g + 8 * hf;
+                        const int kcol = 8 * warp + 2 * t4;
+                        uint32_t hi, lo;
+                        split2(wacc[mt][2 * hf], wacc[mt][2 * hf + 1], hi, lo);
+                        *reinterpret_cast<uint32_t *>(Wh + f64(j, kcol)) = hi;
+                        *reinterpret_cast<uint32_t *>(Wl + f64(j, kcol)) = lo;
+                    }
+            }
+            fence_async_smem();   // tiles written by threads -> read by the tensor core
+            cbar();
+            if (tid == 0) mbar_arrive(&sig[1]);   // W, QG, KD (and K_r) are in place: W S and QG S may start
+
+            // ---- P9: the state scan: -v'^T (fp32) -> v'^T hi/lo A operand, 16 columns per warp ----
+            if (!mbar_wait(&bars[0], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
+                report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
-            // The v tile is consumed: fetch the next one.
-            if (has_next && !track_here && tid == 0) issue_v(c + 1);
-            // -v'^T (fp32) -> v'^T hi/lo A operand, 16 columns per warp.
             {
                 uint32_t r[16], hi[8], lo[8];
                 tmem_ld16(tq + kColNU + 16 * cs, r);
                 tmem_ld_wait();
-#pragma unroll
+    #pragma unroll
                 for (int e = 0; e < 8; ++e)
                     split2(-__uint_as_float(r[2 * e]), -__uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
                 tmem_st8(tq + kColVH + 8 * cs, hi);
                 tmem_st8(tq + kColVL + 8 * cs, lo);
             }
-            // Tracked prefix: S^T e^{gc_{r-1}} into the freed hi/lo columns, then
-            // the deferred S^T e^{gl}.
+            // Tracked prefix: S^T e^{gc_{r-1}} into the S hi/lo columns (consumed:
+            // their last reader finished before bars[0]), then the deferred S^T e^{gl}.
             if (track_here) {
                 uint32_t r[SC], t[SC];
                 tmem_ld<SC>(tq + kColS + SC * cs, r);
                 tmem_ld_wait();
-#pragma unroll
+    #pragma unroll
                 for (int e = 0; e < SC; ++e) {
                     t[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEtr + SC * cs + e]);
                     r[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEgl + SC * cs + e]);
@@ -1064,100 +1190,60 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tmem_st_wait();
             tc_fence_before();
-            __syncthreads();
-            if (tid == 0) {
-                tc_fence_after();
-                constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
-                constexpr uint32_t id_kd = idesc_bf16(128, D, false, true, false);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
-                    const uint64_t dh = sdesc(s_base + L::kZ + kk * 2048, 8192, 1024);
-                    const uint64_t dl = sdesc(s_base + L::kZ + BT * D * 2 + kk * 2048, 8192, 1024);
-                    umma_ts(tmem + kColS, al, dh, id_kd, 1u);
-                    umma_ts(tmem + kColS, ah, dl, id_kd, 1u);
-                    umma_ts(tmem + kColS, ah, dh, id_kd, 1u);
-                    const uint64_t qh = sdesc(s_base + L::kAQh + kk * 32, 16, 1024);
-                    const uint64_t ql = sdesc(s_base + L::kAQl + kk * 32, 16, 1024);
-                    umma_ts(tmem + kColO, al, qh, id_n64, 1u);
-                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
-                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
-                    if (track_here) {
-                        const uint64_t rh = sdesc(s_base + L::kRawQ + kk * 2048, 8192, 1024);
-                        const uint64_t rl = sdesc(s_base + L::kRawK + kk * 2048, 8192, 1024);
-                        umma_ts(tmem + kColTR, al, rh, id_kd, 1u);
-                        umma_ts(tmem + kColTR, ah, rl, id_kd, 1u);
-                        umma_ts(tmem + kColTR, ah, rh, id_kd, 1u);
-                    }
-                }
-                umma_commit(&bars[1]);
-            }
-            if (!mbar_wait(&bars[1], ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
-            tc_fence_after();
-            // o rows of this chunk: lane = value row, column = chunk row. Each
-            // warp converts 16 rows; the bf16 tile is staged row-major in the
-            // W region (consumed by the first batch) and leaves by TMA.
-            {
-                uint32_t r[16];
-                tmem_ld16(tq + kColO + 16 * cs, r);
-                tmem_ld_wait();
-                if (p.out_fp32) {
-                    if (srow < D) {
-                        float *o = static_cast<float *>(p.out) + (t0 * H + h) * D + srow;
-                        const int64_t row_stride = static_cast<int64_t>(H) * D;
-#pragma unroll
-                        for (int e = 0; e < 16; ++e)
-                            if (16 * cs + e < n) o[(16 * cs + e) * row_stride] = __uint_as_float(r[e]);
-                    }
-                } else {
-                    if (srow < D) {
-#pragma unroll
-                        for (int e = 0; e < 16; ++e)
-                            Ostage[(16 * cs + e) * D + srow] = __float2bfloat16_rn(__uint_as_float(r[e]));
-                    }
-                    fence_async_smem();
-                }
-            }
-            __syncthreads();
-            if (!p.out_fp32 && tid == 0) {
-                if (n == BT) {
-                    tma_store_3d(&maps.o, Ostage, 0, h, static_cast<int>(t0));
-                } else {
-                    __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (t0 * H + h) * D;
-                    for (int rw = 0; rw < n; ++rw)
-                        bulk_s2g(o + static_cast<int64_t>(rw) * H * D, Ostage + rw * D, D * 2);
-                }
-                bulk_commit();
-            }
+            cbar();
+            if (tid == 0) mbar_arrive(&sig[2]);   // the state update and o += Aqk v' may start
             if (track_here) {
+                // A tracked chunk finishes here: the checkpoint leaves tensor memory
+                // before the next S split reuses its columns; the o tile goes too.
+                if (!mbar_wait(&bars[3], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
+                    report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                tc_fence_after();
+                o_cols(OstX, t0, n, 16 * cs, 16);
+                fence_async_smem();
+                cbar();
+                if (tid == 0) o_store(OstX, t0, n);
                 float *ts = p.state + tslot * s0 + h * s1;
                 uint32_t r[SC];
                 tmem_ld<SC>(tq + kColTR + SC * cs, r);
                 tmem_ld_wait();
                 if (srow < D) {
-#pragma unroll
+    #pragma unroll
                     for (int e = 0; e < SC; ++e) ts[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
                 }
+                o_pending = false;
+            } else {
+                o_pending = true;
+                o_t0 = t0;
+                o_n = n;
+            }
+            }   // chunk loop
+
+        if (nchunks > 0) {
+            const uint32_t lph = static_cast<uint32_t>((nchunks - 1) & 1);
+            if (o_pending) {
+                if (!mbar_wait(&bars[3], lph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                tc_fence_after();
+                o_cols(OstX, o_t0, o_n, 16 * cs, 16);
+                fence_async_smem();
+                cbar();
+                if (tid == 0) o_store(OstX, o_t0, o_n);
+            }
+            if (!mbar_wait(&bars[1], lph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+        }
+        // Final state S^T -> pool slot (padding slot 0 is never written).
+        {
+            float *hs = p.state + slot * s0 + h * s1;
+            uint32_t r[SC];
+            tmem_ld<SC>(tq + kColS + SC * cs, r);
+            tmem_ld_wait();
+            if (slot > 0 && srow < D) {
+#pragma unroll
+                for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
             }
         }
-        if (track_here && has_next) {
-            __syncthreads();   // K_r (raw region) is consumed
-            if (tid == 0) issue_tiles(c + 1, true);
-            load_beta(c + 1);
-        }
+        if (tid == 0 || tid == 384) bulk_wait_all();   // output stores complete before the CTA exits
     }
-    // Final state S^T -> pool slot (padding slot 0 is never written).
-    {
-        float *hs = p.state + slot * s0 + h * s1;
-        uint32_t r[SC];
-        tmem_ld<SC>(tq + kColS + SC * cs, r);
-        tmem_ld_wait();
-        if (slot > 0 && srow < D) {
-#pragma unroll
-            for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
-        }
-    }
-    if (tid == 0) bulk_wait_all();   // output stores complete before the CTA exits
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -1239,7 +1325,7 @@ static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
     }
     if (order != nullptr) chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
     const int64_t grid = static_cast<int64_t>(a->num_req) * a->head_count;
-    chunk::chunk_kernel<D, MODE><<<static_cast<unsigned>(grid), chunk::kThreads, L::kAlloc, st>>>(*a, order, maps);
+    chunk::chunk_kernel<D, MODE><<<static_cast<unsigned>(grid), chunk::kThreads + 32, L::kAlloc, st>>>(*a, order, maps);
     return KDA_OK;
 }
 
