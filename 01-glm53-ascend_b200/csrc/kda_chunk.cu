@@ -1070,39 +1070,55 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             if (tid == 0) mbar_arrive(&sig[0]);   // u = TB v may start
             if (has_next) load_beta(c + 1);
 
-            // ---- P7: W = TB (kn e^{gc}); warp w owns key columns [8w, 8w+8) ----
-            // kn e^{gc} = X e^{m_I}: X's bf16 hi/lo fragments scaled exactly by 2^{m_I / ln 2}.
-            float wacc[4][4] = {};
-            if (warp < D / 8) {
-                uint32_t kbh[4][2], kbl[4][2];
-                const int kcol = 8 * warp + g;
+            // ---- P7 (warps 0..D/16-1): W = TB (kn e^{gc}), 16 key columns per warp ----
+            // kn e^{gc} = X e^{m_I}: X's bf16 hi/lo fragments scaled exactly by
+            // 2^{m_I / ln 2}. The other warps run P8 meanwhile (disjoint tiles).
+            constexpr int NW7 = D / 16;
+            if (warp < NW7) {
+                float wacc[4][2][4] = {};
                 const uint16_t *sv16 = reinterpret_cast<const uint16_t *>(vec + L::vS);
-    #pragma unroll
+#pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
-                    const uint32_t ob = 2 * fb_kn8(lane, 16 * ks, 8 * warp);
-                    ldsm_x2_t(kbh[ks], s_base + L::kX + ob);
-                    ldsm_x2_t(kbl[ks], s_base + L::kX + BT * D * 2 + ob);
-                    const uint32_t sc = static_cast<uint32_t>(sv16[ks * D + kcol]) * 0x10001u;
-                    kbh[ks][0] = bmul2(kbh[ks][0], sc);
-                    kbh[ks][1] = bmul2(kbh[ks][1], sc);
-                    kbl[ks][0] = bmul2(kbl[ks][0], sc);
-                    kbl[ks][1] = bmul2(kbl[ks][1], sc);
-                }
-    #pragma unroll
-                for (int mt = 0; mt < 4; ++mt) {
-    #pragma unroll
-                    for (int ks = 0; ks <= mt; ++ks) {
+                    uint32_t kbh[4], kbl[4];
+                    const uint32_t ob = 2 * f64(16 * ks + (lane & 7) + (((lane >> 3) & 1) << 3), 16 * warp + ((lane >> 4) << 3));
+                    ldsm_x4_t(kbh, s_base + L::kX + ob);
+                    ldsm_x4_t(kbl, s_base + L::kX + BT * D * 2 + ob);
+                    const uint32_t s0 = static_cast<uint32_t>(sv16[ks * D + 16 * warp + g]) * 0x10001u;
+                    const uint32_t s1 = static_cast<uint32_t>(sv16[ks * D + 16 * warp + 8 + g]) * 0x10001u;
+                    kbh[0] = bmul2(kbh[0], s0);
+                    kbh[1] = bmul2(kbh[1], s0);
+                    kbh[2] = bmul2(kbh[2], s1);
+                    kbh[3] = bmul2(kbh[3], s1);
+                    kbl[0] = bmul2(kbl[0], s0);
+                    kbl[1] = bmul2(kbl[1], s0);
+                    kbl[2] = bmul2(kbl[2], s1);
+                    kbl[3] = bmul2(kbl[3], s1);
+#pragma unroll
+                    for (int mt = ks; mt < 4; ++mt) {
                         uint32_t ah[4], al[4];
                         ldsm_x4(ah, s_base + L::kTBh + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
                         ldsm_x4(al, s_base + L::kTBl + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
-                        mma3(wacc[mt], ah, al, kbh[ks][0], kbh[ks][1], kbl[ks][0], kbl[ks][1]);
+                        mma3(wacc[mt][0], ah, al, kbh[0], kbh[1], kbl[0], kbl[1]);
+                        mma3(wacc[mt][1], ah, al, kbh[2], kbh[3], kbl[2], kbl[3]);
                     }
                 }
-            }
-
+                nbar(4, 32 * NW7);   // X fully consumed: W replaces it
+#pragma unroll
+                for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {
+                            const int j = 16 * mt + g + 8 * hf;
+                            const int kcol = 16 * warp + 8 * nt + 2 * t4;
+                            uint32_t hi, lo;
+                            split2(wacc[mt][nt][2 * hf], wacc[mt][nt][2 * hf + 1], hi, lo);
+                            *reinterpret_cast<uint32_t *>(Wh + f64(j, kcol)) = hi;
+                            *reinterpret_cast<uint32_t *>(Wl + f64(j, kcol)) = lo;
+                        }
             // ---- P8: QG = Y e^{m_I} (exact), KD = Z e^{gl - m_J}, tracked K_r; in place ----
-            {
-                for (int j = tid; j < BT * D / 8; j += kThreads) {
+            } else {
+                for (int j = tid - 32 * NW7; j < BT * D / 8; j += kThreads - 32 * NW7) {
                     const int row = j / (D / 8), c = 8 * (j % (D / 8)), blk = row >> 4;
                     const int o = f64(row, c);
                     {
@@ -1141,20 +1157,6 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                         *reinterpret_cast<uint4 *>(KRl + o) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
                     }
                 }
-            }
-            cbar();   // X fully consumed: W replaces it
-            if (warp < D / 8) {
-    #pragma unroll
-                for (int mt = 0; mt < 4; ++mt)
-    #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        const int j = 16 * mt + g + 8 * hf;
-                        const int kcol = 8 * warp + 2 * t4;
-                        uint32_t hi, lo;
-                        split2(wacc[mt][2 * hf], wacc[mt][2 * hf + 1], hi, lo);
-                        *reinterpret_cast<uint32_t *>(Wh + f64(j, kcol)) = hi;
-                        *reinterpret_cast<uint32_t *>(Wl + f64(j, kcol)) = lo;
-                    }
             }
             fence_async_smem();   // tiles written by threads -> read by the tensor core
             cbar();
