@@ -311,10 +311,11 @@ struct Smem {
     // the tracked-prefix operand K_r (hi at kRawQ, lo at kRawK) as well.
     static constexpr int kAp = 0;
     static constexpr int kT = kAp + BT * AS * 4;
-    static constexpr int kP = kT + BT * AS * 4;            // fp32 [3][16][16] inverse partial products
+    static constexpr int PS = 20;                          // row stride of the P scratch blocks
+    static constexpr int kP = kT + BT * AS * 4;            // fp32 [3][16][PS] inverse partial products
     // bf16 [64][D] o tile of the previous chunk, staged for its TMA store
     // while A', T and P occupy the front of the raw region.
-    static constexpr int kOst = r1k(kP + 3 * 256 * 4);
+    static constexpr int kOst = r1k(kP + 3 * 16 * PS * 4);
     static constexpr int kOstEnd = kOst + BT * D * 2;
     static constexpr int kV = r1k(kRawEnd > kOstEnd ? kRawEnd : kOstEnd);   // bf16 f64 tile [j][v]
     // bf16 hi/lo f64 tiles (hi at the base, lo BT*D*2 bytes later):
@@ -945,124 +946,158 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
             cbar();
 
-                // Warps 12..15 (one per lane quadrant), beside the inverse: this
-            // chunk's S^T is split into the bf16 hi/lo A operand and rescaled
-            // by e^{gl} (deferred on a tracked chunk).
-            auto p4_side = [&] {
+            // ---- P4: T = (I + A')^-1 on warps 0-3, beside the S split on warps 8-15 ----
+            if (warp < 4) {
+                // Diagonal 16x16 blocks: lane (I, j) of warps 0-1 solves column j
+                // of block I by forward substitution in fp32 (entries above the
+                // diagonal stay 0, so the unpredicated sums are exact).
+                if (warp < 2) {
+                    const int I = 2 * warp + (lane >> 4), j = lane & 15;
+                    float col[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float *arow = Ap + (16 * I + i) * AS + 16 * I;
+                        float s0a = 0.f, s1a = 0.f;
+#pragma unroll
+                        for (int m = 0; m + 1 < i; m += 2) {
+                            s0a = fmaf(arow[m], col[m], s0a);
+                            s1a = fmaf(arow[m + 1], col[m + 1], s1a);
+                        }
+                        if (i & 1) s0a = fmaf(arow[i - 1], col[i - 1], s0a);
+                        col[i] = (i == j) ? 1.f : (i > j ? -(s0a + s1a) : 0.f);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
+                }
+                nbar(2, 128);
+                // Off-diagonal blocks by distance d = I - J, one block per warp:
+                // P = sum_{M=J}^{I-1} A'_IM T_MJ, then T_IJ = -T_II P, both as
+                // split-bf16 products (fp32 operands split into hi + lo).
+                float *const Pw = Pp + warp * 16 * L::PS;
+#pragma unroll
+                for (int d = 1; d <= 3; ++d) {
+                    if (warp < 4 - d) {
+                        const int J = warp, I = warp + d;
+                        // B fragments of a fp32 16x16 block at (r0, c0) of a row-major
+                        // tile with row stride `ld`, columns [c0 + 8 nt, +8).
+                        auto bfrag = [&](const float *base, int ld, int r0, int c0, int nt, uint32_t &bh0,
+                                         uint32_t &bh1, uint32_t &bl0, uint32_t &bl1) {
+                            const float *b = base + (r0 + 2 * t4) * ld + c0 + 8 * nt + g;
+                            split2(b[0], b[ld], bh0, bl0);
+                            split2(b[8 * ld], b[9 * ld], bh1, bl1);
+                        };
+                        auto afrag = [&](const float *base, int ld, int r0, int c0, uint32_t (&ah)[4],
+                                         uint32_t (&al)[4]) {
+                            const float *a = base + (r0 + g) * ld + c0 + 2 * t4;
+                            const float2 a0 = *reinterpret_cast<const float2 *>(a);
+                            const float2 a1 = *reinterpret_cast<const float2 *>(a + 8 * ld);
+                            const float2 a2 = *reinterpret_cast<const float2 *>(a + 8);
+                            const float2 a3 = *reinterpret_cast<const float2 *>(a + 8 * ld + 8);
+                            split2(a0.x, a0.y, ah[0], al[0]);
+                            split2(a1.x, a1.y, ah[1], al[1]);
+                            split2(a2.x, a2.y, ah[2], al[2]);
+                            split2(a3.x, a3.y, ah[3], al[3]);
+                        };
+                        float pacc[2][4] = {};
+#pragma unroll
+                        for (int m = 0; m < d; ++m) {
+                            const int M = J + m;
+                            uint32_t ah[4], al[4];
+                            afrag(Ap, AS, 16 * I, 16 * M, ah, al);
+#pragma unroll
+                            for (int nt = 0; nt < 2; ++nt) {
+                                uint32_t bh0, bh1, bl0, bl1;
+                                bfrag(Tm, AS, 16 * M, 16 * J, nt, bh0, bh1, bl0, bl1);
+                                mma3(pacc[nt], ah, al, bh0, bh1, bl0, bl1);
+                            }
+                        }
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt) {
+                            *reinterpret_cast<float2 *>(Pw + g * L::PS + 8 * nt + 2 * t4) = make_float2(pacc[nt][0], pacc[nt][1]);
+                            *reinterpret_cast<float2 *>(Pw + (g + 8) * L::PS + 8 * nt + 2 * t4) =
+                                make_float2(pacc[nt][2], pacc[nt][3]);
+                        }
+                        __syncwarp();
+                        uint32_t ah[4], al[4];
+                        afrag(Tm, AS, 16 * I, 16 * I, ah, al);
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt) {
+                            uint32_t bh0, bh1, bl0, bl1;
+                            bfrag(Pw, L::PS, 0, 0, nt, bh0, bh1, bl0, bl1);
+                            float tacc[4] = {};
+                            mma3(tacc, ah, al, bh0, bh1, bl0, bl1);
+                            float *t = Tm + (16 * I + g) * AS + 16 * J + 8 * nt + 2 * t4;
+                            *reinterpret_cast<float2 *>(t) = make_float2(-tacc[0], -tacc[1]);
+                            *reinterpret_cast<float2 *>(t + 8 * AS) = make_float2(-tacc[2], -tacc[3]);
+                        }
+                        __syncwarp();
+                    }
+                    nbar(2, 128);
+                }
+            } else if (warp >= 8) {
+                // S^T -> bf16 hi/lo A operand and S^T <- S^T e^{gl} (deferred on a
+                // tracked chunk): two warps per lane quadrant, half the columns each.
                 if (c > 0) {
                     if (!mbar_wait(&bars[1], static_cast<uint32_t>((c - 1) & 1), p.status) && lane == 0)
                         report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
                     tc_fence_after();
                 }
+                const int cb = ((warp >> 2) & 1) * (D / 2);
 #pragma unroll
-                for (int c32 = 0; c32 < D / 32; ++c32) {
+                for (int c32 = 0; c32 < D / 64; ++c32) {
+                    const int col = cb + 32 * c32;
                     uint32_t r[32], hi[16], lo[16];
-                    tmem_ld32(tq + kColS + 32 * c32, r);
+                    tmem_ld32(tq + kColS + col, r);
                     tmem_ld_wait();
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
                         split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
-                    tmem_st16(tq + kColSH + 16 * c32, hi);
-                    tmem_st16(tq + kColSL + 16 * c32, lo);
+                    tmem_st16(tq + kColSH + col / 2, hi);
+                    tmem_st16(tq + kColSL + col / 2, lo);
                     if (!track_here) {
-                        const float *eg = vec + L::vEgl + 32 * c32;
+                        const float4 *eg = reinterpret_cast<const float4 *>(vec + L::vEgl + col);
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * eg[e]);
-                        tmem_st32(tq + kColS + 32 * c32, r);
+                        for (int e4 = 0; e4 < 8; ++e4) {
+                            const float4 f = eg[e4];
+                            r[4 * e4] = __float_as_uint(__uint_as_float(r[4 * e4]) * f.x);
+                            r[4 * e4 + 1] = __float_as_uint(__uint_as_float(r[4 * e4 + 1]) * f.y);
+                            r[4 * e4 + 2] = __float_as_uint(__uint_as_float(r[4 * e4 + 2]) * f.z);
+                            r[4 * e4 + 3] = __float_as_uint(__uint_as_float(r[4 * e4 + 3]) * f.w);
+                        }
+                        tmem_st32(tq + kColS + col, r);
                     }
                 }
                 tmem_st_wait();
                 tc_fence_before();
-            };
-            // ---- P4: T = (I + A')^-1, blocked forward substitution in fp32 (warps 0-11) ----
-            if (warp < 12) {
-            // Diagonal 16x16 blocks: lane (I, j) of warps 0-1 solves column j of
-            // block I (entries above the diagonal of the column stay 0, so the
-            // unpredicated sums are exact); two partial sums halve the FMA chain.
-            if (warp < 2) {
-                const int I = 2 * warp + (lane >> 4), j = lane & 15;
-                float col[16];
-    #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float *arow = Ap + (16 * I + i) * AS + 16 * I;
-                    float s0a = 0.f, s1a = 0.f;
-    #pragma unroll
-                    for (int m = 0; m + 1 < i; m += 2) {
-                        s0a = fmaf(arow[m], col[m], s0a);
-                        s1a = fmaf(arow[m + 1], col[m + 1], s1a);
-                    }
-                    if (i & 1) s0a = fmaf(arow[i - 1], col[i - 1], s0a);
-                    col[i] = (i == j) ? 1.f : (i > j ? -(s0a + s1a) : 0.f);
-                }
-    #pragma unroll
-                for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
-            }
-            nbar(2, 384);
-            // Off-diagonal blocks by distance d = I - J, all pairs of one distance
-            // at once: P = sum_{M=J}^{I-1} A'_IM T_MJ, then T_IJ = -T_II P. A
-            // thread computes two adjacent columns of one row.
-    #pragma unroll
-            for (int d = 1; d <= 3; ++d) {
-                const int njob = (4 - d) * 128;               // (pair, row, column pair)
-                const int q = tid >> 7, i = (tid >> 3) & 15, j = (tid & 7) * 2;
-                const int I = d + q, J = q;
-                if (tid < njob) {
-                    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
-                    const float *arow = Ap + (16 * I + i) * AS;
-    #pragma unroll
-                    for (int M = 0; M < d; ++M) {
-                        const int k0 = 16 * (J + M);
-    #pragma unroll
-                        for (int m = 0; m < 16; m += 2) {
-                            const float x0 = arow[k0 + m], x1 = arow[k0 + m + 1];
-                            const float2 t0 = *reinterpret_cast<const float2 *>(Tm + (k0 + m) * AS + 16 * J + j);
-                            const float2 t1 = *reinterpret_cast<const float2 *>(Tm + (k0 + m + 1) * AS + 16 * J + j);
-                            a0.x = fmaf(x0, t0.x, a0.x);
-                            a0.y = fmaf(x0, t0.y, a0.y);
-                            a1.x = fmaf(x1, t1.x, a1.x);
-                            a1.y = fmaf(x1, t1.y, a1.y);
-                        }
-                    }
-                    *reinterpret_cast<float2 *>(Pp + q * 256 + i * 16 + j) = make_float2(a0.x + a1.x, a0.y + a1.y);
-                }
-                nbar(2, 384);
-                if (tid < njob) {
-                    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
-                    const float *trow = Tm + (16 * I + i) * AS + 16 * I;
-    #pragma unroll
-                    for (int m = 0; m < 16; m += 2) {
-                        const float x0 = trow[m], x1 = trow[m + 1];
-                        const float2 p0 = *reinterpret_cast<const float2 *>(Pp + q * 256 + m * 16 + j);
-                        const float2 p1 = *reinterpret_cast<const float2 *>(Pp + q * 256 + (m + 1) * 16 + j);
-                        a0.x = fmaf(x0, p0.x, a0.x);
-                        a0.y = fmaf(x0, p0.y, a0.y);
-                        a1.x = fmaf(x1, p1.x, a1.x);
-                        a1.y = fmaf(x1, p1.y, a1.y);
-                    }
-                    *reinterpret_cast<float2 *>(Tm + (16 * I + i) * AS + 16 * J + j) =
-                        make_float2(-(a0.x + a1.x), -(a0.y + a1.y));
-                }
-                nbar(2, 384);
-            }
-            } else {
-                p4_side();
             }
             cbar();
 
             // ---- P5: TB = T diag(beta) hi/lo; Aqk's upper blocks zeroed ----
-            for (int e = tid; e < BT * (BT / 2); e += kThreads) {
-                const int j = e / (BT / 2), jc = (e % (BT / 2)) * 2;
-                const float x0 = (jc <= j) ? Tm[j * AS + jc] * vec[L::vBeta + jc] : 0.f;
-                const float x1 = (jc + 1 <= j) ? Tm[j * AS + jc + 1] * vec[L::vBeta + jc + 1] : 0.f;
-                uint32_t hi, lo;
-                split2(x0, x1, hi, lo);
-                *reinterpret_cast<uint32_t *>(TBh + swz<BT>(j, jc)) = hi;
-                *reinterpret_cast<uint32_t *>(TBl + swz<BT>(j, jc)) = lo;
+            // One 8-column chunk of one row per thread.
+            {
+                const int j = tid >> 3, c8 = (tid & 7) * 8;
+                uint4 hv = make_uint4(0u, 0u, 0u, 0u), lv = make_uint4(0u, 0u, 0u, 0u);
+                if (c8 <= j) {
+                    const float4 t0v = *reinterpret_cast<const float4 *>(Tm + j * AS + c8);
+                    const float4 t1v = *reinterpret_cast<const float4 *>(Tm + j * AS + c8 + 4);
+                    const float4 b0v = *reinterpret_cast<const float4 *>(vec + L::vBeta + c8);
+                    const float4 b1v = *reinterpret_cast<const float4 *>(vec + L::vBeta + c8 + 4);
+                    const float x[8] = {t0v.x * b0v.x, t0v.y * b0v.y, t0v.z * b0v.z, t0v.w * b0v.w,
+                                        t1v.x * b1v.x, t1v.y * b1v.y, t1v.z * b1v.z, t1v.w * b1v.w};
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        split2(c8 + 2 * e <= j ? x[2 * e] : 0.f, c8 + 2 * e + 1 <= j ? x[2 * e + 1] : 0.f, hw[e], lw[e]);
+                    hv = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    lv = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
+                *reinterpret_cast<uint4 *>(TBh + swz<BT>(j, c8)) = hv;
+                *reinterpret_cast<uint4 *>(TBl + swz<BT>(j, c8)) = lv;
                 // Aqk's strictly-upper 16x16 blocks are never computed but are read
                 // by the full-width tensor-core product: make them zero.
-                if ((jc >> 4) > (j >> 4)) {
-                    *reinterpret_cast<uint32_t *>(AQh + swz<BT>(j, jc)) = 0u;
-                    *reinterpret_cast<uint32_t *>(AQl + swz<BT>(j, jc)) = 0u;
+                if ((c8 >> 4) > (j >> 4)) {
+                    *reinterpret_cast<uint4 *>(AQh + swz<BT>(j, c8)) = make_uint4(0u, 0u, 0u, 0u);
+                    *reinterpret_cast<uint4 *>(AQl + swz<BT>(j, c8)) = make_uint4(0u, 0u, 0u, 0u);
                 }
             }
             fence_async_smem();   // tiles written by threads -> read by the tensor core
@@ -1134,7 +1169,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     uint4 h = *reinterpret_cast<const uint4 *>(KDh + o);
                     uint4 l = *reinterpret_cast<const uint4 *>(KDl + o);
                     const uint32_t hw[4] = {h.x, h.y, h.z, h.w}, lw[4] = {l.x, l.y, l.z, l.w};
-                    const float *eg = vec + L::vEglm + blk * D + c;
+                    const float4 eg0 = *reinterpret_cast<const float4 *>(vec + L::vEglm + blk * D + c);
+                    const float4 eg1 = *reinterpret_cast<const float4 *>(vec + L::vEglm + blk * D + c + 4);
+                    const float eg[8] = {eg0.x, eg0.y, eg0.z, eg0.w, eg1.x, eg1.y, eg1.z, eg1.w};
                     float z[8];
     #pragma unroll
                     for (int e = 0; e < 4; ++e) {
@@ -1147,7 +1184,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     *reinterpret_cast<uint4 *>(KDh + o) = make_uint4(dh[0], dh[1], dh[2], dh[3]);
                     *reinterpret_cast<uint4 *>(KDl + o) = make_uint4(dl[0], dl[1], dl[2], dl[3]);
                     if (track_here) {
-                        const float *et = vec + L::vEtrm + blk * D + c;
+                        const float4 et0 = *reinterpret_cast<const float4 *>(vec + L::vEtrm + blk * D + c);
+                        const float4 et1 = *reinterpret_cast<const float4 *>(vec + L::vEtrm + blk * D + c + 4);
+                        const float et[8] = {et0.x, et0.y, et0.z, et0.w, et1.x, et1.y, et1.z, et1.w};
                         const bool live = row < rtrack;
     #pragma unroll
                         for (int e = 0; e < 4; ++e)
