@@ -843,6 +843,15 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     }
                 }
             }
+            // The previous chunk's last products (o = QG S + Aqk v', the state
+            // update) still read QG, KD and Aqk in the Y, Z and Aqk tiles this
+            // chunk rewrites: wait for them (bars[3] tracks all three) before the
+            // tiles below; the factor tables above touch none of them.
+            if (c > 0) {
+                if (!mbar_wait(&bars[3], static_cast<uint32_t>((c - 1) & 1), p.status) && tid == 0)
+                    report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                tc_fence_after();
+            }
             for (int j = tid; j < BT * D / 8; j += kThreads) {
                 const int row = j / (D / 8), c = 8 * (j % (D / 8));
                 const float4 x0 = *reinterpret_cast<const float4 *>(xg + row * D + c);
