@@ -12,30 +12,37 @@
 //   S   <- e^{gc_last} S + (kn e^{gc_last - gc})^T v'
 //
 // B200 design (no counterpart in the reference):
-//   * one CTA per (sequence, head), 16 warps, the whole chunk loop in one CTA;
-//     requests are visited longest-first (a one-block prologue kernel writes
-//     the order into the workspace).
+//   * one CTA per (sequence, head), the whole chunk loop in one CTA; requests
+//     are visited longest-first (a one-block prologue kernel writes the order
+//     into the workspace). 16 compute warps plus one producer warp whose
+//     single thread issues every TMA load and every tcgen05 product, in the
+//     order mbarrier signals from the compute warps allow, so no compute warp
+//     blocks on a tensor-core issue queue.
 //   * every tensor-core product splits each inexact fp32 operand into hi + lo
 //     bf16 and issues three products (hi.hi + hi.lo + lo.hi): plain bf16
 //     operands miss the output bar (5e-3 of the output RMS) by 3-13x on these
 //     inputs, the split form lands at ~2e-4.
 //   * the exponent range is handled with 16-row blocks anchored at their
-//     midpoint row m_I: X = kn e^{gc - m_I}, Y = qn e^{gc - m_I} and
-//     Z = kn e^{m_I - gc} stay within e^{+-8|g|}, and a block pair (I, J)
-//     is X_I (e^{m_I - m_J}) Z_J^T with the factor <= 1 (fp32 exp overflows at
+//     midpoint row, the anchor rounded to a multiple of ln 2:
+//     X = kn e^{gc - m_I}, Y = qn e^{gc - m_I} and Z = kn e^{m_I - gc} stay
+//     within e^{+-(8|g| + ln2/2)} and are split into bf16 hi/lo once; a block
+//     pair (I, J) is X_I (e^{m_I - m_J}) Z_J^T where the factor is an exact
+//     power of two <= 1, applied to Z's bf16 fragments without rounding, and
+//     QG = Y e^{m_I}, kn e^{gc} = X e^{m_I} likewise (fp32 exp overflows at
 //     e^88.7; the reference rebases per 32 rows for the same reason,
 //     kda_varlen_chunk.h:24-29).
-//   * intra-chunk products (A blocks, W) run on mma.sync with fragments built
-//     in registers; the state scan runs on the 5th-gen tensor core: the state
-//     S^T (value rows x key columns, the pool's own [V][K] order) lives in
-//     tensor memory as a 128-lane fp32 accumulator, its bf16 hi/lo split is
+//   * intra-chunk products (A blocks, inverse levels, W) run on mma.sync with
+//     ldmatrix fragments; the state scan runs on the 5th-gen tensor core: the
+//     state S^T (value rows x key columns, the pool's own [V][K] order) lives
+//     in tensor memory as a 128-lane fp32 accumulator, its bf16 hi/lo split is
 //     stored back to tensor memory and used as the A operand, and the
 //     intra-chunk results (W, QG, KD, TB, Aqk) are B operands in 128-byte
-//     swizzled shared-memory tiles. One thread issues the tcgen05.mma chain;
-//     warpgroup 0 converts accumulators and writes the output.
+//     swizzled shared-memory tiles. Conversions of tensor memory (state split,
+//     v', output) are spread over compute warps that the intra-chunk phases
+//     leave idle.
 //   * the next chunk's q/k/g (and v) tiles are fetched by TMA (one tensor
 //     map each, the v tile written in the 128-byte swizzle the tensor core
-//     reads) while the W product and the scan of this chunk run.
+//     reads) while this chunk runs; output tiles leave by TMA stores.
 //   * any sequence length: a partial last chunk is zero-filled (k = q = v =
 //     g = beta = 0), which leaves the state and the real rows unchanged.
 //   * every mbarrier wait is bounded; tensor memory is freed on every path.
