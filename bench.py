@@ -58,10 +58,12 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # output bf16 256 B.
 DECODE_BYTES_PER_TOKEN_HEAD = 65536 * 2 + 768 + 512 + 4 + 256
 
-# DRAM bytes (read + write) per launch from one ncu capture of each kernel at
-# the benchmark shape: profiles/decode_cfg2_ncu.md, profiles/chunk_cfg3_ncu.md.
+# DRAM bytes (read + write) per launch from one ncu capture of each kernel:
+# decode at the benchmark shape; chunk prefill captured with 8 of config 3's
+# 32 heads (412,781,824 B) and scaled by 4, traffic being proportional to the
+# heads processed.
 DECODE_TRAFFIC_PER_LAUNCH = 1026264832
-PREFILL_TRAFFIC_PER_LAUNCH = 1670459648
+PREFILL_TRAFFIC_PER_LAUNCH = 1651127296
 
 METRIC = "KDA tokens/s (prefill, decode) H32 d128 @1/2/4/8 B200; decode HBM GB/s vs peak"
 
@@ -406,6 +408,8 @@ def main():
     ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--mode", choices=("full", "kernel", "prefill-kernel"), default="full",
                     help="kernel / prefill-kernel: only the timed decode / chunk op loop (profiler captures)")
+    ap.add_argument("--prefill-heads", type=int, default=32,
+                    help="prefill-kernel mode: heads of config 3 (fewer keeps a full ncu capture small)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -419,7 +423,7 @@ def main():
     hbm_gbs, bf16_tf, bf16_tf_sus, peak_kind = _peaks()
     if args.mode == "prefill-kernel":
         from sgl_glm53_ascend_ops import ops, workloads
-        kw = workloads.config3(seed=2000 + dist.rank).to("cuda").kwargs()
+        kw = workloads.config3(seed=2000 + dist.rank, heads=args.prefill_heads).to("cuda").kwargs()
         ms = time_steps(lambda: ops.kda_varlen_chunk_g(**kw, prefill=True), args.steps, args.warmup, dist)
         if dist.rank == 0:
             print(json.dumps({"mode": "prefill-kernel", "ms_per_step": ms / args.steps}), flush=True)
