@@ -320,6 +320,38 @@ def bench_prefill(args, dist: Dist, hbm_gbs: float, bf16_tf: float, steps: int, 
     }
 
 
+def bench_prefill_long(args, dist: Dist, steps: int, warmup: int) -> dict:
+    """one 131,072-token sequence, 4 heads per GPU (the
+    configuration shards H=32 as 4 heads on each of 8 GPUs), fp32 initial
+    state from the pool. Every chunk of a head follows the previous one, so
+    this measures the serial inter-chunk state pass."""
+    from sgl_glm53_ascend_ops import ops, workloads
+
+    heads = 4
+    w = workloads.config4(seed=3000 + dist.rank, heads=heads)
+    d = w.to("cuda")
+    kw = d.kwargs()
+    pool0 = d.pool.clone()
+
+    def step():
+        ops.kda_varlen_chunk_g(**kw, prefill=True)
+
+    ms = time_steps(step, steps, warmup, dist) / steps
+    d.pool.copy_(pool0)
+    return {
+        "metric": "KDA long-context prefill tokens/s (chunk-64, configs[3])",
+        "value": round(dist.world * w.tokens * heads / (ms / 1e3), 1),
+        "unit": "token-heads/s",
+        "ms_per_step": round(ms, 4),
+        "per_chunk_us": round(ms * 1e3 / (w.tokens / 64), 3),
+        "steps": steps,
+        "warmup": warmup,
+        "config": {"workload": f"cfg4: 1 sequence x {w.tokens} tokens, {heads} heads per GPU (of H=32), "
+                               "K=V=128, fp32 initial state ~ 0.1 N(0,1), log-gate op",
+                   "scaling": "weak (4 heads per GPU)"},
+    }
+
+
 def cpu_prefill_rate(tokens: int, budget_s: float, seed: int = 8):
     """tokens/s of the CPU chunk oracle on one sequence of `tokens` tokens, H=32."""
     from oracle import kda_ref
@@ -406,7 +438,7 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-oracle work")
     ap.add_argument("--prefill-steps", type=int, default=20)
-    ap.add_argument("--mode", choices=("full", "kernel", "prefill-kernel"), default="full",
+    ap.add_argument("--mode", choices=("full", "kernel", "prefill-kernel", "prefill-long"), default="full",
                     help="kernel / prefill-kernel: only the timed decode / chunk op loop (profiler captures)")
     ap.add_argument("--prefill-heads", type=int, default=32,
                     help="prefill-kernel mode: heads of config 3 (fewer keeps a full ncu capture small)")
@@ -429,6 +461,12 @@ def main():
             print(json.dumps({"mode": "prefill-kernel", "ms_per_step": ms / args.steps}), flush=True)
         dist.close()
         return
+    if args.mode == "prefill-long":
+        r = bench_prefill_long(args, dist, steps=args.steps, warmup=args.warmup)
+        if dist.rank == 0:
+            print(json.dumps({"mode": "prefill-long", **r}), flush=True)
+        dist.close()
+        return
     if args.mode == "kernel":
         from sgl_glm53_ascend_ops import ops, workloads
         kw = workloads.config2(seed=1000 + dist.rank).to("cuda").kwargs()
@@ -440,6 +478,7 @@ def main():
     dec = bench_decode(args, dist, hbm_gbs, peak_kind)
 
     pre = bench_prefill(args, dist, hbm_gbs, bf16_tf, steps=args.prefill_steps, warmup=3)
+    pre_long = bench_prefill_long(args, dist, steps=5, warmup=3)
 
     cpu = None
     if dist.rank == 0 and dist.world == 1:
@@ -474,6 +513,7 @@ def main():
             "gpu_launches": dec["gpu_launches"],
             "clocks": dec["clocks"],
             "prefill": pre,
+            "prefill_long": pre_long,
         }
         print(json.dumps(line), flush=True)
     dist.close()
