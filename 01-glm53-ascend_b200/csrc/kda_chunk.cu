@@ -50,6 +50,8 @@
 #include "kda_common.cuh"
 
 #include <cuda.h>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 namespace kda {
@@ -354,6 +356,24 @@ struct Smem {
     static_assert(kAlloc <= 232448, "chunk kernel shared memory exceeds the 227 KiB per-CTA limit");
 };
 
+// Split path (long sequences, few (sequence, head) chains): the prep kernel
+// stores each chunk-head's scan operands as one record, in the shared-memory
+// layout the scan kernel reads, so every part is a single bulk copy.
+template <int D>
+struct Rec {
+    static constexpr int kW = 0;                       // bf16 hi/lo f64 tiles [64][D] (W)
+    static constexpr int kQG = kW + BT * D * 4;         // QG
+    static constexpr int kKD = kQG + BT * D * 4;        // KD
+    static constexpr int kTB = kKD + BT * D * 4;        // bf16 hi/lo [64][64] swizzled (TB)
+    static constexpr int kAQ = kTB + BT * BT * 4;       // Aqk
+    static constexpr int kEgl = kAQ + BT * BT * 4;      // fp32 [D] e^{gl}
+    static constexpr int kBytes = r1k(kEgl + D * 4);
+    // per (request, head): the tracked-prefix operand and e^{gtr}
+    static constexpr int tKR = 0;                       // bf16 hi/lo f64 [64][D]
+    static constexpr int tEtr = BT * D * 4;             // fp32 [D]
+    static constexpr int tBytes = r1k(tEtr + D * 4);
+};
+
 // Block pair index p -> (I, J), J <= I, in the order (0,0) (1,0) (1,1) (2,0) ...
 __device__ __forceinline__ void pair_ij(int p, int &I, int &J) {
     I = (p >= 6) ? 3 : (p >= 3) ? 2 : (p >= 1) ? 1 : 0;
@@ -418,9 +438,10 @@ __global__ void __launch_bounds__(1024) order_kernel(const KdaArgs p, int32_t *o
     }
 }
 
-template <int D, int MODE>
+template <int D, int MODE, bool PREP>
 __global__ void __launch_bounds__(kThreads + 32, 1)
-    chunk_kernel(const KdaArgs p, const int32_t *order, const __grid_constant__ TmaMaps maps) {
+    chunk_kernel(const KdaArgs p, const int32_t *order, const __grid_constant__ TmaMaps maps, uint8_t *rec,
+                 uint8_t *trec, const int32_t *cbase) {
     using L = Smem<D>;
     constexpr int KS = D / 16;              // k-steps over the key dim
     constexpr int ELEM = 4 * D;             // threads of the column-per-thread passes
@@ -467,9 +488,20 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t4 = lane & 3;
     const int H = p.num_heads;
-    const int rr = blockIdx.x / p.head_count;
     const int h = p.head_begin + blockIdx.x % p.head_count;
-    const int req = order != nullptr ? order[rr] : rr;
+    int req, cprep = 0;   // PREP: this CTA's request and chunk within it
+    if constexpr (PREP) {
+        // Chunk slot -> (request, chunk): cbase[r] = chunks of requests < r.
+        const int sl = blockIdx.x / p.head_count;
+        int r = 0;
+        while (r < p.num_req && cbase[r + 1] <= sl) ++r;
+        if (r >= p.num_req) return;   // past the batch's last chunk
+        req = r;
+        cprep = sl - cbase[r];
+    } else {
+        const int rr = blockIdx.x / p.head_count;
+        req = order != nullptr ? order[rr] : rr;
+    }
 
     const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
     const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
@@ -518,9 +550,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 #pragma unroll
         for (int blk = 0; blk < D / 64; ++blk) tma_load_3d(Vt + blk * 4096, &maps.v, 64 * blk, h, t0c, &bars[2]);
     };
-    auto issue_tiles = [&](int c, bool with_v) {
+    auto issue_tiles = [&](int c, bool with_v, bool expect_v = true) {
         const int t0c = static_cast<int>(bos + static_cast<int64_t>(c) * BT);
-        mbar_arrive_expect_tx(&bars[2], kTileBytes);
+        mbar_arrive_expect_tx(&bars[2], expect_v ? kTileBytes : kTileBytes - BT * D * 2);
         tma_load_3d(rawQ, &maps.q, 0, h, t0c, &bars[2]);
         tma_load_3d(rawK, &maps.k, 0, h, t0c, &bars[2]);
         tma_load_3d(rawG, &maps.g, 0, h, t0c, &bars[2]);
@@ -542,7 +574,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     // landed, 3 = o^T done, 4 = u product done (v tile free). sig: consumer ->
     // producer, 0 = TB/QG/S-split ready, 1 = W/KD ready, 2 = v' hi/lo ready.
     uint64_t *const sig = bars + 5;
-    if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+    if (!PREP && warp == 0) tmem_alloc(tmem_slot, kTmemCols);
     if (tid == 0) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
@@ -551,7 +583,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem = PREP ? 0u : *tmem_slot;
     // Tensor-memory slices: warp w reaches lanes [32 (w % 4), +32) (value
     // rows) and takes column slice w / 4 of every conversion.
     const int q4 = warp & 3, cs = warp >> 2;
@@ -559,7 +591,10 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q4) << 16);
     constexpr int SC = D / 4;                        // state columns per slice
 
-    if (warp == kThreads / 32) {
+    if (PREP && warp == kThreads / 32) {
+        // Prep: this CTA's one chunk of q, k and the gate (v is not needed).
+        if (lane == 0) issue_tiles(cprep, false, false);
+    } else if (warp == kThreads / 32) {
         // ===== producer warp: one thread issues every tensor-core product and
         // every TMA load, in the order the consumers' signals allow =====
         if (lane == 0 && nchunks > 0) {
@@ -693,7 +728,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 
         // Initial state S^T -> tensor memory (zero for slot 0 and the padding rows
         // of D = 64); a length-0 prefix checkpoint is the initial state.
-        {
+        if (!PREP) {
             const float *hs = p.state + slot * s0 + h * s1;
             float *ts = p.state + tslot * s0 + h * s1;
             const bool row_ok = srow < D;
@@ -708,18 +743,18 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tmem_st<SC>(tq + kColS + SC * cs, r);
             tmem_st_wait();
         }
-        if (nchunks > 0) load_beta(0);
+        if (nchunks > 0) load_beta(cprep);
 
         bool o_pending = false;   // the previous chunk's o^T waits in tensor memory
         int64_t o_t0 = 0;
         int o_n = 0;
-        for (int c = 0; c < nchunks; ++c) {
+        for (int c = cprep; c < (PREP ? cprep + 1 : nchunks); ++c) {
             const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
             const int n = chunk_rows(c);
             const int64_t rtrack = tlen - static_cast<int64_t>(c) * BT;
             const bool track_here = tslot > 0 && rtrack > 0 && rtrack <= BT;
-            const bool has_next = c + 1 < nchunks;
-            if (!mbar_wait(&bars[2], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
+            const bool has_next = !PREP && c + 1 < nchunks;
+            if (!mbar_wait(&bars[2], static_cast<uint32_t>(PREP ? 0 : c & 1), p.status) && tid == 0)
                 report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             if (tid == 0) bulk_wait_read();   // a tracked chunk's o tile has left the W region
             if (n < BT) {
@@ -854,7 +889,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             // update) still read QG, KD and Aqk in the Y, Z and Aqk tiles this
             // chunk rewrites: wait for them (bars[3] tracks all three) before the
             // tiles below; the factor tables above touch none of them.
-            if (c > 0) {
+            if (!PREP && c > 0) {
                 if (!mbar_wait(&bars[3], static_cast<uint32_t>((c - 1) & 1), p.status) && tid == 0)
                     report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
                 tc_fence_after();
@@ -1050,7 +1085,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     }
                     nbar(2, 128);
                 }
-            } else if (warp >= 8) {
+            } else if (!PREP && warp >= 8) {
                 // S^T -> bf16 hi/lo A operand and S^T <- S^T e^{gl} (deferred on a
                 // tracked chunk): two warps per lane quadrant, half the columns each.
                 if (c > 0) {
@@ -1118,7 +1153,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
             fence_async_smem();   // tiles written by threads -> read by the tensor core
             cbar();
-            if (tid == 0) mbar_arrive(&sig[0]);   // u = TB v may start
+            if (!PREP && tid == 0) mbar_arrive(&sig[0]);   // u = TB v may start
             if (has_next) load_beta(c + 1);
 
             // ---- P7 (warps 0..D/16-1): W = TB (kn e^{gc}), 16 key columns per warp ----
@@ -1215,6 +1250,29 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
             fence_async_smem();   // tiles written by threads -> read by the tensor core
             cbar();
+            if constexpr (PREP) {
+                // The chunk-head's scan operands -> its record (and the tracked
+                // prefix operand -> the request's), one bulk copy per part.
+                if (tid == 0) {
+                    using R = Rec<D>;
+                    const int hl = h - p.head_begin;
+                    uint8_t *rc = rec + (static_cast<int64_t>(cbase[req] + c) * p.head_count + hl) * R::kBytes;
+                    bulk_s2g(rc + R::kW, sm + L::kX, BT * D * 4);
+                    bulk_s2g(rc + R::kQG, sm + L::kY, BT * D * 4);
+                    bulk_s2g(rc + R::kKD, sm + L::kZ, BT * D * 4);
+                    bulk_s2g(rc + R::kTB, sm + L::kTBh, BT * BT * 4);
+                    bulk_s2g(rc + R::kAQ, sm + L::kAQh, BT * BT * 4);
+                    bulk_s2g(rc + R::kEgl, vec + L::vEgl, D * 4);
+                    if (track_here) {
+                        uint8_t *tr = trec + (static_cast<int64_t>(req) * p.head_count + hl) * R::tBytes;
+                        bulk_s2g(tr + R::tKR, sm + L::kRawQ, BT * D * 4);
+                        bulk_s2g(tr + R::tEtr, vec + L::vEtr, D * 4);
+                    }
+                    bulk_commit();
+                    bulk_wait_all();
+                }
+                continue;
+            }
             if (tid == 0) mbar_arrive(&sig[1]);   // W, QG, KD (and K_r) are in place: W S and QG S may start
 
             // ---- P9: the state scan: -v'^T (fp32) -> v'^T hi/lo A operand, 16 columns per warp ----
@@ -1275,7 +1333,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
             }   // chunk loop
 
-        if (nchunks > 0) {
+        if (!PREP && nchunks > 0) {
             const uint32_t lph = static_cast<uint32_t>((nchunks - 1) & 1);
             if (o_pending) {
                 if (!mbar_wait(&bars[3], lph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
@@ -1289,7 +1347,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tc_fence_after();
         }
         // Final state S^T -> pool slot (padding slot 0 is never written).
-        {
+        if (!PREP) {
             float *hs = p.state + slot * s0 + h * s1;
             uint32_t r[SC];
             tmem_ld<SC>(tq + kColS + SC * cs, r);
@@ -1303,10 +1361,426 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     }
     tc_fence_before();
     __syncthreads();
+    if (!PREP && warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Split path, part 2: the inter-chunk scan alone. One CTA per (sequence,
+// head). The producer thread streams each chunk's record (written by the
+// prep kernel) into the operand slots of shared memory as soon as the
+// previous chunk's product reading a slot has completed, and issues the five
+// tcgen05 products; the compute warps split the state, convert v', and store
+// the output. Per chunk the serial chain is: S split -> W S -> v' conversion
+// -> state update -> next S split.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(kThreads + 32, 1)
+    chunk_scan_kernel(const KdaArgs p, const int32_t *order, const __grid_constant__ TmaMaps maps,
+                      const uint8_t *rec, const uint8_t *trec, const int32_t *cbase) {
+    using L = Smem<D>;
+    using R = Rec<D>;
+    constexpr int KS = D / 16;
+    constexpr int SC = D / 4;                        // state columns per slice
+    extern __shared__ __align__(1024) unsigned char sm_raw[];
+    unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
+    uint16_t *const Vt = reinterpret_cast<uint16_t *>(sm + L::kV);
+    __nv_bfloat16 *const Ost = reinterpret_cast<__nv_bfloat16 *>(sm + L::kOst);
+    float *const vec = reinterpret_cast<float *>(sm + L::kVec);
+    uint64_t *const mb = reinterpret_cast<uint64_t *>(sm + L::kBar);
+    // product completions
+    uint64_t *const bG1 = mb + 0, *const bG2 = mb + 1, *const bG3a = mb + 2, *const bG4 = mb + 3, *const bO = mb + 4;
+    // operand-slot loads
+    uint64_t *const lTB = mb + 5, *const lEgl = mb + 6, *const lW = mb + 7, *const lQG = mb + 8, *const lKD = mb + 9,
+                    *const lAQ = mb + 10, *const lTR = mb + 11;
+    // compute warps -> producer
+    uint64_t *const sSplit = mb + 12, *const sConv = mb + 13, *const sOut = mb + 14;
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 120);
+    const uint32_t s_base = smem_addr(sm);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int H = p.num_heads;
+    const int rr = blockIdx.x / p.head_count;
+    const int hl = blockIdx.x % p.head_count, h = p.head_begin + hl;
+    const int req = order != nullptr ? order[rr] : rr;
+    const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
+    const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
+    const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
+    if (bos < 0 || eos < bos || eos > p.num_tokens) {
+        if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
+        return;
+    }
+    if (slot < 0 || slot >= p.num_slots) {
+        if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+        return;
+    }
+    int64_t tslot = 0, tlen = -1;
+    if (p.track_indices != nullptr) {
+        tslot = load_index(p.track_indices, p.index_bytes[2], req);
+        if (tslot < 0 || tslot >= p.num_slots) {
+            if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+            return;
+        }
+        if (tslot > 0) tlen = load_index(p.track_lens, p.index_bytes[3], req);
+    }
+    const int nchunks = static_cast<int>((eos - bos + BT - 1) / BT);
+    const int64_t s0 = p.state_stride[0], s1 = p.state_stride[1], sk = p.state_stride[2], sv = p.state_stride[3];
+    auto chunk_rows = [&](int c) {
+        const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
+        return static_cast<int>(eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT));
+    };
+    auto trk_at = [&](int c) {
+        const int64_t rt = tlen - static_cast<int64_t>(c) * BT;
+        return tslot > 0 && rt > 0 && rt <= BT;
+    };
+    auto rec_of = [&](int c) {
+        return rec + (static_cast<int64_t>(cbase[req] + c) * p.head_count + hl) * R::kBytes;
+    };
+    const uint8_t *trk_rec = trec + (static_cast<int64_t>(req) * p.head_count + hl) * R::tBytes;
+
+    if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+    if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < 15; ++i) mbar_init(&mb[i], 1);
+        fence_mbar_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int q4 = warp & 3, cs = warp >> 2;
+    const int srow = 32 * q4 + lane;
+    const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+
+    if (warp == kThreads / 32) {
+        // ===== producer =====
+        if (lane == 0 && nchunks > 0) {
+            constexpr uint32_t id_v = idesc_bf16(128, 64, true, false, true);      // -(v^T TB^T)
+            constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
+            constexpr uint32_t id_kd = idesc_bf16(128, D, false, true, false);
+            auto pwait = [&](uint64_t *b, uint32_t ph) {
+                if (!mbar_wait(b, ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            };
+            auto load = [&](uint64_t *bar, void *dst, const uint8_t *src, uint32_t bytes) {
+                mbar_arrive_expect_tx(bar, bytes);
+                bulk_g2s(dst, src, bytes, bar);
+            };
+            auto load_tb = [&](int c) {   // TB and the v tile (TMA, 128-byte swizzle)
+                mbar_arrive_expect_tx(lTB, BT * BT * 4 + BT * D * 2);
+                bulk_g2s(sm + L::kTBh, rec_of(c) + R::kTB, BT * BT * 4, lTB);
+                const int t0c = static_cast<int>(bos + static_cast<int64_t>(c) * BT);
+#pragma unroll
+                for (int blk = 0; blk < D / 64; ++blk) tma_load_3d(Vt + blk * 4096, &maps.v, 64 * blk, h, t0c, lTB);
+            };
+            auto load_tr = [&] {
+                mbar_arrive_expect_tx(lTR, BT * D * 4 + D * 4);
+                bulk_g2s(sm + L::kRawQ, trk_rec + R::tKR, BT * D * 4, lTR);
+                bulk_g2s(vec + L::vEtr, trk_rec + R::tEtr, D * 4, lTR);
+            };
+            load_tb(0);
+            load(lEgl, vec + L::vEgl, rec_of(0) + R::kEgl, D * 4);
+            load(lW, sm + L::kX, rec_of(0) + R::kW, BT * D * 4);
+            load(lQG, sm + L::kY, rec_of(0) + R::kQG, BT * D * 4);
+            load(lKD, sm + L::kZ, rec_of(0) + R::kKD, BT * D * 4);
+            load(lAQ, sm + L::kAQh, rec_of(0) + R::kAQ, BT * BT * 4);
+            if (trk_at(0)) load_tr();
+            uint32_t trph = 0;
+            for (int c = 0; c < nchunks; ++c) {
+                const uint32_t ph = static_cast<uint32_t>(c & 1);
+                const bool trk = trk_at(c), nxt = c + 1 < nchunks;
+                const int n = chunk_rows(c);
+                // u: NU = -u^T = -(TB v)^T. Rows of the v box past the sequence
+                // (the next sequence, or TMA's zero fill) are cleared first.
+                pwait(lTB, ph);
+                if (n < BT) {
+                    for (int e = n * (D / 8); e < BT * (D / 8); ++e)
+                        reinterpret_cast<uint4 *>(Vt)[((e / (D / 8)) * 8 + (e % 8)) + ((e % (D / 8)) / 8) * 512] =
+                            make_uint4(0u, 0u, 0u, 0u);
+                    fence_async_smem();
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t a = sdesc(s_base + L::kV + kk * 2048, 8192, 1024);
+                    umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBh + kk * 32, 16, 1024), id_v, kk > 0 ? 1u : 0u);
+                    umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBl + kk * 32, 16, 1024), id_v, 1u);
+                }
+                umma_commit(bG1);
+                // NU += (W S)^T -> -v'^T, once the state is split and W landed.
+                pwait(sSplit, ph);
+                pwait(lW, ph);
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+                    const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
+                    const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
+                    const uint64_t wh = sdesc(s_base + L::kX + off, 16, 1024);
+                    const uint64_t wl = sdesc(s_base + L::kX + BT * D * 2 + off, 16, 1024);
+                    umma_ts(tmem + kColNU, al, wh, id_n64, 1u);
+                    umma_ts(tmem + kColNU, ah, wl, id_n64, 1u);
+                    umma_ts(tmem + kColNU, ah, wh, id_n64, 1u);
+                }
+                umma_commit(bG2);
+                // e^{gl} of the next chunk once this one's last reader is done: the
+                // split, or on a tracked chunk the v' conversion.
+                if (nxt && !trk) load(lEgl, vec + L::vEgl, rec_of(c + 1) + R::kEgl, D * 4);
+                // o^T = (QG S)^T once the previous o tile has left tensor memory.
+                pwait(lQG, ph);
+                if (c > 0) pwait(sOut, static_cast<uint32_t>((c - 1) & 1));
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+                    const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
+                    const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
+                    const uint64_t qh = sdesc(s_base + L::kY + off, 16, 1024);
+                    const uint64_t ql = sdesc(s_base + L::kY + BT * D * 2 + off, 16, 1024);
+                    umma_ts(tmem + kColO, al, qh, id_n64, kk > 0 ? 1u : 0u);
+                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
+                }
+                umma_commit(bG3a);
+                // W and TB/v of the next chunk as soon as W S (and with it u,
+                // issued earlier) has completed: W is the first operand the next
+                // chunk's chain needs.
+                if (nxt) {
+                    pwait(bG2, ph);
+                    load(lW, sm + L::kX, rec_of(c + 1) + R::kW, BT * D * 4);
+                    load_tb(c + 1);
+                }
+                // S^T += v'^T KD (and the tracked prefix), o^T += v'^T Aqk^T.
+                pwait(sConv, ph);
+                if (nxt && trk) load(lEgl, vec + L::vEgl, rec_of(c + 1) + R::kEgl, D * 4);
+                pwait(lKD, ph);
+                pwait(lAQ, ph);
+                if (trk) pwait(lTR, trph);
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
+                    const uint64_t dh = sdesc(s_base + L::kZ + kk * 2048, 8192, 1024);
+                    const uint64_t dl = sdesc(s_base + L::kZ + BT * D * 2 + kk * 2048, 8192, 1024);
+                    umma_ts(tmem + kColS, al, dh, id_kd, 1u);
+                    umma_ts(tmem + kColS, ah, dl, id_kd, 1u);
+                    umma_ts(tmem + kColS, ah, dh, id_kd, 1u);
+                    if (trk) {
+                        const uint64_t rh = sdesc(s_base + L::kRawQ + kk * 2048, 8192, 1024);
+                        const uint64_t rl = sdesc(s_base + L::kRawK + kk * 2048, 8192, 1024);
+                        umma_ts(tmem + kColTR, al, rh, id_kd, 1u);
+                        umma_ts(tmem + kColTR, ah, rl, id_kd, 1u);
+                        umma_ts(tmem + kColTR, ah, rh, id_kd, 1u);
+                    }
+                }
+                umma_commit(bG4);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
+                    const uint64_t qh = sdesc(s_base + L::kAQh + kk * 32, 16, 1024);
+                    const uint64_t ql = sdesc(s_base + L::kAQl + kk * 32, 16, 1024);
+                    umma_ts(tmem + kColO, al, qh, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
+                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
+                }
+                umma_commit(bO);
+                if (trk) trph ^= 1u;
+                if (nxt) {
+                    pwait(bG3a, ph);
+                    load(lQG, sm + L::kY, rec_of(c + 1) + R::kQG, BT * D * 4);
+                    pwait(bG4, ph);
+                    load(lKD, sm + L::kZ, rec_of(c + 1) + R::kKD, BT * D * 4);
+                    if (trk_at(c + 1)) load_tr();
+                    pwait(bO, ph);
+                    load(lAQ, sm + L::kAQh, rec_of(c + 1) + R::kAQ, BT * BT * 4);
+                }
+            }
+        }
+    } else {
+        // ===== compute warps 0..15 =====
+        auto cbar = [] { nbar(1, kThreads); };
+        auto o_cols = [&](int64_t ot0, int on) {   // this warp's 16 output rows -> staging (or fp32 out)
+            uint32_t r[16];
+            tmem_ld16(tq + kColO + 16 * cs, r);
+            tmem_ld_wait();
+            if (srow < D) {
+                if (p.out_fp32) {
+                    float *o = static_cast<float *>(p.out) + (ot0 * H + h) * D + srow;
+                    const int64_t row_stride = static_cast<int64_t>(H) * D;
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        if (16 * cs + e < on) o[(16 * cs + e) * row_stride] = __uint_as_float(r[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        Ost[(16 * cs + e) * D + srow] = __float2bfloat16_rn(__uint_as_float(r[e]));
+                }
+            }
+        };
+        auto o_store = [&](int64_t ot0, int on) {   // issuing thread only
+            if (p.out_fp32) return;
+            if (on == BT) {
+                tma_store_3d(&maps.o, Ost, 0, h, static_cast<int>(ot0));
+            } else {
+                __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (ot0 * H + h) * D;
+                for (int rw = 0; rw < on; ++rw)
+                    bulk_s2g(o + static_cast<int64_t>(rw) * H * D, Ost + rw * D, D * 2);
+            }
+            bulk_commit();
+        };
+        // o tile of chunk c-1 -> out, once its last product completed.
+        auto o_out = [&](int cprev) {
+            if (!mbar_wait(bO, static_cast<uint32_t>(cprev & 1), p.status) && tid == 0)
+                report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+            if (tid == 0) bulk_wait_read();   // the previous tile has left the staging area
+            cbar();
+            o_cols(bos + static_cast<int64_t>(cprev) * BT, chunk_rows(cprev));
+            fence_async_smem();
+            tc_fence_before();
+            cbar();
+            if (tid == 0) o_store(bos + static_cast<int64_t>(cprev) * BT, chunk_rows(cprev));
+        };
+
+        // Initial state S^T -> tensor memory; a length-0 checkpoint is the initial state.
+        {
+            const float *hs = p.state + slot * s0 + h * s1;
+            float *ts = p.state + tslot * s0 + h * s1;
+            const bool row_ok = srow < D;
+            uint32_t r[SC];
+#pragma unroll
+            for (int e = 0; e < SC; ++e) {
+                const int k = SC * cs + e;
+                const float x = (slot > 0 && row_ok) ? hs[srow * sv + k * sk] : 0.f;
+                r[e] = __float_as_uint(x);
+                if (row_ok && tslot > 0 && tlen == 0) ts[srow * sv + k * sk] = x;
+            }
+            tmem_st<SC>(tq + kColS + SC * cs, r);
+            tmem_st_wait();
+        }
+        uint32_t trph = 0;
+        for (int c = 0; c < nchunks; ++c) {
+            const uint32_t ph = static_cast<uint32_t>(c & 1);
+            const bool trk = trk_at(c);
+            // S^T -> bf16 hi/lo A operand; S^T <- S^T e^{gl} (deferred on a tracked chunk).
+            if (c > 0) {
+                if (!mbar_wait(bG4, static_cast<uint32_t>((c - 1) & 1), p.status) && tid == 0)
+                    report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            }
+            if (!mbar_wait(lEgl, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+            {
+                uint32_t r[SC], hi[SC / 2], lo[SC / 2];
+                tmem_ld<SC>(tq + kColS + SC * cs, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < SC / 2; ++e)
+                    split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+                tmem_st<SC / 2>(tq + kColSH + (SC / 2) * cs, hi);
+                tmem_st<SC / 2>(tq + kColSL + (SC / 2) * cs, lo);
+                if (!trk) {
+                    const float *eg = vec + L::vEgl + SC * cs;
+#pragma unroll
+                    for (int e = 0; e < SC; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * eg[e]);
+                    tmem_st<SC>(tq + kColS + SC * cs, r);
+                }
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            cbar();
+            if (tid == 0) mbar_arrive(sSplit);
+            // The previous chunk's o tile, while W S runs.
+            if (c > 0) {
+                o_out(c - 1);
+                if (tid == 0) mbar_arrive(sOut);
+            }
+            // -v'^T (fp32) -> v'^T hi/lo A operand.
+            if (!mbar_wait(bG2, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+            {
+                uint32_t r[16], hi[8], lo[8];
+                tmem_ld16(tq + kColNU + 16 * cs, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    split2(-__uint_as_float(r[2 * e]), -__uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+                tmem_st8(tq + kColVH + 8 * cs, hi);
+                tmem_st8(tq + kColVL + 8 * cs, lo);
+            }
+            if (trk) {
+                // S^T e^{gc_{r-1}} into the S hi/lo columns once o = QG S has
+                // read them, then the deferred S^T e^{gl}.
+                if (!mbar_wait(bG3a, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                if (!mbar_wait(lTR, trph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                tc_fence_after();
+                uint32_t r[SC], t[SC];
+                tmem_ld<SC>(tq + kColS + SC * cs, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < SC; ++e) {
+                    t[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEtr + SC * cs + e]);
+                    r[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEgl + SC * cs + e]);
+                }
+                tmem_st<SC>(tq + kColTR + SC * cs, t);
+                tmem_st<SC>(tq + kColS + SC * cs, r);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            cbar();
+            if (tid == 0) mbar_arrive(sConv);
+            if (trk) {
+                // The checkpoint leaves tensor memory before the next split reuses its columns.
+                if (!mbar_wait(bG4, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                tc_fence_after();
+                float *ts = p.state + tslot * s0 + h * s1;
+                uint32_t r[SC];
+                tmem_ld<SC>(tq + kColTR + SC * cs, r);
+                tmem_ld_wait();
+                if (srow < D) {
+#pragma unroll
+                    for (int e = 0; e < SC; ++e) ts[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
+                }
+                trph ^= 1u;
+            }
+        }
+        if (nchunks > 0) {
+            o_out(nchunks - 1);
+            if (!mbar_wait(bG4, static_cast<uint32_t>((nchunks - 1) & 1), p.status) && tid == 0)
+                report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+        }
+        // Final state S^T -> pool slot (padding slot 0 is never written).
+        {
+            float *hs = p.state + slot * s0 + h * s1;
+            uint32_t r[SC];
+            tmem_ld<SC>(tq + kColS + SC * cs, r);
+            tmem_ld_wait();
+            if (slot > 0 && srow < D) {
+#pragma unroll
+                for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
+            }
+        }
+        if (tid == 0) bulk_wait_all();
+    }
+    tc_fence_before();
+    __syncthreads();
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+}
+
+// Chunk slot offsets of the split path: cbase[r] = chunks of requests < r
+// (num_req + 1 entries). One thread; the split path serves few requests.
+__global__ void chunk_base_kernel(const KdaArgs p, int32_t *cbase) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    int32_t acc = 0;
+    for (int r = 0; r < p.num_req; ++r) {
+        cbase[r] = acc;
+        const int64_t len = load_index(p.cu_seqlens, p.index_bytes[1], r + 1) -
+                            load_index(p.cu_seqlens, p.index_bytes[1], r);
+        acc += static_cast<int32_t>(len > 0 ? (len + BT - 1) / BT : 0);
+    }
+    cbase[p.num_req] = acc;
 }
 
 }  // namespace chunk
@@ -1355,34 +1829,114 @@ static bool encode_rows(CUtensorMap *map, const void *base, CUtensorMapDataType 
               swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static bool encode_maps(chunk::TmaMaps &maps, const KdaArgs *a, int D, bool raw) {
+    const int H = a->num_heads;
+    const int64_t T = a->num_tokens;
+    return encode_rows(&maps.q, a->q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           encode_rows(&maps.k, a->k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           encode_rows(&maps.g, raw ? a->a : a->g,
+                       raw ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, raw ? 2 : 4, D, H,
+                       T, D, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           encode_rows(&maps.v, a->v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, 64, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_rows(&maps.o, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Opt a kernel into the chunk kernels' dynamic shared memory once per device.
+template <typename K>
+static bool opt_in(K kernel, bool (&done)[64], int bytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    dev = (dev >= 0 && dev < 64) ? dev : 0;
+    if (!done[dev]) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+            return false;
+        done[dev] = true;
+    }
+    return true;
+}
+
 template <int D, int MODE>
 static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
     using L = chunk::Smem<D>;
     chunk::TmaMaps maps;
-    const int H = a->num_heads;
-    const int64_t T = a->num_tokens;
-    const bool raw = MODE == KDA_GATE_RAW;
-    if (!encode_rows(&maps.q, a->q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_rows(&maps.k, a->k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_rows(&maps.g, raw ? a->a : a->g,
-                     raw ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, raw ? 2 : 4, D, H, T,
-                     D, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_rows(&maps.v, a->v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_rows(&maps.o, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, H, T, D, CU_TENSOR_MAP_SWIZZLE_NONE))
-        return KDA_ERR_LAUNCH;
+    if (!encode_maps(maps, a, D, MODE == KDA_GATE_RAW)) return KDA_ERR_LAUNCH;
     static bool opted[64];
+    if (!opt_in(chunk::chunk_kernel<D, MODE, false>, opted, L::kAlloc)) return KDA_ERR_LAUNCH;
+    if (order != nullptr) chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
+    const int64_t grid = static_cast<int64_t>(a->num_req) * a->head_count;
+    chunk::chunk_kernel<D, MODE, false><<<static_cast<unsigned>(grid), chunk::kThreads + 32, L::kAlloc, st>>>(
+        *a, order, maps, nullptr, nullptr, nullptr);
+    return KDA_OK;
+}
+
+// ---- Split path: which batches use it, and its workspace ----
+//
+// The fused kernel runs one CTA per (sequence, head) chain through every
+// phase of every chunk; that fills the GPU when there are many chains. With
+// few chains (a long context over a few heads) most SMs would idle, so the
+// split path first computes every chunk's intra-chunk operands with one CTA
+// per (chunk, head) on all SMs, then runs only the serial scan per chain.
+// KDA_CHUNK_PATH=fused|split overrides the choice.
+
+static int sm_count() {
+    static int count[64];
     int dev = 0;
     cudaGetDevice(&dev);
     dev = (dev >= 0 && dev < 64) ? dev : 0;
-    if (!opted[dev]) {
-        if (cudaFuncSetAttribute(chunk::chunk_kernel<D, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 L::kAlloc) != cudaSuccess)
-            return KDA_ERR_LAUNCH;
-        opted[dev] = true;
+    if (count[dev] == 0) {
+        int c = 0;
+        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+        count[dev] = c > 0 ? c : 1;
     }
-    if (order != nullptr) chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
-    const int64_t grid = static_cast<int64_t>(a->num_req) * a->head_count;
-    chunk::chunk_kernel<D, MODE><<<static_cast<unsigned>(grid), chunk::kThreads + 32, L::kAlloc, st>>>(*a, order, maps);
+    return count[dev];
+}
+
+static bool want_split(int32_t num_req, int32_t heads, int32_t num_tokens) {
+    const char *env = getenv("KDA_CHUNK_PATH");
+    if (env != nullptr && strcmp(env, "fused") == 0) return false;
+    if (env != nullptr && strcmp(env, "split") == 0) return num_req > 0 && num_req <= 1024;
+    const int64_t chains = static_cast<int64_t>(num_req) * heads;
+    return num_req > 0 && num_req <= 1024 && chains * 2 <= sm_count() &&
+           static_cast<int64_t>(num_tokens) >= static_cast<int64_t>(num_req) * chunk::BT * 8;
+}
+
+static size_t a256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct SplitLayout {
+    size_t cbase, rec, trec, total;
+};
+static SplitLayout split_layout(int32_t num_req, int32_t num_tokens, int32_t heads, int32_t D) {
+    const size_t slots = static_cast<size_t>(num_tokens) / chunk::BT + static_cast<size_t>(num_req);
+    const size_t rb = D == 64 ? chunk::Rec<64>::kBytes : chunk::Rec<128>::kBytes;
+    const size_t tb = D == 64 ? chunk::Rec<64>::tBytes : chunk::Rec<128>::tBytes;
+    SplitLayout l;
+    l.cbase = order_bytes(num_req);
+    l.rec = l.cbase + a256((static_cast<size_t>(num_req) + 1) * sizeof(int32_t));
+    l.trec = l.rec + slots * static_cast<size_t>(heads) * rb;
+    l.total = l.trec + static_cast<size_t>(num_req) * static_cast<size_t>(heads) * tb;
+    return l;
+}
+
+template <int D, int MODE>
+static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
+    using L = chunk::Smem<D>;
+    chunk::TmaMaps maps;
+    if (!encode_maps(maps, a, D, MODE == KDA_GATE_RAW)) return KDA_ERR_LAUNCH;
+    static bool opted_prep[64], opted_scan[64];
+    if (!opt_in(chunk::chunk_kernel<D, MODE, true>, opted_prep, L::kAlloc) ||
+        !opt_in(chunk::chunk_scan_kernel<D>, opted_scan, L::kAlloc))
+        return KDA_ERR_LAUNCH;
+    const SplitLayout lay = split_layout(a->num_req, a->num_tokens, a->head_count, D);
+    int32_t *order = reinterpret_cast<int32_t *>(ws);
+    int32_t *cbase = reinterpret_cast<int32_t *>(ws + lay.cbase);
+    uint8_t *rec = ws + lay.rec, *trec = ws + lay.trec;
+    chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
+    chunk::chunk_base_kernel<<<1, 32, 0, st>>>(*a, cbase);
+    const int64_t slots = static_cast<int64_t>(a->num_tokens) / chunk::BT + a->num_req;
+    chunk::chunk_kernel<D, MODE, true><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads + 32,
+                                         L::kAlloc, st>>>(*a, nullptr, maps, rec, trec, cbase);
+    chunk::chunk_scan_kernel<D><<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count),
+                                  chunk::kThreads + 32, L::kAlloc, st>>>(*a, order, maps, rec, trec, cbase);
     return KDA_OK;
 }
 
@@ -1390,10 +1944,11 @@ static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
 
 extern "C" size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens, int32_t num_heads,
                                             int32_t head_dim) {
-    (void)num_tokens;
-    (void)num_heads;
-    (void)head_dim;
-    return (num_req > 0 && num_req <= 1024) ? kda::order_bytes(num_req) : 0;
+    if (num_req <= 0) return 0;
+    if ((head_dim == 64 || head_dim == 128) && num_tokens >= 0 && num_heads > 0 &&
+        kda::want_split(num_req, num_heads, num_tokens))
+        return kda::split_layout(num_req, num_tokens, num_heads, head_dim).total;
+    return num_req <= 1024 ? kda::order_bytes(num_req) : 0;
 }
 
 extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream) {
@@ -1421,15 +1976,32 @@ extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t wor
     const void *rows[] = {args->q, args->k, args->v, args->gate_mode == KDA_GATE_RAW ? args->a : args->g, args->out};
     for (const void *ptr : rows)
         if (!kda::chunk_aligned16(ptr)) return KDA_ERR_ALIGNMENT;
-    const size_t need = kda_chunk_workspace_bytes(args->num_req, args->num_tokens, args->num_heads, args->head_dim);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc;
+    // The split path runs when it pays off and the workspace holds its records;
+    // otherwise the fused kernel, which needs only the request order.
+    const bool split = kda::want_split(args->num_req, args->head_count, args->num_tokens) && workspace != nullptr &&
+                       (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
+                       workspace_bytes >=
+                           kda::split_layout(args->num_req, args->num_tokens, args->head_count, args->head_dim).total;
+    if (split) {
+        uint8_t *ws = static_cast<uint8_t *>(workspace);
+        if (args->head_dim == 128)
+            rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk_split<128, KDA_GATE_RAW>(args, ws, st)
+                                                 : kda::launch_chunk_split<128, KDA_GATE_LOG>(args, ws, st);
+        else
+            rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk_split<64, KDA_GATE_RAW>(args, ws, st)
+                                                 : kda::launch_chunk_split<64, KDA_GATE_LOG>(args, ws, st);
+        if (rc != KDA_OK) return rc;
+        return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+    }
+    const size_t need = args->num_req <= 1024 ? kda::order_bytes(args->num_req) : 0;
     int32_t *order = nullptr;
     if (need > 0) {
         if (workspace == nullptr || workspace_bytes < need) return KDA_ERR_WORKSPACE;
         if ((reinterpret_cast<uintptr_t>(workspace) & 3u) != 0) return KDA_ERR_ALIGNMENT;
         order = static_cast<int32_t *>(workspace);
     }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    int rc;
     if (args->head_dim == 128)
         rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk<128, KDA_GATE_RAW>(args, order, st)
                                              : kda::launch_chunk<128, KDA_GATE_LOG>(args, order, st);
