@@ -5,8 +5,14 @@ chunks and sequences, the zero slot, tracked checkpoints before, inside, on the
 boundary of and at the end of a chunk; untouched slots) and adds what the B200
 op supports beyond it: lengths that are not multiples of 64, any head count,
 K = V = 64, the log-gate entry point, BASELINE config 3 at full size, int64
-metadata and CUDA-graph replay. Tolerances: tests/kda_checks.py.
+metadata and CUDA-graph replay. Every test runs twice: with the library's own
+choice between the fused kernel and the split path (prep + scan kernels), and
+with the split path forced (KDA_CHUNK_PATH=split), so both are covered.
+BASELINE config 4 (one 131,072-token sequence) runs on the split path at full
+size. Tolerances: tests/kda_checks.py.
 """
+
+import os
 
 import pytest
 import torch
@@ -24,6 +30,17 @@ SLOTS = 8
 def ops():
     from sgl_glm53_ascend_ops import ops as _ops
     return _ops
+
+
+@pytest.fixture(autouse=True, params=["auto", "split"])
+def chunk_path(request, monkeypatch):
+    """Selects the chunk prefill path through the variable the library reads
+    on every launch; "auto" leaves the library's own choice."""
+    if request.param == "auto":
+        monkeypatch.delenv("KDA_CHUNK_PATH", raising=False)
+    else:
+        monkeypatch.setenv("KDA_CHUNK_PATH", request.param)
+    return request.param
 
 
 def _dev(kw):
@@ -235,3 +252,36 @@ def test_chunk_cuda_graph_replay(ops):
         assert torch.equal(d["initial_state_source"], ref_pool)
         assert torch.equal(captured, expected)
     del graph
+
+
+def test_cfg4_long_context(ops, chunk_path):
+    """one 131,072-token sequence (2048 chunks), here 4 heads
+    with an fp32 initial state. Head 0 is checked against the oracle's token
+    recurrence over the whole sequence; the fused kernel and the split path
+    agree; the run is deterministic."""
+    if chunk_path != "auto":
+        pytest.skip("config 4 already takes the split path by itself")
+    from sgl_glm53_ascend_ops import workloads
+    w = workloads.config4(seed=4, heads=4)
+    d = w.to(DEV)
+    pool0 = clone_pool(d.pool)
+    out = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
+    pool_split = clone_pool(d.pool)
+    d.pool.copy_(pool0)
+    out_b = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out_b) and torch.equal(pool_split, d.pool), "not deterministic"
+    os.environ["KDA_CHUNK_PATH"] = "fused"
+    try:
+        d.pool.copy_(pool0)
+        out_f = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
+        torch.cuda.synchronize()
+    finally:
+        del os.environ["KDA_CHUNK_PATH"]
+    assert_out_close(out_f.cpu(), out.cpu())          # both bf16: one-ulp credit
+    assert_state_close(d.pool.cpu()[1:], pool_split.cpu()[1:])
+    sub = w.head_shard(0, 4)                          # head 0
+    ref_pool = clone_pool(sub.pool)
+    ref = kda_ref.kda_varlen_recurrent_g(**dict(sub.kwargs(), initial_state_source=ref_pool), out_fp32=True)
+    assert_out_close(out[:, :, 0:1].cpu(), ref)
+    assert_state_close(pool_split[1:, 0:1].cpu(), ref_pool[1:])
