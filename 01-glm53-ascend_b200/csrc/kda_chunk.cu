@@ -364,8 +364,11 @@ struct Rec {
     static constexpr int kW = 0;                       // bf16 hi/lo f64 tiles [64][D] (W)
     static constexpr int kQG = kW + BT * D * 4;         // QG
     static constexpr int kKD = kQG + BT * D * 4;        // KD
-    static constexpr int kTB = kKD + BT * D * 4;        // bf16 hi/lo [64][64] swizzled (TB)
-    static constexpr int kAQ = kTB + BT * BT * 4;       // Aqk
+    // -u^T = -(TB v)^T, fp32, float (t, v) at ((t / 4) * D + v) * 4 + t % 4: a
+    // compute warp reads its 16 tokens of value row v as four 16-byte pieces,
+    // eight consecutive rows per 128 bytes.
+    static constexpr int kU = kKD + BT * D * 4;
+    static constexpr int kAQ = kU + BT * D * 4;         // Aqk (bf16 hi/lo [64][64] swizzled)
     static constexpr int kEgl = kAQ + BT * BT * 4;      // fp32 [D] e^{gl}
     static constexpr int kBytes = r1k(kEgl + D * 4);
     // per (request, head): the tracked-prefix operand and e^{gtr}
@@ -592,8 +595,8 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     constexpr int SC = D / 4;                        // state columns per slice
 
     if (PREP && warp == kThreads / 32) {
-        // Prep: this CTA's one chunk of q, k and the gate (v is not needed).
-        if (lane == 0) issue_tiles(cprep, false, false);
+        // Prep: this CTA's one chunk of q, k, the gate and v.
+        if (lane == 0) issue_tiles(cprep, true);
     } else if (warp == kThreads / 32) {
         // ===== producer warp: one thread issues every tensor-core product and
         // every TMA load, in the order the consumers' signals allow =====
@@ -1202,6 +1205,40 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                             *reinterpret_cast<uint32_t *>(Wh + f64(j, kcol)) = hi;
                             *reinterpret_cast<uint32_t *>(Wl + f64(j, kcol)) = lo;
                         }
+                if constexpr (PREP) {
+                    // u = TB v for value columns [16w, 16w + 16) (v is exact in bf16:
+                    // two products), stored negated in the record's layout in the
+                    // gate region (consumed in P2).
+                    float uacc[4][2][4] = {};
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) {
+                        uint32_t vb[4];
+                        ldsm_x4_t(vb, s_base + L::kV +
+                                          2 * f64(16 * ks + (lane & 7) + (((lane >> 3) & 1) << 3),
+                                                  16 * warp + ((lane >> 4) << 3)));
+#pragma unroll
+                        for (int mt = ks; mt < 4; ++mt) {
+                            uint32_t ah[4], al[4];
+                            ldsm_x4(ah, s_base + L::kTBh + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
+                            ldsm_x4(al, s_base + L::kTBl + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
+                            mma16816(uacc[mt][0], al, vb[0], vb[1]);
+                            mma16816(uacc[mt][0], ah, vb[0], vb[1]);
+                            mma16816(uacc[mt][1], al, vb[2], vb[3]);
+                            mma16816(uacc[mt][1], ah, vb[2], vb[3]);
+                        }
+                    }
+                    float *ust = reinterpret_cast<float *>(sm + L::kRawG);
+#pragma unroll
+                    for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                            for (int hf = 0; hf < 2; ++hf) {
+                                const int t = 16 * mt + g + 8 * hf, v0 = 16 * warp + 8 * nt + 2 * t4;
+                                ust[((t >> 2) * D + v0) * 4 + (t & 3)] = -uacc[mt][nt][2 * hf];
+                                ust[((t >> 2) * D + v0 + 1) * 4 + (t & 3)] = -uacc[mt][nt][2 * hf + 1];
+                            }
+                }
             // ---- P8: QG = Y e^{m_I} (exact), KD = Z e^{gl - m_J}, tracked K_r; in place ----
             } else {
                 for (int j = tid - 32 * NW7; j < BT * D / 8; j += kThreads - 32 * NW7) {
@@ -1260,7 +1297,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     bulk_s2g(rc + R::kW, sm + L::kX, BT * D * 4);
                     bulk_s2g(rc + R::kQG, sm + L::kY, BT * D * 4);
                     bulk_s2g(rc + R::kKD, sm + L::kZ, BT * D * 4);
-                    bulk_s2g(rc + R::kTB, sm + L::kTBh, BT * BT * 4);
+                    bulk_s2g(rc + R::kU, sm + L::kRawG, BT * D * 4);
                     bulk_s2g(rc + R::kAQ, sm + L::kAQh, BT * BT * 4);
                     bulk_s2g(rc + R::kEgl, vec + L::vEgl, D * 4);
                     if (track_here) {
@@ -1386,14 +1423,14 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     constexpr int SC = D / 4;                        // state columns per slice
     extern __shared__ __align__(1024) unsigned char sm_raw[];
     unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
-    uint16_t *const Vt = reinterpret_cast<uint16_t *>(sm + L::kV);
-    __nv_bfloat16 *const Ost = reinterpret_cast<__nv_bfloat16 *>(sm + L::kOst);
+    const float *const Us = reinterpret_cast<const float *>(sm + L::kRawG);          // -u^T slot (record layout)
+    __nv_bfloat16 *const Ost = reinterpret_cast<__nv_bfloat16 *>(sm + L::kV);      // o tile staging
     float *const vec = reinterpret_cast<float *>(sm + L::kVec);
     uint64_t *const mb = reinterpret_cast<uint64_t *>(sm + L::kBar);
     // product completions
-    uint64_t *const bG1 = mb + 0, *const bG2 = mb + 1, *const bG3a = mb + 2, *const bG4 = mb + 3, *const bO = mb + 4;
+    uint64_t *const bG2 = mb + 1, *const bG3a = mb + 2, *const bG4 = mb + 3, *const bO = mb + 4;
     // operand-slot loads
-    uint64_t *const lTB = mb + 5, *const lEgl = mb + 6, *const lW = mb + 7, *const lQG = mb + 8, *const lKD = mb + 9,
+    uint64_t *const lU = mb + 5, *const lEgl = mb + 6, *const lW = mb + 7, *const lQG = mb + 8, *const lKD = mb + 9,
                     *const lAQ = mb + 10, *const lTR = mb + 11;
     // compute warps -> producer
     uint64_t *const sSplit = mb + 12, *const sConv = mb + 13, *const sOut = mb + 14;
@@ -1457,7 +1494,6 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     if (warp == kThreads / 32) {
         // ===== producer =====
         if (lane == 0 && nchunks > 0) {
-            constexpr uint32_t id_v = idesc_bf16(128, 64, true, false, true);      // -(v^T TB^T)
             constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
             constexpr uint32_t id_kd = idesc_bf16(128, D, false, true, false);
             auto pwait = [&](uint64_t *b, uint32_t ph) {
@@ -1467,19 +1503,12 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 mbar_arrive_expect_tx(bar, bytes);
                 bulk_g2s(dst, src, bytes, bar);
             };
-            auto load_tb = [&](int c) {   // TB and the v tile (TMA, 128-byte swizzle)
-                mbar_arrive_expect_tx(lTB, BT * BT * 4 + BT * D * 2);
-                bulk_g2s(sm + L::kTBh, rec_of(c) + R::kTB, BT * BT * 4, lTB);
-                const int t0c = static_cast<int>(bos + static_cast<int64_t>(c) * BT);
-#pragma unroll
-                for (int blk = 0; blk < D / 64; ++blk) tma_load_3d(Vt + blk * 4096, &maps.v, 64 * blk, h, t0c, lTB);
-            };
             auto load_tr = [&] {
                 mbar_arrive_expect_tx(lTR, BT * D * 4 + D * 4);
                 bulk_g2s(sm + L::kRawQ, trk_rec + R::tKR, BT * D * 4, lTR);
                 bulk_g2s(vec + L::vEtr, trk_rec + R::tEtr, D * 4, lTR);
             };
-            load_tb(0);
+            load(lU, sm + L::kRawG, rec_of(0) + R::kU, BT * D * 4);
             load(lEgl, vec + L::vEgl, rec_of(0) + R::kEgl, D * 4);
             load(lW, sm + L::kX, rec_of(0) + R::kW, BT * D * 4);
             load(lQG, sm + L::kY, rec_of(0) + R::kQG, BT * D * 4);
@@ -1490,26 +1519,10 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             for (int c = 0; c < nchunks; ++c) {
                 const uint32_t ph = static_cast<uint32_t>(c & 1);
                 const bool trk = trk_at(c), nxt = c + 1 < nchunks;
-                const int n = chunk_rows(c);
-                // u: NU = -u^T = -(TB v)^T. Rows of the v box past the sequence
-                // (the next sequence, or TMA's zero fill) are cleared first.
-                pwait(lTB, ph);
-                if (n < BT) {
-                    for (int e = n * (D / 8); e < BT * (D / 8); ++e)
-                        reinterpret_cast<uint4 *>(Vt)[((e / (D / 8)) * 8 + (e % 8)) + ((e % (D / 8)) / 8) * 512] =
-                            make_uint4(0u, 0u, 0u, 0u);
-                    fence_async_smem();
-                }
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t a = sdesc(s_base + L::kV + kk * 2048, 8192, 1024);
-                    umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBh + kk * 32, 16, 1024), id_v, kk > 0 ? 1u : 0u);
-                    umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBl + kk * 32, 16, 1024), id_v, 1u);
-                }
-                umma_commit(bG1);
-                // NU += (W S)^T -> -v'^T, once the state is split and W landed.
+                // NU (= -u^T, set by the compute warps with the split) += (W S)^T
+                // -> -v'^T, once the state is split and W landed.
                 pwait(sSplit, ph);
+                if (nxt) load(lU, sm + L::kRawG, rec_of(c + 1) + R::kU, BT * D * 4);   // -u^T was copied
                 pwait(lW, ph);
                 tc_fence_after();
 #pragma unroll
@@ -1541,13 +1554,11 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
                 }
                 umma_commit(bG3a);
-                // W and TB/v of the next chunk as soon as W S (and with it u,
-                // issued earlier) has completed: W is the first operand the next
-                // chunk's chain needs.
+                // W of the next chunk as soon as W S has completed: it is the first
+                // operand the next chunk's chain needs.
                 if (nxt) {
                     pwait(bG2, ph);
                     load(lW, sm + L::kX, rec_of(c + 1) + R::kW, BT * D * 4);
-                    load_tb(c + 1);
                 }
                 // S^T += v'^T KD (and the tracked prefix), o^T += v'^T Aqk^T.
                 pwait(sConv, ph);
@@ -1667,7 +1678,22 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             }
             if (!mbar_wait(lEgl, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (!mbar_wait(lU, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
+            {
+                // NU <- -u^T (this warp's 16 token columns of value row srow).
+                uint32_t r[16];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 u4 = srow < D ? *reinterpret_cast<const float4 *>(Us + ((4 * cs + k) * D + srow) * 4)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                    r[4 * k] = __float_as_uint(u4.x);
+                    r[4 * k + 1] = __float_as_uint(u4.y);
+                    r[4 * k + 2] = __float_as_uint(u4.z);
+                    r[4 * k + 3] = __float_as_uint(u4.w);
+                }
+                tmem_st16(tq + kColNU + 16 * cs, r);
+            }
             {
                 uint32_t r[SC], hi[SC / 2], lo[SC / 2];
                 tmem_ld<SC>(tq + kColS + SC * cs, r);
@@ -1687,7 +1713,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tmem_st_wait();
             tc_fence_before();
             cbar();
-            if (tid == 0) mbar_arrive(sSplit);
+            if (tid == 0) mbar_arrive(sSplit);   // S split, NU = -u^T, e^{gl} and -u^T slots read
             // The previous chunk's o tile, while W S runs.
             if (c > 0) {
                 o_out(c - 1);
