@@ -16,6 +16,7 @@ namespace kda {
 
 constexpr float kNormEps = 1e-6f;   // inside the sqrt, kda_python.py:28-29
 constexpr uint32_t kMaxWaitPolls = 1u << 22;
+constexpr uint32_t kWaitSuspendNs = 1000;   // per poll; bounds a wait at ~4 s
 
 __device__ __forceinline__ float bf16_lo(uint32_t x) { return __uint_as_float(x << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
@@ -80,12 +81,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int32_t
     const uint32_t addr = smem_addr(bar);
     for (uint32_t i = 0; i < kMaxWaitPolls; ++i) {
         uint32_t done;
+        // The suspend-time hint lets a waiting warp sleep instead of spinning,
+        // leaving issue slots to the warps that do the work.
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
             "selp.u32 %0, 1, 0, p;\n\t}"
             : "=r"(done)
-            : "r"(addr), "r"(phase)
+            : "r"(addr), "r"(phase), "r"(kWaitSuspendNs)
             : "memory");
         if (done) return true;
     }
