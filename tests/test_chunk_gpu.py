@@ -285,3 +285,24 @@ def test_cfg4_long_context(ops, chunk_path):
     ref = kda_ref.kda_varlen_recurrent_g(**dict(sub.kwargs(), initial_state_source=ref_pool), out_fp32=True)
     assert_out_close(out[:, :, 0:1].cpu(), ref)
     assert_state_close(pool_split[1:, 0:1].cpu(), ref_pool[1:])
+
+
+def test_cfg5_mixed_batch(ops):
+    """BASELINE config 5 in one chunk-op call: 64 one-token requests and 4
+    resumed 2048-token prefills (68 distinct slots of a 1024-slot pool, nonzero
+    states), H=32. Outputs and the 68 updated slots against the oracle; the
+    955 other slots bit-equal."""
+    from sgl_glm53_ascend_ops import workloads
+    w = workloads.config5()
+    before = clone_pool(w.pool)
+    d = w.to(DEV)
+    out = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
+    torch.cuda.synchronize()
+    got = d.pool.cpu()
+    del d
+    ref_pool = clone_pool(w.pool)
+    ref = kda_ref.kda_varlen_recurrent_g(**dict(w.kwargs(), initial_state_source=ref_pool), out_fp32=True)
+    assert_out_close(out.cpu(), ref)
+    touched = [int(s) for s in w.indices]
+    assert_state_close(got[touched], ref_pool[touched])
+    assert_untouched(got, before, touched)

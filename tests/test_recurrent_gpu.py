@@ -198,6 +198,26 @@ def test_cfg2_decode_full_size(ops):
 # Through the C ABI: fp32 verification output, bit-equal to the torch op
 # ---------------------------------------------------------------------------
 
+def test_cfg5_mixed_batch_recurrent(ops):
+    """BASELINE config 5 through the recurrent op in its prefill regime (the
+    whole mixed batch of 64 one-token and 4 resumed 2048-token requests in one
+    call): outputs and updated slots against the oracle, other slots bit-equal."""
+    from sgl_glm53_ascend_ops import workloads
+    w = workloads.config5(seed=1)
+    before = clone_pool(w.pool)
+    d = w.to(DEV)
+    out = ops.kda_varlen_recurrent_g(**d.kwargs(), prefill=True)
+    torch.cuda.synchronize()
+    got = d.pool.cpu()
+    del d
+    ref_pool = clone_pool(w.pool)
+    ref = kda_ref.kda_varlen_recurrent_g(**dict(w.kwargs(), initial_state_source=ref_pool), out_fp32=True)
+    assert_out_close(out.cpu(), ref)
+    touched = [int(s) for s in w.indices]
+    assert_state_close(got[touched], ref_pool[touched])
+    assert_untouched(got, before, touched)
+
+
 def test_abi_fp32_output_meets_bar(abi):
     from sgl_glm53_ascend_ops import workloads
     w = workloads.config2(requests=64, heads=8, slots=80)
