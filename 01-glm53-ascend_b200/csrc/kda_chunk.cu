@@ -377,6 +377,22 @@ struct Rec {
     static constexpr int tBytes = r1k(tEtr + D * 4);
 };
 
+// Split path: what the scan leaves for the output kernel per chunk-head --
+// the chunk-start state S^T and v'^T as bf16 hi/lo, value rows x columns, in
+// groups of 8 columns: element (r, c) of an R-row tile at (c / 8 * R + r) * 8
+// + c % 8. A warp's 32 rows of one group are one 512-byte store, and the 8
+// rows an ldmatrix reads are 128 contiguous bytes.
+template <int D>
+struct ScanOut {
+    static constexpr int kSH = 0;                       // [D][D]  (value, key)
+    static constexpr int kSL = kSH + D * D * 2;
+    static constexpr int kVH = kSL + D * D * 2;         // [D][64] (value, token)
+    static constexpr int kVL = kVH + D * BT * 2;
+    static constexpr int kBytes = r1k(kVL + D * BT * 2);
+};
+template <int R>
+__device__ __forceinline__ int fr(int r, int c) { return ((c >> 3) * R + r) * 8 + (c & 7); }
+
 // Block pair index p -> (I, J), J <= I, in the order (0,0) (1,0) (1,1) (2,0) ...
 __device__ __forceinline__ void pair_ij(int p, int &I, int &J) {
     I = (p >= 6) ? 3 : (p >= 3) ? 2 : (p >= 1) ? 1 : 0;
@@ -1408,15 +1424,15 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 // Split path, part 2: the inter-chunk scan alone. One CTA per (sequence,
 // head). The producer thread streams each chunk's record (written by the
 // prep kernel) into the operand slots of shared memory as soon as the
-// previous chunk's product reading a slot has completed, and issues the five
-// tcgen05 products; the compute warps split the state, convert v', and store
-// the output. Per chunk the serial chain is: S split -> W S -> v' conversion
-// -> state update -> next S split.
+// previous chunk's product reading a slot has completed, and issues the two
+// state products (W S onto -u, the state update); the compute warps split the
+// state, convert v', and leave both splits for the output kernel. Per chunk
+// the serial chain is: S split -> W S -> v' conversion -> state update.
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(kThreads + 32, 1)
     chunk_scan_kernel(const KdaArgs p, const int32_t *order, const __grid_constant__ TmaMaps maps,
-                      const uint8_t *rec, const uint8_t *trec, const int32_t *cbase) {
+                      const uint8_t *rec, const uint8_t *trec, const int32_t *cbase, uint8_t *sout) {
     using L = Smem<D>;
     using R = Rec<D>;
     constexpr int KS = D / 16;
@@ -1424,21 +1440,18 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     extern __shared__ __align__(1024) unsigned char sm_raw[];
     unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
     const float *const Us = reinterpret_cast<const float *>(sm + L::kRawG);          // -u^T slot (record layout)
-    __nv_bfloat16 *const Ost = reinterpret_cast<__nv_bfloat16 *>(sm + L::kV);      // o tile staging
     float *const vec = reinterpret_cast<float *>(sm + L::kVec);
     uint64_t *const mb = reinterpret_cast<uint64_t *>(sm + L::kBar);
     // product completions
-    uint64_t *const bG2 = mb + 1, *const bG3a = mb + 2, *const bG4 = mb + 3, *const bO = mb + 4;
+    uint64_t *const bG2 = mb + 1, *const bG4 = mb + 3;
     // operand-slot loads
-    uint64_t *const lU = mb + 5, *const lEgl = mb + 6, *const lW = mb + 7, *const lQG = mb + 8, *const lKD = mb + 9,
-                    *const lAQ = mb + 10, *const lTR = mb + 11;
+    uint64_t *const lU = mb + 5, *const lEgl = mb + 6, *const lW = mb + 7, *const lKD = mb + 9, *const lTR = mb + 11;
     // compute warps -> producer
-    uint64_t *const sSplit = mb + 12, *const sConv = mb + 13, *const sOut = mb + 14;
+    uint64_t *const sSplit = mb + 12, *const sConv = mb + 13;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 120);
     const uint32_t s_base = smem_addr(sm);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int H = p.num_heads;
     const int rr = blockIdx.x / p.head_count;
     const int hl = blockIdx.x % p.head_count, h = p.head_begin + hl;
     const int req = order != nullptr ? order[rr] : rr;
@@ -1474,6 +1487,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     };
     auto rec_of = [&](int c) {
         return rec + (static_cast<int64_t>(cbase[req] + c) * p.head_count + hl) * R::kBytes;
+    };
+    auto sout_of = [&](int c) {
+        return sout + (static_cast<int64_t>(cbase[req] + c) * p.head_count + hl) * ScanOut<D>::kBytes;
     };
     const uint8_t *trk_rec = trec + (static_cast<int64_t>(req) * p.head_count + hl) * R::tBytes;
 
@@ -1511,9 +1527,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             load(lU, sm + L::kRawG, rec_of(0) + R::kU, BT * D * 4);
             load(lEgl, vec + L::vEgl, rec_of(0) + R::kEgl, D * 4);
             load(lW, sm + L::kX, rec_of(0) + R::kW, BT * D * 4);
-            load(lQG, sm + L::kY, rec_of(0) + R::kQG, BT * D * 4);
             load(lKD, sm + L::kZ, rec_of(0) + R::kKD, BT * D * 4);
-            load(lAQ, sm + L::kAQh, rec_of(0) + R::kAQ, BT * BT * 4);
             if (trk_at(0)) load_tr();
             uint32_t trph = 0;
             for (int c = 0; c < nchunks; ++c) {
@@ -1539,32 +1553,16 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 // e^{gl} of the next chunk once this one's last reader is done: the
                 // split, or on a tracked chunk the v' conversion.
                 if (nxt && !trk) load(lEgl, vec + L::vEgl, rec_of(c + 1) + R::kEgl, D * 4);
-                // o^T = (QG S)^T once the previous o tile has left tensor memory.
-                pwait(lQG, ph);
-                if (c > 0) pwait(sOut, static_cast<uint32_t>((c - 1) & 1));
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < KS; ++kk) {
-                    const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
-                    const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
-                    const uint64_t qh = sdesc(s_base + L::kY + off, 16, 1024);
-                    const uint64_t ql = sdesc(s_base + L::kY + BT * D * 2 + off, 16, 1024);
-                    umma_ts(tmem + kColO, al, qh, id_n64, kk > 0 ? 1u : 0u);
-                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
-                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
-                }
-                umma_commit(bG3a);
                 // W of the next chunk as soon as W S has completed: it is the first
                 // operand the next chunk's chain needs.
                 if (nxt) {
                     pwait(bG2, ph);
                     load(lW, sm + L::kX, rec_of(c + 1) + R::kW, BT * D * 4);
                 }
-                // S^T += v'^T KD (and the tracked prefix), o^T += v'^T Aqk^T.
+                // S^T += v'^T KD (and the tracked prefix).
                 pwait(sConv, ph);
                 if (nxt && trk) load(lEgl, vec + L::vEgl, rec_of(c + 1) + R::kEgl, D * 4);
                 pwait(lKD, ph);
-                pwait(lAQ, ph);
                 if (trk) pwait(lTR, trph);
                 tc_fence_after();
 #pragma unroll
@@ -1584,74 +1582,17 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     }
                 }
                 umma_commit(bG4);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
-                    const uint64_t qh = sdesc(s_base + L::kAQh + kk * 32, 16, 1024);
-                    const uint64_t ql = sdesc(s_base + L::kAQl + kk * 32, 16, 1024);
-                    umma_ts(tmem + kColO, al, qh, id_n64, 1u);
-                    umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
-                    umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
-                }
-                umma_commit(bO);
                 if (trk) trph ^= 1u;
                 if (nxt) {
-                    pwait(bG3a, ph);
-                    load(lQG, sm + L::kY, rec_of(c + 1) + R::kQG, BT * D * 4);
                     pwait(bG4, ph);
                     load(lKD, sm + L::kZ, rec_of(c + 1) + R::kKD, BT * D * 4);
                     if (trk_at(c + 1)) load_tr();
-                    pwait(bO, ph);
-                    load(lAQ, sm + L::kAQh, rec_of(c + 1) + R::kAQ, BT * BT * 4);
                 }
             }
         }
     } else {
         // ===== compute warps 0..15 =====
         auto cbar = [] { nbar(1, kThreads); };
-        auto o_cols = [&](int64_t ot0, int on) {   // this warp's 16 output rows -> staging (or fp32 out)
-            uint32_t r[16];
-            tmem_ld16(tq + kColO + 16 * cs, r);
-            tmem_ld_wait();
-            if (srow < D) {
-                if (p.out_fp32) {
-                    float *o = static_cast<float *>(p.out) + (ot0 * H + h) * D + srow;
-                    const int64_t row_stride = static_cast<int64_t>(H) * D;
-#pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        if (16 * cs + e < on) o[(16 * cs + e) * row_stride] = __uint_as_float(r[e]);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        Ost[(16 * cs + e) * D + srow] = __float2bfloat16_rn(__uint_as_float(r[e]));
-                }
-            }
-        };
-        auto o_store = [&](int64_t ot0, int on) {   // issuing thread only
-            if (p.out_fp32) return;
-            if (on == BT) {
-                tma_store_3d(&maps.o, Ost, 0, h, static_cast<int>(ot0));
-            } else {
-                __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (ot0 * H + h) * D;
-                for (int rw = 0; rw < on; ++rw)
-                    bulk_s2g(o + static_cast<int64_t>(rw) * H * D, Ost + rw * D, D * 2);
-            }
-            bulk_commit();
-        };
-        // o tile of chunk c-1 -> out, once its last product completed.
-        auto o_out = [&](int cprev) {
-            if (!mbar_wait(bO, static_cast<uint32_t>(cprev & 1), p.status) && tid == 0)
-                report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
-            tc_fence_after();
-            if (tid == 0) bulk_wait_read();   // the previous tile has left the staging area
-            cbar();
-            o_cols(bos + static_cast<int64_t>(cprev) * BT, chunk_rows(cprev));
-            fence_async_smem();
-            tc_fence_before();
-            cbar();
-            if (tid == 0) o_store(bos + static_cast<int64_t>(cprev) * BT, chunk_rows(cprev));
-        };
-
         // Initial state S^T -> tensor memory; a length-0 checkpoint is the initial state.
         {
             const float *hs = p.state + slot * s0 + h * s1;
@@ -1703,6 +1644,19 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
                 tmem_st<SC / 2>(tq + kColSH + (SC / 2) * cs, hi);
                 tmem_st<SC / 2>(tq + kColSL + (SC / 2) * cs, lo);
+                if (srow < D) {
+                    // The chunk-start state for the output kernel: (value row, keys).
+                    uint16_t *sh = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kSH);
+                    uint16_t *sl = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kSL);
+#pragma unroll
+                    for (int q8 = 0; q8 < SC / 8; ++q8) {
+                        const int o = fr<D>(srow, SC * cs + 8 * q8);
+                        *reinterpret_cast<uint4 *>(sh + o) =
+                            make_uint4(hi[4 * q8], hi[4 * q8 + 1], hi[4 * q8 + 2], hi[4 * q8 + 3]);
+                        *reinterpret_cast<uint4 *>(sl + o) =
+                            make_uint4(lo[4 * q8], lo[4 * q8 + 1], lo[4 * q8 + 2], lo[4 * q8 + 3]);
+                    }
+                }
                 if (!trk) {
                     const float *eg = vec + L::vEgl + SC * cs;
 #pragma unroll
@@ -1714,11 +1668,6 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tc_fence_before();
             cbar();
             if (tid == 0) mbar_arrive(sSplit);   // S split, NU = -u^T, e^{gl} and -u^T slots read
-            // The previous chunk's o tile, while W S runs.
-            if (c > 0) {
-                o_out(c - 1);
-                if (tid == 0) mbar_arrive(sOut);
-            }
             // -v'^T (fp32) -> v'^T hi/lo A operand.
             if (!mbar_wait(bG2, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
@@ -1731,11 +1680,23 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     split2(-__uint_as_float(r[2 * e]), -__uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
                 tmem_st8(tq + kColVH + 8 * cs, hi);
                 tmem_st8(tq + kColVL + 8 * cs, lo);
+                if (srow < D) {
+                    // v'^T for the output kernel: (value row, tokens).
+                    uint16_t *vh = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kVH);
+                    uint16_t *vl = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kVL);
+#pragma unroll
+                    for (int q8 = 0; q8 < 2; ++q8) {
+                        const int o = fr<D>(srow, 16 * cs + 8 * q8);
+                        *reinterpret_cast<uint4 *>(vh + o) =
+                            make_uint4(hi[4 * q8], hi[4 * q8 + 1], hi[4 * q8 + 2], hi[4 * q8 + 3]);
+                        *reinterpret_cast<uint4 *>(vl + o) =
+                            make_uint4(lo[4 * q8], lo[4 * q8 + 1], lo[4 * q8 + 2], lo[4 * q8 + 3]);
+                    }
+                }
             }
             if (trk) {
-                // S^T e^{gc_{r-1}} into the S hi/lo columns once o = QG S has
-                // read them, then the deferred S^T e^{gl}.
-                if (!mbar_wait(bG3a, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                // S^T e^{gc_{r-1}} into the S hi/lo columns (W S, their last
+                // reader, has completed), then the deferred S^T e^{gl}.
                 if (!mbar_wait(lTR, trph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
                 tc_fence_after();
                 uint32_t r[SC], t[SC];
@@ -1769,7 +1730,6 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
         }
         if (nchunks > 0) {
-            o_out(nchunks - 1);
             if (!mbar_wait(bG4, static_cast<uint32_t>((nchunks - 1) & 1), p.status) && tid == 0)
                 report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
@@ -1785,13 +1745,139 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
             }
         }
-        if (tid == 0) bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// Split path, part 3: the outputs, one CTA per (chunk, head) on all SMs:
+// o = QG S_c + Aqk v' from the chunk's record (QG, Aqk) and the scan's splits
+// of S_c and v', as split-bf16 mma.sync products; the tile leaves by TMA.
+template <int D>
+struct OutSmem {
+    static constexpr int kQG = 0;                              // f64 hi/lo [64][D] (token, key)
+    static constexpr int kAQ = kQG + BT * D * 4;               // swizzled hi/lo [64][64]
+    static constexpr int kS = kAQ + BT * BT * 4;               // ScanOut layout: S hi/lo, v' hi/lo
+    static constexpr int kO = kS + ScanOut<D>::kBytes;         // bf16 [64][D] output staging
+    static constexpr int kBar = kO + BT * D * 2;
+    static constexpr int kAlloc = kBar + 16 + 1024;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) chunk_out_kernel(const KdaArgs p, const __grid_constant__ TmaMaps maps,
+                                                            const uint8_t *rec, const uint8_t *sout,
+                                                            const int32_t *cbase) {
+    using M = OutSmem<D>;
+    using R = Rec<D>;
+    using SO = ScanOut<D>;
+    constexpr int KS = D / 16;
+    constexpr int NT = D / 32;                 // 8-column n-tiles per warp
+    extern __shared__ __align__(1024) unsigned char sm_raw[];
+    unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
+    const uint32_t s_base = smem_addr(sm);
+    uint64_t *const bar = reinterpret_cast<uint64_t *>(sm + M::kBar);
+    __nv_bfloat16 *const Ost = reinterpret_cast<__nv_bfloat16 *>(sm + M::kO);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int H = p.num_heads;
+    const int hl = blockIdx.x % p.head_count, h = p.head_begin + hl;
+    const int sl = blockIdx.x / p.head_count;
+    int req = 0;
+    while (req < p.num_req && cbase[req + 1] <= sl) ++req;
+    if (req >= p.num_req) return;
+    const int c = sl - cbase[req];
+    const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
+    const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
+    const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
+    if (bos < 0 || eos < bos || eos > p.num_tokens || slot < 0 || slot >= p.num_slots) return;   // reported by the scan
+    const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
+    const int n = static_cast<int>(eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT));
+    const int64_t rix = static_cast<int64_t>(sl) * p.head_count + hl;
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(bar, BT * D * 4 + BT * BT * 4 + SO::kBytes);
+        bulk_g2s(sm + M::kQG, rec + rix * R::kBytes + R::kQG, BT * D * 4, bar);
+        bulk_g2s(sm + M::kAQ, rec + rix * R::kBytes + R::kAQ, BT * BT * 4, bar);
+        bulk_g2s(sm + M::kS, sout + rix * SO::kBytes, SO::kBytes, bar);
+    }
+    __syncthreads();
+    if (!mbar_wait(bar, 0, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+
+    // Warp w: tokens [16 (w % 4), +16), values [(w / 4) D/4, +D/4).
+    const int mt = warp & 3, v0 = (warp >> 2) * (D / 4);
+    float acc[NT][4] = {};
+    const uint32_t sh = s_base + M::kS + SO::kSH, slo = s_base + M::kS + SO::kSL;
+    const uint32_t vh = s_base + M::kS + SO::kVH, vlo = s_base + M::kS + SO::kVL;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {   // QG S_c: K = keys
+        uint32_t ah[4], al[4];
+        ldsm_x4(ah, s_base + M::kQG + 2 * fa_a(lane, 16 * mt, 16 * ks));
+        ldsm_x4(al, s_base + M::kQG + BT * D * 2 + 2 * fa_a(lane, 16 * mt, 16 * ks));
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+            const int q = lane >> 3, r = lane & 7;
+            const uint32_t ob = 2 * fr<D>(v0 + 16 * np + r + ((q >> 1) << 3), 16 * ks + ((q & 1) << 3));
+            uint32_t bh[4], bl[4];
+            ldsm_x4(bh, sh + ob);
+            ldsm_x4(bl, slo + ob);
+            mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+            mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+        }
+    }
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {    // Aqk v': K = tokens
+        uint32_t ah[4], al[4];
+        ldsm_x4(ah, s_base + M::kAQ + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
+        ldsm_x4(al, s_base + M::kAQ + BT * BT * 2 + 2 * lda_a<BT>(lane, 16 * mt, 16 * ks));
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+            const int q = lane >> 3, r = lane & 7;
+            const uint32_t ob = 2 * fr<D>(v0 + 16 * np + r + ((q >> 1) << 3), 16 * ks + ((q & 1) << 3));
+            uint32_t bh[4], bl[4];
+            ldsm_x4(bh, vh + ob);
+            ldsm_x4(bl, vlo + ob);
+            mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+            mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+        }
+    }
+    if (p.out_fp32) {
+        float *o = static_cast<float *>(p.out);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int t = 16 * mt + g + 8 * hf, v = v0 + 8 * nt + 2 * t4;
+                if (t < n) {
+                    float *row = o + ((t0 + t) * H + h) * D + v;
+                    row[0] = acc[nt][2 * hf];
+                    row[1] = acc[nt][2 * hf + 1];
+                }
+            }
+        return;
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            const int t = 16 * mt + g + 8 * hf, v = v0 + 8 * nt + 2 * t4;
+            *reinterpret_cast<uint32_t *>(Ost + t * D + v) = pack_bf16(acc[nt][2 * hf], acc[nt][2 * hf + 1]);
+        }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        if (n == BT) {
+            tma_store_3d(&maps.o, Ost, 0, h, static_cast<int>(t0));
+        } else {
+            __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (t0 * H + h) * D;
+            for (int rw = 0; rw < n; ++rw) bulk_s2g(o + static_cast<int64_t>(rw) * H * D, Ost + rw * D, D * 2);
+        }
+        bulk_commit();
+        bulk_wait_all();
     }
 }
 
@@ -1929,17 +2015,19 @@ static bool want_split(int32_t num_req, int32_t heads, int32_t num_tokens) {
 static size_t a256(size_t x) { return (x + 255) / 256 * 256; }
 
 struct SplitLayout {
-    size_t cbase, rec, trec, total;
+    size_t cbase, rec, trec, sout, total;
 };
 static SplitLayout split_layout(int32_t num_req, int32_t num_tokens, int32_t heads, int32_t D) {
     const size_t slots = static_cast<size_t>(num_tokens) / chunk::BT + static_cast<size_t>(num_req);
     const size_t rb = D == 64 ? chunk::Rec<64>::kBytes : chunk::Rec<128>::kBytes;
     const size_t tb = D == 64 ? chunk::Rec<64>::tBytes : chunk::Rec<128>::tBytes;
+    const size_t ob = D == 64 ? chunk::ScanOut<64>::kBytes : chunk::ScanOut<128>::kBytes;
     SplitLayout l;
     l.cbase = order_bytes(num_req);
     l.rec = l.cbase + a256((static_cast<size_t>(num_req) + 1) * sizeof(int32_t));
     l.trec = l.rec + slots * static_cast<size_t>(heads) * rb;
-    l.total = l.trec + static_cast<size_t>(num_req) * static_cast<size_t>(heads) * tb;
+    l.sout = l.trec + static_cast<size_t>(num_req) * static_cast<size_t>(heads) * tb;
+    l.total = l.sout + slots * static_cast<size_t>(heads) * ob;
     return l;
 }
 
@@ -1948,21 +2036,24 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
     using L = chunk::Smem<D>;
     chunk::TmaMaps maps;
     if (!encode_maps(maps, a, D, MODE == KDA_GATE_RAW)) return KDA_ERR_LAUNCH;
-    static bool opted_prep[64], opted_scan[64];
+    static bool opted_prep[64], opted_scan[64], opted_out[64];
     if (!opt_in(chunk::chunk_kernel<D, MODE, true>, opted_prep, L::kAlloc) ||
-        !opt_in(chunk::chunk_scan_kernel<D>, opted_scan, L::kAlloc))
+        !opt_in(chunk::chunk_scan_kernel<D>, opted_scan, L::kAlloc) ||
+        !opt_in(chunk::chunk_out_kernel<D>, opted_out, chunk::OutSmem<D>::kAlloc))
         return KDA_ERR_LAUNCH;
     const SplitLayout lay = split_layout(a->num_req, a->num_tokens, a->head_count, D);
     int32_t *order = reinterpret_cast<int32_t *>(ws);
     int32_t *cbase = reinterpret_cast<int32_t *>(ws + lay.cbase);
-    uint8_t *rec = ws + lay.rec, *trec = ws + lay.trec;
+    uint8_t *rec = ws + lay.rec, *trec = ws + lay.trec, *sout = ws + lay.sout;
     chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
     chunk::chunk_base_kernel<<<1, 32, 0, st>>>(*a, cbase);
     const int64_t slots = static_cast<int64_t>(a->num_tokens) / chunk::BT + a->num_req;
     chunk::chunk_kernel<D, MODE, true><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads + 32,
                                          L::kAlloc, st>>>(*a, nullptr, maps, rec, trec, cbase);
     chunk::chunk_scan_kernel<D><<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count),
-                                  chunk::kThreads + 32, L::kAlloc, st>>>(*a, order, maps, rec, trec, cbase);
+                                  chunk::kThreads + 32, L::kAlloc, st>>>(*a, order, maps, rec, trec, cbase, sout);
+    chunk::chunk_out_kernel<D><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads,
+                                 chunk::OutSmem<D>::kAlloc, st>>>(*a, maps, rec, sout, cbase);
     return KDA_OK;
 }
 
