@@ -378,17 +378,16 @@ struct Rec {
 };
 
 // Split path: what the scan leaves for the output kernel per chunk-head --
-// the chunk-start state S^T and v'^T as bf16 hi/lo, value rows x columns, in
+// the chunk-start state S^T as bf16 hi/lo, value rows x key columns, in
 // groups of 8 columns: element (r, c) of an R-row tile at (c / 8 * R + r) * 8
 // + c % 8. A warp's 32 rows of one group are one 512-byte store, and the 8
-// rows an ldmatrix reads are 128 contiguous bytes.
+// rows an ldmatrix reads are 128 contiguous bytes. (The output kernel keeps
+// v' in the same layout, [D][64] (value, token).)
 template <int D>
 struct ScanOut {
     static constexpr int kSH = 0;                       // [D][D]  (value, key)
     static constexpr int kSL = kSH + D * D * 2;
-    static constexpr int kVH = kSL + D * D * 2;         // [D][64] (value, token)
-    static constexpr int kVL = kVH + D * BT * 2;
-    static constexpr int kBytes = r1k(kVL + D * BT * 2);
+    static constexpr int kBytes = r1k(kSL + D * D * 2);
 };
 template <int R>
 __device__ __forceinline__ int fr(int r, int c) { return ((c >> 3) * R + r) * 8 + (c & 7); }
@@ -1426,8 +1425,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 // prep kernel) into the operand slots of shared memory as soon as the
 // previous chunk's product reading a slot has completed, and issues the two
 // state products (W S onto -u, the state update); the compute warps split the
-// state, convert v', and leave both splits for the output kernel. Per chunk
-// the serial chain is: S split -> W S -> v' conversion -> state update.
+// state (and leave the split for the output kernel) and convert v'. Per chunk
+// the serial chain is: S split -> W S -> v' conversion -> state update; the
+// stores and the next chunk's -u^T copy run beside the products.
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(kThreads + 32, 1)
@@ -1439,13 +1439,15 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     constexpr int SC = D / 4;                        // state columns per slice
     extern __shared__ __align__(1024) unsigned char sm_raw[];
     unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
-    const float *const Us = reinterpret_cast<const float *>(sm + L::kRawG);          // -u^T slot (record layout)
+    // -u^T slots (record layout), chunk c in slot c & 1
+    const float *const Us0 = reinterpret_cast<const float *>(sm + L::kRawG);
+    const float *const Us1 = reinterpret_cast<const float *>(sm + L::kY);
     float *const vec = reinterpret_cast<float *>(sm + L::kVec);
     uint64_t *const mb = reinterpret_cast<uint64_t *>(sm + L::kBar);
     // product completions
     uint64_t *const bG2 = mb + 1, *const bG4 = mb + 3;
     // operand-slot loads
-    uint64_t *const lU = mb + 5, *const lEgl = mb + 6, *const lW = mb + 7, *const lKD = mb + 9, *const lTR = mb + 11;
+    uint64_t *const lU0 = mb + 5, *const lU1 = mb + 4, *const lEgl = mb + 6, *const lW = mb + 7, *const lKD = mb + 9, *const lTR = mb + 11;
     // compute warps -> producer
     uint64_t *const sSplit = mb + 12, *const sConv = mb + 13;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 120);
@@ -1524,7 +1526,8 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 bulk_g2s(sm + L::kRawQ, trk_rec + R::tKR, BT * D * 4, lTR);
                 bulk_g2s(vec + L::vEtr, trk_rec + R::tEtr, D * 4, lTR);
             };
-            load(lU, sm + L::kRawG, rec_of(0) + R::kU, BT * D * 4);
+            load(lU0, sm + L::kRawG, rec_of(0) + R::kU, BT * D * 4);
+            if (nchunks > 1) load(lU1, sm + L::kY, rec_of(1) + R::kU, BT * D * 4);
             load(lEgl, vec + L::vEgl, rec_of(0) + R::kEgl, D * 4);
             load(lW, sm + L::kX, rec_of(0) + R::kW, BT * D * 4);
             load(lKD, sm + L::kZ, rec_of(0) + R::kKD, BT * D * 4);
@@ -1536,7 +1539,10 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 // NU (= -u^T, set by the compute warps with the split) += (W S)^T
                 // -> -v'^T, once the state is split and W landed.
                 pwait(sSplit, ph);
-                if (nxt) load(lU, sm + L::kRawG, rec_of(c + 1) + R::kU, BT * D * 4);   // -u^T was copied
+                // -u^T of chunk c was copied into NU before the split: its slot
+                // takes chunk c + 2.
+                if (c + 2 < nchunks)
+                    load((c & 1) ? lU1 : lU0, sm + ((c & 1) ? L::kY : L::kRawG), rec_of(c + 2) + R::kU, BT * D * 4);
                 pwait(lW, ph);
                 tc_fence_after();
 #pragma unroll
@@ -1550,9 +1556,6 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     umma_ts(tmem + kColNU, ah, wh, id_n64, 1u);
                 }
                 umma_commit(bG2);
-                // e^{gl} of the next chunk once this one's last reader is done: the
-                // split, or on a tracked chunk the v' conversion.
-                if (nxt && !trk) load(lEgl, vec + L::vEgl, rec_of(c + 1) + R::kEgl, D * 4);
                 // W of the next chunk as soon as W S has completed: it is the first
                 // operand the next chunk's chain needs.
                 if (nxt) {
@@ -1561,7 +1564,8 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 }
                 // S^T += v'^T KD (and the tracked prefix).
                 pwait(sConv, ph);
-                if (nxt && trk) load(lEgl, vec + L::vEgl, rec_of(c + 1) + R::kEgl, D * 4);
+                // e^{gl} of the next chunk: this one's was last read before sConv.
+                if (nxt) load(lEgl, vec + L::vEgl, rec_of(c + 1) + R::kEgl, D * 4);
                 pwait(lKD, ph);
                 if (trk) pwait(lTR, trph);
                 tc_fence_after();
@@ -1609,99 +1613,84 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tmem_st<SC>(tq + kColS + SC * cs, r);
             tmem_st_wait();
         }
+        auto cwait = [&](uint64_t *bar, uint32_t phase) {
+            if (!mbar_wait(bar, phase, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+        };
+        // NU <- -u^T of chunk c (this warp's 16 token columns of value row srow);
+        // the copy reaches G2 through the wait, fence and barrier before sSplit.
+        auto init_nu = [&](int c) {
+            cwait((c & 1) ? lU1 : lU0, static_cast<uint32_t>((c >> 1) & 1));
+            const float *us = (c & 1) ? Us1 : Us0;
+            uint32_t r[16];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 u4 = srow < D ? *reinterpret_cast<const float4 *>(us + ((4 * cs + k) * D + srow) * 4)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                r[4 * k] = __float_as_uint(u4.x);
+                r[4 * k + 1] = __float_as_uint(u4.y);
+                r[4 * k + 2] = __float_as_uint(u4.z);
+                r[4 * k + 3] = __float_as_uint(u4.w);
+            }
+            tmem_st16(tq + kColNU + 16 * cs, r);
+        };
+        if (nchunks > 0) init_nu(0);
         uint32_t trph = 0;
         for (int c = 0; c < nchunks; ++c) {
             const uint32_t ph = static_cast<uint32_t>(c & 1);
             const bool trk = trk_at(c);
-            // S^T -> bf16 hi/lo A operand; S^T <- S^T e^{gl} (deferred on a tracked chunk).
-            if (c > 0) {
-                if (!mbar_wait(bG4, static_cast<uint32_t>((c - 1) & 1), p.status) && tid == 0)
-                    report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
-            }
-            if (!mbar_wait(lEgl, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
-            if (!mbar_wait(lU, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            // (1) S^T -> bf16 hi/lo A operand of W S: the only work between the
+            // state update of chunk c - 1 and the producer's next product.
+            if (c > 0) cwait(bG4, static_cast<uint32_t>((c - 1) & 1));
             tc_fence_after();
-            {
-                // NU <- -u^T (this warp's 16 token columns of value row srow).
-                uint32_t r[16];
+            uint32_t r[SC], hi[SC / 2], lo[SC / 2];
+            tmem_ld<SC>(tq + kColS + SC * cs, r);
+            tmem_ld_wait();
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float4 u4 = srow < D ? *reinterpret_cast<const float4 *>(Us + ((4 * cs + k) * D + srow) * 4)
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
-                    r[4 * k] = __float_as_uint(u4.x);
-                    r[4 * k + 1] = __float_as_uint(u4.y);
-                    r[4 * k + 2] = __float_as_uint(u4.z);
-                    r[4 * k + 3] = __float_as_uint(u4.w);
-                }
-                tmem_st16(tq + kColNU + 16 * cs, r);
-            }
-            {
-                uint32_t r[SC], hi[SC / 2], lo[SC / 2];
-                tmem_ld<SC>(tq + kColS + SC * cs, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < SC / 2; ++e)
-                    split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
-                tmem_st<SC / 2>(tq + kColSH + (SC / 2) * cs, hi);
-                tmem_st<SC / 2>(tq + kColSL + (SC / 2) * cs, lo);
-                if (srow < D) {
-                    // The chunk-start state for the output kernel: (value row, keys).
-                    uint16_t *sh = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kSH);
-                    uint16_t *sl = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kSL);
-#pragma unroll
-                    for (int q8 = 0; q8 < SC / 8; ++q8) {
-                        const int o = fr<D>(srow, SC * cs + 8 * q8);
-                        *reinterpret_cast<uint4 *>(sh + o) =
-                            make_uint4(hi[4 * q8], hi[4 * q8 + 1], hi[4 * q8 + 2], hi[4 * q8 + 3]);
-                        *reinterpret_cast<uint4 *>(sl + o) =
-                            make_uint4(lo[4 * q8], lo[4 * q8 + 1], lo[4 * q8 + 2], lo[4 * q8 + 3]);
-                    }
-                }
-                if (!trk) {
-                    const float *eg = vec + L::vEgl + SC * cs;
-#pragma unroll
-                    for (int e = 0; e < SC; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * eg[e]);
-                    tmem_st<SC>(tq + kColS + SC * cs, r);
-                }
-            }
+            for (int e = 0; e < SC / 2; ++e)
+                split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+            tmem_st<SC / 2>(tq + kColSH + (SC / 2) * cs, hi);
+            tmem_st<SC / 2>(tq + kColSL + (SC / 2) * cs, lo);
             tmem_st_wait();
             tc_fence_before();
             cbar();
-            if (tid == 0) mbar_arrive(sSplit);   // S split, NU = -u^T, e^{gl} and -u^T slots read
-            // -v'^T (fp32) -> v'^T hi/lo A operand.
-            if (!mbar_wait(bG2, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
-            tc_fence_after();
-            {
-                uint32_t r[16], hi[8], lo[8];
-                tmem_ld16(tq + kColNU + 16 * cs, r);
-                tmem_ld_wait();
+            if (tid == 0) mbar_arrive(sSplit);   // S split, NU = -u^T, -u^T slot read
+            // (2) while W S runs: the chunk-start state for the output kernel,
+            // (value row, keys), and S^T <- S^T e^{gl} (deferred on a tracked chunk).
+            if (srow < D) {
+                uint16_t *sh = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kSH);
+                uint16_t *sl = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kSL);
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    split2(-__uint_as_float(r[2 * e]), -__uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
-                tmem_st8(tq + kColVH + 8 * cs, hi);
-                tmem_st8(tq + kColVL + 8 * cs, lo);
-                if (srow < D) {
-                    // v'^T for the output kernel: (value row, tokens).
-                    uint16_t *vh = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kVH);
-                    uint16_t *vl = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kVL);
-#pragma unroll
-                    for (int q8 = 0; q8 < 2; ++q8) {
-                        const int o = fr<D>(srow, 16 * cs + 8 * q8);
-                        *reinterpret_cast<uint4 *>(vh + o) =
-                            make_uint4(hi[4 * q8], hi[4 * q8 + 1], hi[4 * q8 + 2], hi[4 * q8 + 3]);
-                        *reinterpret_cast<uint4 *>(vl + o) =
-                            make_uint4(lo[4 * q8], lo[4 * q8 + 1], lo[4 * q8 + 2], lo[4 * q8 + 3]);
-                    }
+                for (int q8 = 0; q8 < SC / 8; ++q8) {
+                    const int o = fr<D>(srow, SC * cs + 8 * q8);
+                    *reinterpret_cast<uint4 *>(sh + o) =
+                        make_uint4(hi[4 * q8], hi[4 * q8 + 1], hi[4 * q8 + 2], hi[4 * q8 + 3]);
+                    *reinterpret_cast<uint4 *>(sl + o) =
+                        make_uint4(lo[4 * q8], lo[4 * q8 + 1], lo[4 * q8 + 2], lo[4 * q8 + 3]);
                 }
             }
+            cwait(lEgl, ph);
+            if (!trk) {
+                const float *eg = vec + L::vEgl + SC * cs;
+#pragma unroll
+                for (int e = 0; e < SC; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * eg[e]);
+                tmem_st<SC>(tq + kColS + SC * cs, r);
+            }
+            // (3) -v'^T (fp32) -> v'^T hi/lo A operand of the state update.
+            cwait(bG2, ph);
+            tc_fence_after();
+            uint32_t v[16], vh[8], vl[8];
+            tmem_ld16(tq + kColNU + 16 * cs, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+                split2(-__uint_as_float(v[2 * e]), -__uint_as_float(v[2 * e + 1]), vh[e], vl[e]);
+            tmem_st8(tq + kColVH + 8 * cs, vh);
+            tmem_st8(tq + kColVL + 8 * cs, vl);
             if (trk) {
                 // S^T e^{gc_{r-1}} into the S hi/lo columns (W S, their last
                 // reader, has completed), then the deferred S^T e^{gl}.
-                if (!mbar_wait(lTR, trph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
-                tc_fence_after();
-                uint32_t r[SC], t[SC];
-                tmem_ld<SC>(tq + kColS + SC * cs, r);
-                tmem_ld_wait();
+                cwait(lTR, trph);
+                uint32_t t[SC];
 #pragma unroll
                 for (int e = 0; e < SC; ++e) {
                     t[e] = __float_as_uint(__uint_as_float(r[e]) * vec[L::vEtr + SC * cs + e]);
@@ -1713,20 +1702,27 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tmem_st_wait();
             tc_fence_before();
             cbar();
-            if (tid == 0) mbar_arrive(sConv);
+            if (tid == 0) mbar_arrive(sConv);   // v' split, S^T e^{gl} (and the checkpoint operand) stored
+            // (4) while the state update runs: -u^T of the next chunk into NU
+            // (the conversion above was its last reader).
+            if (c + 1 < nchunks) init_nu(c + 1);
             if (trk) {
-                // The checkpoint leaves tensor memory before the next split reuses its columns.
-                if (!mbar_wait(bG4, ph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                // The checkpoint leaves tensor memory before the next split
+                // reuses its columns (the barrier orders every warp's read
+                // before any warp's next split).
+                cwait(bG4, ph);
                 tc_fence_after();
                 float *ts = p.state + tslot * s0 + h * s1;
-                uint32_t r[SC];
-                tmem_ld<SC>(tq + kColTR + SC * cs, r);
+                uint32_t t[SC];
+                tmem_ld<SC>(tq + kColTR + SC * cs, t);
                 tmem_ld_wait();
                 if (srow < D) {
 #pragma unroll
-                    for (int e = 0; e < SC; ++e) ts[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
+                    for (int e = 0; e < SC; ++e) ts[srow * sv + (SC * cs + e) * sk] = __uint_as_float(t[e]);
                 }
                 trph ^= 1u;
+                tc_fence_before();
+                cbar();
             }
         }
         if (nchunks > 0) {
@@ -1754,17 +1750,25 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     }
 }
 
-// Split path, part 3: the outputs, one CTA per (chunk, head) on all SMs:
-// o = QG S_c + Aqk v' from the chunk's record (QG, Aqk) and the scan's splits
-// of S_c and v', as split-bf16 mma.sync products; the tile leaves by TMA.
+// Split path, part 3: the outputs, one CTA per (chunk, head) on all SMs. From
+// the chunk's record (W, QG, -u^T, Aqk) and the scan's split of the
+// chunk-start state S_c: v' = u - W S_c, then o = QG S_c + Aqk v', as
+// split-bf16 mma.sync products; the tile leaves by TMA. Recomputing v' here
+// keeps the scan's stores to the state alone (an SM stores 32 B per cycle).
 template <int D>
 struct OutSmem {
-    static constexpr int kQG = 0;                              // f64 hi/lo [64][D] (token, key)
-    static constexpr int kAQ = kQG + BT * D * 4;               // swizzled hi/lo [64][64]
-    static constexpr int kS = kAQ + BT * BT * 4;               // ScanOut layout: S hi/lo, v' hi/lo
-    static constexpr int kO = kS + ScanOut<D>::kBytes;         // bf16 [64][D] output staging
-    static constexpr int kBar = kO + BT * D * 2;
+    static constexpr int kW = 0;                               // f64 hi/lo [64][D] (token, key)
+    static constexpr int kQG = kW + BT * D * 4;                // f64 hi/lo [64][D] (record order: W, QG)
+    static constexpr int kU = kQG + BT * D * 4;                // -u^T, record layout
+    static constexpr int kAQ = kU + BT * D * 4;                // swizzled hi/lo [64][64] (record order: U, Aqk)
+    static constexpr int kS = kAQ + BT * BT * 4;               // ScanOut layout: S hi/lo
+    static constexpr int kV = kS + ScanOut<D>::kBytes;         // v' hi/lo, fr layout [D][64] (value, token)
+    static constexpr int kO = kW;                              // bf16 [64][D] output staging (W is dead by then)
+    static constexpr int kBar = kV + BT * D * 4;
     static constexpr int kAlloc = kBar + 16 + 1024;
+    static_assert(Rec<D>::kQG == Rec<D>::kW + BT * D * 4 && Rec<D>::kAQ == Rec<D>::kU + BT * D * 4,
+                  "record pieces the output kernel copies together must be adjacent");
+    static_assert(kAlloc <= 232448, "output kernel shared memory exceeds the 227 KiB per-CTA limit");
 };
 
 template <int D>
@@ -1800,9 +1804,10 @@ __global__ void __launch_bounds__(kThreads) chunk_out_kernel(const KdaArgs p, co
     if (tid == 0) {
         mbar_init(bar, 1);
         fence_mbar_init();
-        mbar_arrive_expect_tx(bar, BT * D * 4 + BT * BT * 4 + SO::kBytes);
-        bulk_g2s(sm + M::kQG, rec + rix * R::kBytes + R::kQG, BT * D * 4, bar);
-        bulk_g2s(sm + M::kAQ, rec + rix * R::kBytes + R::kAQ, BT * BT * 4, bar);
+        const uint8_t *r = rec + rix * R::kBytes;
+        mbar_arrive_expect_tx(bar, 2 * BT * D * 4 + BT * D * 4 + BT * BT * 4 + SO::kBytes);
+        bulk_g2s(sm + M::kW, r + R::kW, 2 * BT * D * 4, bar);                  // W, QG
+        bulk_g2s(sm + M::kU, r + R::kU, BT * D * 4 + BT * BT * 4, bar);        // -u^T, Aqk
         bulk_g2s(sm + M::kS, sout + rix * SO::kBytes, SO::kBytes, bar);
     }
     __syncthreads();
@@ -1810,14 +1815,16 @@ __global__ void __launch_bounds__(kThreads) chunk_out_kernel(const KdaArgs p, co
 
     // Warp w: tokens [16 (w % 4), +16), values [(w / 4) D/4, +D/4).
     const int mt = warp & 3, v0 = (warp >> 2) * (D / 4);
-    float acc[NT][4] = {};
+    float acc[NT][4] = {}, wsv[NT][4] = {};
     const uint32_t sh = s_base + M::kS + SO::kSH, slo = s_base + M::kS + SO::kSL;
-    const uint32_t vh = s_base + M::kS + SO::kVH, vlo = s_base + M::kS + SO::kVL;
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) {   // QG S_c: K = keys
-        uint32_t ah[4], al[4];
+    const uint32_t vh = s_base + M::kV, vlo = s_base + M::kV + D * BT * 2;
+#pragma unroll 2
+    for (int ks = 0; ks < KS; ++ks) {   // QG S_c and W S_c: K = keys, one pass over the S fragments
+        uint32_t ah[4], al[4], wh[4], wl[4];
         ldsm_x4(ah, s_base + M::kQG + 2 * fa_a(lane, 16 * mt, 16 * ks));
         ldsm_x4(al, s_base + M::kQG + BT * D * 2 + 2 * fa_a(lane, 16 * mt, 16 * ks));
+        ldsm_x4(wh, s_base + M::kW + 2 * fa_a(lane, 16 * mt, 16 * ks));
+        ldsm_x4(wl, s_base + M::kW + BT * D * 2 + 2 * fa_a(lane, 16 * mt, 16 * ks));
 #pragma unroll
         for (int np = 0; np < NT / 2; ++np) {
             const int q = lane >> 3, r = lane & 7;
@@ -1827,8 +1834,30 @@ __global__ void __launch_bounds__(kThreads) chunk_out_kernel(const KdaArgs p, co
             ldsm_x4(bl, slo + ob);
             mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
             mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+            mma3(wsv[2 * np], wh, wl, bh[0], bh[1], bl[0], bl[1]);
+            mma3(wsv[2 * np + 1], wh, wl, bh[2], bh[3], bl[2], bl[3]);
         }
     }
+    {
+        // v' = -(-u + W S_c) -> bf16 hi/lo at (value, token) for Aqk v'.
+        const float *us = reinterpret_cast<const float *>(sm + M::kU);
+        uint16_t *vph = reinterpret_cast<uint16_t *>(sm + M::kV);
+        uint16_t *vpl = vph + D * BT;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int t = 16 * mt + g + 8 * hf, v = v0 + 8 * nt + 2 * t4 + e;
+                    const float x = -(us[((t >> 2) * D + v) * 4 + (t & 3)] + wsv[nt][2 * hf + e]);
+                    uint16_t xh, xl;
+                    split1(x, xh, xl);
+                    vph[fr<D>(v, t)] = xh;
+                    vpl[fr<D>(v, t)] = xl;
+                }
+    }
+    __syncthreads();
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {    // Aqk v': K = tokens
         uint32_t ah[4], al[4];
