@@ -52,6 +52,7 @@
 #include <cuda.h>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 
 namespace kda {
@@ -391,6 +392,83 @@ struct ScanOut {
 };
 template <int R>
 __device__ __forceinline__ int fr(int r, int c) { return ((c >> 3) * R + r) * 8 + (c & 7); }
+
+// Split path, segmented scan. The state recurrence of one (sequence, head) is
+// affine, S_{c+1} = A_c S_c + B_c (A_c = diag(e^{gl}) - KD^T W, B_c = KD^T u),
+// so a long sequence is cut into P segments of about L chunks that scan side
+// by side: segment 0 from the true initial state, and segments 1..P-2 twice,
+// once from zero (their B) and once from the identity with u = 0 (their A).
+// A combine step then chains S_start[i+1] = A_i S_start[i] + B_i, and segments
+// 1..P-1 rescan from their true start states, storing the splits the output
+// kernel reads. Two segments gain nothing, so a sequence has 1 or >= 3.
+//
+// The plan (int32 words in the workspace, written by plan_kernel):
+//   [0] state-slot capacity, [1] first-pass task count, [2] rescan task
+//   count, [3] task capacity, then per request: segments P_r, segment length
+//   L_r (chunks), first state slot; then the first-pass and rescan task lists.
+// A task is req | kind << 10 | segment << 12.
+enum : int { kTaskTrue = 0, kTaskZero = 1, kTaskIdent = 2 };
+constexpr int kMinSegChunks = 8;
+struct PlanView {
+    int32_t *w;
+    int R, cap;
+    __host__ __device__ PlanView(int32_t *words, int num_req, int task_cap) : w(words), R(num_req), cap(task_cap) {}
+    __device__ int32_t *segs() const { return w + 4; }
+    __device__ int32_t *seglen() const { return w + 4 + R; }
+    __device__ int32_t *sbase() const { return w + 4 + 2 * R; }
+    __device__ int32_t *tasks(int phase) const { return w + 4 + 3 * R + phase * cap; }
+    __host__ __device__ static size_t words(int num_req, int task_cap) {
+        return 4 + 3 * static_cast<size_t>(num_req) + 2 * static_cast<size_t>(task_cap);
+    }
+};
+__device__ __forceinline__ int32_t task_word(int req, int kind, int seg) { return req | (kind << 10) | (seg << 12); }
+// State exchange layout of one D x D fp32 state S^T (value row v, key column
+// k): float at ((k / 4) D + v) * 4 + k % 4, so a warp's 32 rows of one float4
+// column are 512 contiguous bytes. Slot `slot` of kind `which` (0 start
+// states, 1 segment B, 2 segment A) for head hl:
+template <int D>
+__device__ __forceinline__ float *state_slot(float *states, int cap, int heads, int which, int slot, int hl) {
+    return states + ((static_cast<int64_t>(which) * cap + slot) * heads + hl) * (D * D);
+}
+
+// Exclusive prefix sum over a 1024-thread block (one value per thread); the
+// total lands in `total`. Every thread of the block must call it.
+__device__ int block_scan(int x, int32_t *tmp, int &total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int v = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+    }
+    if (lane == 31) tmp[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        int w = tmp[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        tmp[lane] = w;
+    }
+    __syncthreads();
+    const int before = (warp > 0 ? tmp[warp - 1] : 0) + v - x;
+    total = tmp[31];
+    __syncthreads();
+    return before;
+}
+__device__ int block_max(int x, int32_t *tmp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x = max(x, __shfl_xor_sync(0xffffffffu, x, o));
+    if (lane == 0) tmp[warp] = x;
+    __syncthreads();
+    int m = tmp[0];
+    for (int i = 1; i < 32; ++i) m = max(m, tmp[i]);
+    __syncthreads();
+    return m;
+}
 
 // Block pair index p -> (I, J), J <= I, in the order (0,0) (1,0) (1,1) (2,0) ...
 __device__ __forceinline__ void pair_ij(int p, int &I, int &J) {
@@ -1431,8 +1509,8 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 // ---------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(kThreads + 32, 1)
-    chunk_scan_kernel(const KdaArgs p, const int32_t *order, const __grid_constant__ TmaMaps maps,
-                      const uint8_t *rec, const uint8_t *trec, const int32_t *cbase, uint8_t *sout) {
+    chunk_scan_kernel(const KdaArgs p, const int32_t *plan, int phase, const __grid_constant__ TmaMaps maps,
+                      const uint8_t *rec, const uint8_t *trec, const int32_t *cbase, uint8_t *sout, float *states) {
     using L = Smem<D>;
     using R = Rec<D>;
     constexpr int KS = D / 16;
@@ -1454,9 +1532,15 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     const uint32_t s_base = smem_addr(sm);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rr = blockIdx.x / p.head_count;
+    const int ti = blockIdx.x / p.head_count;
     const int hl = blockIdx.x % p.head_count, h = p.head_begin + hl;
-    const int req = order != nullptr ? order[rr] : rr;
+    if (ti >= plan[1 + phase]) return;
+    const PlanView pv(const_cast<int32_t *>(plan), p.num_req, plan[3]);
+    const int32_t task = pv.tasks(phase)[ti];
+    const int req = task & 1023, kind = (task >> 10) & 3, seg = task >> 12;
+    const int nseg = pv.segs()[req], seglen = pv.seglen()[req];
+    const bool truth = kind == kTaskTrue;
+    const int slot_cap = plan[0];
     const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
     const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
     const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
@@ -1469,7 +1553,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         return;
     }
     int64_t tslot = 0, tlen = -1;
-    if (p.track_indices != nullptr) {
+    if (p.track_indices != nullptr && truth) {
         tslot = load_index(p.track_indices, p.index_bytes[2], req);
         if (tslot < 0 || tslot >= p.num_slots) {
             if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
@@ -1477,22 +1561,27 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         }
         if (tslot > 0) tlen = load_index(p.track_lens, p.index_bytes[3], req);
     }
-    const int nchunks = static_cast<int>((eos - bos + BT - 1) / BT);
+    // This task's chunks [c0, c0 + nchunks) of the request; below, chunk
+    // indices are relative to c0.
+    const int req_chunks = static_cast<int>((eos - bos + BT - 1) / BT);
+    const int c0 = seg * seglen;
+    const int nchunks = max(0, min(req_chunks, c0 + seglen) - c0);
     const int64_t s0 = p.state_stride[0], s1 = p.state_stride[1], sk = p.state_stride[2], sv = p.state_stride[3];
-    auto chunk_rows = [&](int c) {
-        const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
-        return static_cast<int>(eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT));
-    };
     auto trk_at = [&](int c) {
-        const int64_t rt = tlen - static_cast<int64_t>(c) * BT;
+        const int64_t rt = tlen - static_cast<int64_t>(c0 + c) * BT;
         return tslot > 0 && rt > 0 && rt <= BT;
     };
     auto rec_of = [&](int c) {
-        return rec + (static_cast<int64_t>(cbase[req] + c) * p.head_count + hl) * R::kBytes;
+        return rec + (static_cast<int64_t>(cbase[req] + c0 + c) * p.head_count + hl) * R::kBytes;
     };
     auto sout_of = [&](int c) {
-        return sout + (static_cast<int64_t>(cbase[req] + c) * p.head_count + hl) * ScanOut<D>::kBytes;
+        return sout + (static_cast<int64_t>(cbase[req] + c0 + c) * p.head_count + hl) * ScanOut<D>::kBytes;
     };
+    // Exchange slots of this request's segment boundaries (segment sg >= 1).
+    auto xslot = [&](int which, int sg) {
+        return state_slot<D>(states, slot_cap, p.head_count, which, pv.sbase()[req] + sg - 1, hl);
+    };
+    const bool use_u = kind != kTaskIdent;
     const uint8_t *trk_rec = trec + (static_cast<int64_t>(req) * p.head_count + hl) * R::tBytes;
 
     if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
@@ -1526,8 +1615,10 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 bulk_g2s(sm + L::kRawQ, trk_rec + R::tKR, BT * D * 4, lTR);
                 bulk_g2s(vec + L::vEtr, trk_rec + R::tEtr, D * 4, lTR);
             };
-            load(lU0, sm + L::kRawG, rec_of(0) + R::kU, BT * D * 4);
-            if (nchunks > 1) load(lU1, sm + L::kY, rec_of(1) + R::kU, BT * D * 4);
+            if (use_u) {
+                load(lU0, sm + L::kRawG, rec_of(0) + R::kU, BT * D * 4);
+                if (nchunks > 1) load(lU1, sm + L::kY, rec_of(1) + R::kU, BT * D * 4);
+            }
             load(lEgl, vec + L::vEgl, rec_of(0) + R::kEgl, D * 4);
             load(lW, sm + L::kX, rec_of(0) + R::kW, BT * D * 4);
             load(lKD, sm + L::kZ, rec_of(0) + R::kKD, BT * D * 4);
@@ -1541,7 +1632,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 pwait(sSplit, ph);
                 // -u^T of chunk c was copied into NU before the split: its slot
                 // takes chunk c + 2.
-                if (c + 2 < nchunks)
+                if (use_u && c + 2 < nchunks)
                     load((c & 1) ? lU1 : lU0, sm + ((c & 1) ? L::kY : L::kRawG), rec_of(c + 2) + R::kU, BT * D * 4);
                 pwait(lW, ph);
                 tc_fence_after();
@@ -1597,18 +1688,37 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     } else {
         // ===== compute warps 0..15 =====
         auto cbar = [] { nbar(1, kThreads); };
-        // Initial state S^T -> tensor memory; a length-0 checkpoint is the initial state.
+        // Initial state S^T -> tensor memory: the pool slot (a length-0
+        // checkpoint is the initial state), a segment's exchanged start state,
+        // zero, or the identity.
         {
-            const float *hs = p.state + slot * s0 + h * s1;
-            float *ts = p.state + tslot * s0 + h * s1;
             const bool row_ok = srow < D;
             uint32_t r[SC];
+            if (truth && seg == 0) {
+                const float *hs = p.state + slot * s0 + h * s1;
+                float *ts = p.state + tslot * s0 + h * s1;
 #pragma unroll
-            for (int e = 0; e < SC; ++e) {
-                const int k = SC * cs + e;
-                const float x = (slot > 0 && row_ok) ? hs[srow * sv + k * sk] : 0.f;
-                r[e] = __float_as_uint(x);
-                if (row_ok && tslot > 0 && tlen == 0) ts[srow * sv + k * sk] = x;
+                for (int e = 0; e < SC; ++e) {
+                    const int k = SC * cs + e;
+                    const float x = (slot > 0 && row_ok) ? hs[srow * sv + k * sk] : 0.f;
+                    r[e] = __float_as_uint(x);
+                    if (row_ok && tslot > 0 && tlen == 0) ts[srow * sv + k * sk] = x;
+                }
+            } else if (truth) {
+                const float *xs = xslot(0, seg);
+#pragma unroll
+                for (int e = 0; e < SC / 4; ++e) {
+                    const float4 x = row_ok ? *reinterpret_cast<const float4 *>(xs + ((SC / 4 * cs + e) * D + srow) * 4)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                    r[4 * e] = __float_as_uint(x.x);
+                    r[4 * e + 1] = __float_as_uint(x.y);
+                    r[4 * e + 2] = __float_as_uint(x.z);
+                    r[4 * e + 3] = __float_as_uint(x.w);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < SC; ++e)
+                    r[e] = __float_as_uint(kind == kTaskIdent && row_ok && SC * cs + e == srow ? 1.f : 0.f);
             }
             tmem_st<SC>(tq + kColS + SC * cs, r);
             tmem_st_wait();
@@ -1618,14 +1728,16 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         };
         // NU <- -u^T of chunk c (this warp's 16 token columns of value row srow);
         // the copy reaches G2 through the wait, fence and barrier before sSplit.
+        // A transfer chain (identity start) has u = 0.
         auto init_nu = [&](int c) {
-            cwait((c & 1) ? lU1 : lU0, static_cast<uint32_t>((c >> 1) & 1));
+            if (use_u) cwait((c & 1) ? lU1 : lU0, static_cast<uint32_t>((c >> 1) & 1));
             const float *us = (c & 1) ? Us1 : Us0;
             uint32_t r[16];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const float4 u4 = srow < D ? *reinterpret_cast<const float4 *>(us + ((4 * cs + k) * D + srow) * 4)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 u4 = use_u && srow < D
+                                      ? *reinterpret_cast<const float4 *>(us + ((4 * cs + k) * D + srow) * 4)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
                 r[4 * k] = __float_as_uint(u4.x);
                 r[4 * k + 1] = __float_as_uint(u4.y);
                 r[4 * k + 2] = __float_as_uint(u4.z);
@@ -1656,7 +1768,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             if (tid == 0) mbar_arrive(sSplit);   // S split, NU = -u^T, -u^T slot read
             // (2) while W S runs: the chunk-start state for the output kernel,
             // (value row, keys), and S^T <- S^T e^{gl} (deferred on a tracked chunk).
-            if (srow < D) {
+            if (truth && srow < D) {
                 uint16_t *sh = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kSH);
                 uint16_t *sl = reinterpret_cast<uint16_t *>(sout_of(c) + ScanOut<D>::kSL);
 #pragma unroll
@@ -1730,15 +1842,28 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
         }
-        // Final state S^T -> pool slot (padding slot 0 is never written).
+        // Final state S^T: the last segment's goes to the pool slot (padding
+        // slot 0 is never written); segment 0 of a segmented request hands its
+        // end state to segment 1; the first-pass chains leave B and A.
         {
-            float *hs = p.state + slot * s0 + h * s1;
             uint32_t r[SC];
             tmem_ld<SC>(tq + kColS + SC * cs, r);
             tmem_ld_wait();
-            if (slot > 0 && srow < D) {
+            if (truth && seg == nseg - 1) {
+                float *hs = p.state + slot * s0 + h * s1;
+                if (slot > 0 && srow < D) {
 #pragma unroll
-                for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
+                    for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
+                }
+            } else if (!truth || seg == 0) {
+                float *xs = truth ? xslot(0, 1) : xslot(kind, seg);
+                if (srow < D) {
+#pragma unroll
+                    for (int e = 0; e < SC / 4; ++e)
+                        *reinterpret_cast<float4 *>(xs + ((SC / 4 * cs + e) * D + srow) * 4) =
+                            make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                        __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+                }
             }
         }
     }
@@ -1747,6 +1872,105 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// Split path, segmented scan, the combine step: one CTA per (request, head)
+// with >= 3 segments chains the start states through the first pass's
+// segment transfers, S_start[i+1]^T = S_start[i]^T A_i^T + B_i^T for
+// i = 1 .. P-2 (S_start[1] is segment 0's end state). Each step is a D x D x D
+// split-bf16 mma.sync product with the B term as the accumulator's start; the
+// new start state stays in shared memory (bf16 hi/lo) for the next step.
+template <int D>
+struct CombSmem {
+    static constexpr int kSh = 0;                      // S^T hi/lo, swizzled [v][j]
+    static constexpr int kSl = kSh + D * D * 2;
+    static constexpr int kXh = kSl + D * D * 2;        // A^T hi/lo, swizzled [j][k]
+    static constexpr int kXl = kXh + D * D * 2;
+    static constexpr int kAlloc = kXl + D * D * 2 + 1024;
+};
+
+// fp32 state (exchange layout) -> bf16 hi/lo swizzled row-major tile in shared memory.
+template <int D>
+__device__ __forceinline__ void state_to_tile(const float *src, unsigned char *hi, unsigned char *lo) {
+    for (int q = threadIdx.x; q < D * D / 4; q += blockDim.x) {
+        const int row = q % D, c4 = q / D;
+        const float4 x = *reinterpret_cast<const float4 *>(src + static_cast<int64_t>(q) * 4);
+        uint32_t h0, h1, l0, l1;
+        split2(x.x, x.y, h0, l0);
+        split2(x.z, x.w, h1, l1);
+        const int o = swz<D>(row, 4 * c4) * 2;
+        *reinterpret_cast<uint2 *>(hi + o) = make_uint2(h0, h1);
+        *reinterpret_cast<uint2 *>(lo + o) = make_uint2(l0, l1);
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) chunk_combine_kernel(const KdaArgs p, const int32_t *plan,
+                                                                float *states) {
+    using M = CombSmem<D>;
+    constexpr int MT = D / 16;                 // 16-row tiles
+    constexpr int WPR = 16 / MT;               // warps per row tile
+    constexpr int NC = D / WPR;                // columns per warp
+    constexpr int NT = NC / 8;                 // 8-column n-tiles per warp
+    extern __shared__ __align__(1024) unsigned char sm_raw[];
+    unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
+    const uint32_t s_base = smem_addr(sm);
+    const int req = blockIdx.x / p.head_count, hl = blockIdx.x % p.head_count;
+    const PlanView pv(const_cast<int32_t *>(plan), p.num_req, plan[3]);
+    const int P = pv.segs()[req];
+    if (P < 3) return;
+    const int cap = plan[0], sb = pv.sbase()[req];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int mt = warp % MT, n0 = (warp / MT) * NC;
+    float acc[NT][4];
+    state_to_tile<D>(state_slot<D>(states, cap, p.head_count, 0, sb, hl), sm + M::kSh, sm + M::kSl);
+    for (int i = 1; i + 1 < P; ++i) {
+        // slot sb + i - 1 holds segment i's B and A; the result is start state i + 1
+        state_to_tile<D>(state_slot<D>(states, cap, p.head_count, 2, sb + i - 1, hl), sm + M::kXh, sm + M::kXl);
+        const float *bt = state_slot<D>(states, cap, p.head_count, 1, sb + i - 1, hl);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int v = 16 * mt + g + 8 * hf, k = n0 + 8 * nt + 2 * t4;
+                const float2 b = *reinterpret_cast<const float2 *>(bt + ((k >> 2) * D + v) * 4 + (k & 3));
+                acc[nt][2 * hf] = b.x;
+                acc[nt][2 * hf + 1] = b.y;
+            }
+        __syncthreads();
+#pragma unroll 2
+        for (int ks = 0; ks < D / 16; ++ks) {
+            uint32_t ah[4], al[4];
+            ldsm_x4(ah, s_base + M::kSh + 2 * lda_a<D>(lane, 16 * mt, 16 * ks));
+            ldsm_x4(al, s_base + M::kSl + 2 * lda_a<D>(lane, 16 * mt, 16 * ks));
+#pragma unroll
+            for (int np = 0; np < NT / 2; ++np) {
+                uint32_t bh[4], bl[4];
+                ldsm_x4_t(bh, s_base + M::kXh + 2 * lda_b_kn<D>(lane, 16 * ks, n0 + 16 * np));
+                ldsm_x4_t(bl, s_base + M::kXl + 2 * lda_b_kn<D>(lane, 16 * ks, n0 + 16 * np));
+                mma3(acc[2 * np], ah, al, bh[0], bh[1], bl[0], bl[1]);
+                mma3(acc[2 * np + 1], ah, al, bh[2], bh[3], bl[2], bl[3]);
+            }
+        }
+        __syncthreads();
+        float *out = state_slot<D>(states, cap, p.head_count, 0, sb + i, hl);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int v = 16 * mt + g + 8 * hf, k = n0 + 8 * nt + 2 * t4;
+                const float x0 = acc[nt][2 * hf], x1 = acc[nt][2 * hf + 1];
+                *reinterpret_cast<float2 *>(out + ((k >> 2) * D + v) * 4 + (k & 3)) = make_float2(x0, x1);
+                uint32_t hi2, lo2;
+                split2(x0, x1, hi2, lo2);
+                const int o = swz<D>(v, k) * 2;
+                *reinterpret_cast<uint32_t *>(sm + M::kSh + o) = hi2;
+                *reinterpret_cast<uint32_t *>(sm + M::kSl + o) = lo2;
+            }
+        // The next step's A^T conversion overwrites only the X tiles; its
+        // barrier orders these S writes before the next products read them.
     }
 }
 
@@ -1910,18 +2134,69 @@ __global__ void __launch_bounds__(kThreads) chunk_out_kernel(const KdaArgs p, co
     }
 }
 
-// Chunk slot offsets of the split path: cbase[r] = chunks of requests < r
-// (num_req + 1 entries). One thread; the split path serves few requests.
-__global__ void chunk_base_kernel(const KdaArgs p, int32_t *cbase) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    int32_t acc = 0;
-    for (int r = 0; r < p.num_req; ++r) {
-        cbase[r] = acc;
+// Split-path plan, one thread per request (num_req <= 1024): the chunk slot
+// offsets cbase[r] (chunks of requests < r, num_req + 1 entries) and the
+// segmentation. The segment length is the shortest (>= kMinSegChunks) whose
+// first pass fits `budget` CTAs per head, so that pass runs in one wave.
+__global__ void __launch_bounds__(1024) plan_kernel(const KdaArgs p, int32_t *cbase, int32_t *plan, int budget,
+                                                   int task_cap, int slot_cap) {
+    __shared__ int32_t tmp[32];
+    const int r = threadIdx.x;
+    const bool live = r < p.num_req;
+    int n = 0;
+    if (live) {
         const int64_t len = load_index(p.cu_seqlens, p.index_bytes[1], r + 1) -
                             load_index(p.cu_seqlens, p.index_bytes[1], r);
-        acc += static_cast<int32_t>(len > 0 ? (len + BT - 1) / BT : 0);
+        n = static_cast<int>(len > 0 ? (len + BT - 1) / BT : 0);
     }
-    cbase[p.num_req] = acc;
+    int total;
+    const int cb = block_scan(n, tmp, total);
+    if (live) cbase[r] = cb;
+    if (r == 0) cbase[p.num_req] = total;
+    auto segs = [&](int L) { return n <= L ? 1 : max(3, (n + L - 1) / L); };
+    auto cost = [&](int L) {
+        const int P = segs(L);
+        return live ? (P == 1 ? 1 : 2 * P - 3) : 0;
+    };
+    const int maxn = block_max(n, tmp);
+    int hi = max(maxn, kMinSegChunks), lo = kMinSegChunks;
+    int t;
+    block_scan(cost(lo), tmp, t);
+    if (t > budget) {
+        // Binary search for the shortest segment whose first pass fits.
+        while (lo < hi) {
+            const int mid = (lo + hi) / 2;
+            block_scan(cost(mid), tmp, t);
+            if (t <= budget) hi = mid;
+            else lo = mid + 1;
+        }
+    } else {
+        hi = lo;
+    }
+    const int L = hi;
+    const PlanView pv(plan, p.num_req, task_cap);
+    const int P = live ? segs(L) : 0;
+    int na, nc;
+    const int oa = block_scan(live ? (P == 1 ? 1 : 2 * P - 3) : 0, tmp, na);
+    const int oc = block_scan(P >= 3 ? P - 1 : 0, tmp, nc);
+    if (live) {
+        pv.segs()[r] = P;
+        pv.seglen()[r] = (n + P - 1) / P;
+        pv.sbase()[r] = oc;
+        int32_t *ta = pv.tasks(0), *tc = pv.tasks(1);
+        ta[oa] = task_word(r, kTaskTrue, 0);
+        for (int sg = 1; sg + 1 < P; ++sg) {
+            ta[oa + 2 * sg - 1] = task_word(r, kTaskZero, sg);
+            ta[oa + 2 * sg] = task_word(r, kTaskIdent, sg);
+        }
+        for (int sg = 1; sg < P && P >= 3; ++sg) tc[oc + sg - 1] = task_word(r, kTaskTrue, sg);
+    }
+    if (r == 0) {
+        plan[0] = slot_cap;
+        plan[1] = na;
+        plan[2] = nc;
+        plan[3] = task_cap;
+    }
 }
 
 }  // namespace chunk
@@ -2043,8 +2318,13 @@ static bool want_split(int32_t num_req, int32_t heads, int32_t num_tokens) {
 
 static size_t a256(size_t x) { return (x + 255) / 256 * 256; }
 
+// Split-path workspace: chunk offsets, the segmentation plan, the per-chunk
+// records, the tracked-prefix records, the state splits for the output
+// kernel, and the segment-boundary states (start, B, A) of the segmented scan.
+// The first pass gets `budget` CTAs per head, so that it runs in one wave.
 struct SplitLayout {
-    size_t cbase, rec, trec, sout, total;
+    size_t cbase, plan, rec, trec, sout, states, total;
+    int budget, task_cap, slot_cap;
 };
 static SplitLayout split_layout(int32_t num_req, int32_t num_tokens, int32_t heads, int32_t D) {
     const size_t slots = static_cast<size_t>(num_tokens) / chunk::BT + static_cast<size_t>(num_req);
@@ -2052,11 +2332,16 @@ static SplitLayout split_layout(int32_t num_req, int32_t num_tokens, int32_t hea
     const size_t tb = D == 64 ? chunk::Rec<64>::tBytes : chunk::Rec<128>::tBytes;
     const size_t ob = D == 64 ? chunk::ScanOut<64>::kBytes : chunk::ScanOut<128>::kBytes;
     SplitLayout l;
-    l.cbase = order_bytes(num_req);
-    l.rec = l.cbase + a256((static_cast<size_t>(num_req) + 1) * sizeof(int32_t));
+    l.budget = std::max(1, sm_count() / std::max(1, static_cast<int>(heads)));
+    l.task_cap = std::max(l.budget, static_cast<int>(num_req));
+    l.slot_cap = l.budget;
+    l.cbase = 0;
+    l.plan = a256((static_cast<size_t>(num_req) + 1) * sizeof(int32_t));
+    l.rec = l.plan + a256(chunk::PlanView::words(num_req, l.task_cap) * sizeof(int32_t));
     l.trec = l.rec + slots * static_cast<size_t>(heads) * rb;
     l.sout = l.trec + static_cast<size_t>(num_req) * static_cast<size_t>(heads) * tb;
-    l.total = l.sout + slots * static_cast<size_t>(heads) * ob;
+    l.states = l.sout + slots * static_cast<size_t>(heads) * ob;
+    l.total = l.states + 3 * static_cast<size_t>(l.slot_cap) * static_cast<size_t>(heads) * D * D * sizeof(float);
     return l;
 }
 
@@ -2065,22 +2350,30 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
     using L = chunk::Smem<D>;
     chunk::TmaMaps maps;
     if (!encode_maps(maps, a, D, MODE == KDA_GATE_RAW)) return KDA_ERR_LAUNCH;
-    static bool opted_prep[64], opted_scan[64], opted_out[64];
+    static bool opted_prep[64], opted_scan[64], opted_comb[64], opted_out[64];
     if (!opt_in(chunk::chunk_kernel<D, MODE, true>, opted_prep, L::kAlloc) ||
         !opt_in(chunk::chunk_scan_kernel<D>, opted_scan, L::kAlloc) ||
+        !opt_in(chunk::chunk_combine_kernel<D>, opted_comb, chunk::CombSmem<D>::kAlloc) ||
         !opt_in(chunk::chunk_out_kernel<D>, opted_out, chunk::OutSmem<D>::kAlloc))
         return KDA_ERR_LAUNCH;
     const SplitLayout lay = split_layout(a->num_req, a->num_tokens, a->head_count, D);
-    int32_t *order = reinterpret_cast<int32_t *>(ws);
     int32_t *cbase = reinterpret_cast<int32_t *>(ws + lay.cbase);
+    int32_t *plan = reinterpret_cast<int32_t *>(ws + lay.plan);
     uint8_t *rec = ws + lay.rec, *trec = ws + lay.trec, *sout = ws + lay.sout;
-    chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
-    chunk::chunk_base_kernel<<<1, 32, 0, st>>>(*a, cbase);
+    float *states = reinterpret_cast<float *>(ws + lay.states);
+    chunk::plan_kernel<<<1, 1024, 0, st>>>(*a, cbase, plan, lay.budget, lay.task_cap, lay.slot_cap);
     const int64_t slots = static_cast<int64_t>(a->num_tokens) / chunk::BT + a->num_req;
     chunk::chunk_kernel<D, MODE, true><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads + 32,
                                          L::kAlloc, st>>>(*a, nullptr, maps, rec, trec, cbase);
-    chunk::chunk_scan_kernel<D><<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count),
-                                  chunk::kThreads + 32, L::kAlloc, st>>>(*a, order, maps, rec, trec, cbase, sout);
+    // Segmented scan: first pass, combine, rescan (CTAs past a phase's task
+    // count exit at once).
+    const unsigned scan_grid = static_cast<unsigned>(static_cast<int64_t>(lay.task_cap) * a->head_count);
+    chunk::chunk_scan_kernel<D><<<scan_grid, chunk::kThreads + 32, L::kAlloc, st>>>(*a, plan, 0, maps, rec, trec,
+                                                                                 cbase, sout, states);
+    chunk::chunk_combine_kernel<D><<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count),
+                                     chunk::kThreads, chunk::CombSmem<D>::kAlloc, st>>>(*a, plan, states);
+    chunk::chunk_scan_kernel<D><<<scan_grid, chunk::kThreads + 32, L::kAlloc, st>>>(*a, plan, 1, maps, rec, trec,
+                                                                                 cbase, sout, states);
     chunk::chunk_out_kernel<D><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads,
                                  chunk::OutSmem<D>::kAlloc, st>>>(*a, maps, rec, sout, cbase);
     return KDA_OK;

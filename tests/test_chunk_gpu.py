@@ -168,6 +168,27 @@ def test_loggate_matches_oracle(ops):
     assert_state_close(d.pool.cpu()[1:], ref_pool[1:])
 
 
+# Requests long enough (and heads few enough) that the split path cuts them
+# into segments: a first pass from zero and from the identity per segment, the
+# combine of the segment transfers, and a rescan from the true start states.
+# Mixed with short requests that stay whole; checkpoints at 0, inside segment
+# 0, on a segment boundary, inside a middle and the last segment, at the end.
+SEGMENTED = [
+    (2, [0, 3000], [1], None),
+    (1, [0, 3000, 3001, 5500, 6100, 8100], [1, 0, 2, 3, 7], ([4, 0, 5, 6, 0], [1024, 0, 2300, 300, 0])),
+    (2, [0, 1500, 2800], [1, 2], ([3, 4], [0, 1300])),
+    (3, [0, 1111, 1175], [2, 1], ([5, 6], [100, 64])),
+]
+
+
+@pytest.mark.parametrize("heads,cu_seqlens,slots,track", SEGMENTED, ids=lambda x: str(x))
+@pytest.mark.parametrize("D", (64, 128))
+def test_segmented_scan_matches_oracle(ops, heads, cu_seqlens, slots, track, D):
+    kw = _case(heads, cu_seqlens, slots, track, seed=len(cu_seqlens) + D, D=D)
+    touched = {s for s in slots if s > 0} | ({s for s in track[0] if s > 0} if track else set())
+    _check(ops, kw, touched)
+
+
 def test_cfg3_full_size(ops):
     """8 sequences (33,494 tokens, none a multiple of 64), H=32.
 
