@@ -132,8 +132,10 @@ int kda_recurrent_launch(const KdaArgs *args, void *stream);
 /* Bytes of device workspace kda_chunk_launch needs for these sizes (replaces
  * kda_chunk::kWorkspaceFloatsPerBlock, kda_varlen_chunk.h:79-116). For batches
  * of few long sequences (requests x heads at most half the SM count) this is
- * the size of the split path's per-chunk operand records, ~132 KB per chunk
- * and head at D = 128; otherwise a few bytes per request. */
+ * the size of the split path's per-chunk records and state splits, ~210 KB
+ * per chunk and head at D = 128 (plus a few MB of segment-boundary states);
+ * otherwise a few bytes per request. The split-path size depends on the SM
+ * count of the current device, so query it on the device that launches. */
 size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens,
                                  int32_t num_heads, int32_t head_dim);
 
@@ -141,12 +143,14 @@ size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens,
  * workspace must be at least kda_chunk_workspace_bytes(...) bytes; its
  * contents need no initialisation. Replaces LaunchKdaVarlenChunk
  * (kda_varlen_chunk.h:143-144). `intermediate` must be NULL.
- * Two internal paths give the same results: a fused kernel (one CTA per
- * (sequence, head) through every chunk) and, for few long sequences, a prep
- * kernel over all (chunk, head) pairs followed by a scan kernel per
- * (sequence, head); the split path runs only when the workspace holds its
- * records (256-byte aligned). The environment variable KDA_CHUNK_PATH=fused
- * or =split overrides the choice. */
+ * Two internal paths give the same results within the fp32 tolerances: a
+ * fused kernel (one CTA per (sequence, head) through every chunk) and, for
+ * few long sequences, a split path: a prep kernel over all (chunk, head)
+ * pairs, a state scan that cuts long sequences into segments scanned side by
+ * side and then chained, and an output kernel over all (chunk, head) pairs.
+ * The split path runs only when the workspace holds it (256-byte aligned).
+ * The environment variable KDA_CHUNK_PATH=fused or =split overrides the
+ * choice. */
 int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes,
                      void *stream);
 
