@@ -157,8 +157,13 @@ __device__ __forceinline__ bool decode_item(const KdaArgs &p, int64_t it, int ns
 // The token loop of one item with the state rows already in registers:
 // prologue, recurrence step, output, prefix/per-step checkpoints, final
 // write-back (kda_python.py:271-307).
+template <int D, int MODE>
+__device__ __forceinline__ void token_from_stage(TokenRaw<D, MODE> &r, const unsigned char *stage, float bval,
+                                                 int sub, int row0);
+
 template <int D, int MODE, bool FAST>
-__device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float (&s)[2][D / 8], int row0, int sub) {
+__device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float (&s)[2][D / 8], int row0, int sub,
+                                         const unsigned char *stage = nullptr, float bval = 0.f) {
     constexpr int NC = D / 32;
     constexpr int NE = D / 8;
     const int h = m.h, v0 = m.v0;
@@ -184,7 +189,10 @@ __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float 
             : nullptr;
 
     TokenRaw<D, MODE> cur, nxt;
-    if (m.bos < m.eos) load_token<D, MODE>(cur, p, m.bos, h, sub, v0 + row0);
+    if (m.bos < m.eos) {
+        if (stage != nullptr) token_from_stage<D, MODE>(cur, stage, bval, sub, row0);
+        else load_token<D, MODE>(cur, p, m.bos, h, sub, v0 + row0);
+    }
 
     for (int64_t t = m.bos; t < m.eos; ++t) {
         if (t + 1 < m.eos) load_token<D, MODE>(nxt, p, t + 1, h, sub, v0 + row0);
@@ -302,63 +310,203 @@ __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float 
 }
 
 // Production layout (K-contiguous, 16-byte aligned): persistent CTAs walk the
-// items with a STAGES-deep ring of bulk-TMA state tiles, so each SM keeps
-// several 16 KiB loads in flight while it computes. Item n of a CTA uses ring
-// stage n % STAGES, whose mbarrier completes phase (n / STAGES) & 1.
-template <int D, int MODE, int STAGES>
-__global__ void __launch_bounds__(kRecThreads, 3)
-recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items) {
+// items with a STAGES-deep ring. Thread 0 fills a ring stage with everything
+// an item needs -- its 32 x D state rows and, when the token pointers are
+// 16-byte aligned, its first token's q, k, gate rows and v slice, all by bulk
+// TMA copies on the stage's mbarrier -- plus a header with the item's
+// metadata; it reads the next item's cu_seqlens and slot one refill ahead, and
+// the compute threads read beta one item ahead, so no global-memory round
+// trip sits between an item's stage landing and its arithmetic. Item n of a
+// CTA uses stage n % STAGES, whose mbarrier completes phase (n / STAGES) & 1.
+struct StageMeta {
+    int64_t bos, eos, slot, tslot, tlen;
+    int req, h, v0, ok;
+};
+template <int D, int MODE>
+struct RingStage {
+    static constexpr int QE = MODE == KDA_GATE_PREPARED ? 4 : 2;   // q, k element bytes
+    static constexpr int GE = MODE == KDA_GATE_RAW ? 2 : 4;        // gate row element bytes (a or g)
+    static constexpr int kQ = kBV * D * 4;                         // after the state rows
+    static constexpr int kK = kQ + D * QE;
+    static constexpr int kG = kK + D * QE;
+    static constexpr int kV = kG + D * GE;                         // bf16 v slice (kBV values)
+    static constexpr int kTokBytes = kV + kBV * 2 - kQ;
+    static constexpr int kMeta = (kV + kBV * 2 + 15) / 16 * 16;
+    static constexpr int kBytes = (kMeta + static_cast<int>(sizeof(StageMeta)) + 127) / 128 * 128;
+};
+
+// The first token of an item from its ring stage (beta / raw b from `bval`).
+template <int D, int MODE>
+__device__ __forceinline__ void token_from_stage(TokenRaw<D, MODE> &r, const unsigned char *stage, float bval,
+                                                 int sub, int row0) {
+    using RS = RingStage<D, MODE>;
+    constexpr int NC = D / 32;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        const int e = c * 32 + sub * 4;
+        if constexpr (MODE == KDA_GATE_PREPARED) {
+            r.qf[c] = *reinterpret_cast<const float4 *>(stage + RS::kQ + e * 4);
+            r.kf[c] = *reinterpret_cast<const float4 *>(stage + RS::kK + e * 4);
+            r.gf[c] = *reinterpret_cast<const float4 *>(stage + RS::kG + e * 4);
+        } else {
+            r.qb[c] = *reinterpret_cast<const uint2 *>(stage + RS::kQ + e * 2);
+            r.kb[c] = *reinterpret_cast<const uint2 *>(stage + RS::kK + e * 2);
+            if constexpr (MODE == KDA_GATE_LOG)
+                r.gf[c] = *reinterpret_cast<const float4 *>(stage + RS::kG + e * 4);
+            else
+                r.ab[c] = *reinterpret_cast<const uint2 *>(stage + RS::kG + e * 2);
+        }
+    }
+    const uint16_t *vs = reinterpret_cast<const uint16_t *>(stage + RS::kV);
+    r.vb[0] = vs[row0];
+    r.vb[1] = vs[row0 + 4];
+    if constexpr (MODE == KDA_GATE_RAW)
+        r.bb = static_cast<uint16_t>(__float_as_uint(bval));
+    else
+        r.beta = bval;
+}
+
+// beta (or the raw b bits, carried in a float) of token t, head h.
+template <int MODE>
+__device__ __forceinline__ float load_bval(const KdaArgs &p, int64_t t, int h) {
+    if constexpr (MODE == KDA_GATE_RAW)
+        return __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t *>(p.b)[t * p.num_heads + h]));
+    else
+        return __ldg(p.beta + t * p.num_heads + h);
+}
+
+// Index entry i (int32 or int64) of `base` -> shared memory, asynchronously.
+__device__ __forceinline__ void cp_async_index(int64_t *dst, const void *base, int bytes, int64_t i) {
+    const char *src = static_cast<const char *>(base) + i * bytes;
+    if (bytes == 8)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ int64_t read_index(const int64_t *src, int bytes) {
+    return bytes == 8 ? *src : static_cast<int64_t>(*reinterpret_cast<const int32_t *>(src));
+}
+
+template <int D, int MODE, int STAGES, int MINB>
+__global__ void __launch_bounds__(kRecThreads, MINB)
+recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bulk) {
+    using RS = RingStage<D, MODE>;
     constexpr int NC = D / 32;
     constexpr uint32_t kTileBytes = kBV * D * sizeof(float);
-    extern __shared__ __align__(128) float ring[];            // STAGES x kBV x D
+    extern __shared__ __align__(128) unsigned char ring[];    // STAGES x RS::kBytes
     __shared__ __align__(8) uint64_t bars[STAGES];
+    __shared__ __align__(8) int64_t pre[3];                   // next issue's bos, eos, slot
 
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int sub = lane & 7, rq = lane >> 3;
     const int row0 = warp * kRowsPerWarp + rq;
     const int64_t first = blockIdx.x, stride = gridDim.x;
+    auto meta_of = [&](int st) { return reinterpret_cast<StageMeta *>(ring + st * RS::kBytes + RS::kMeta); };
 
-    // Thread 0 fills ring stage `st` with item `it` (or just arrives when the
-    // item has no state to read), so the stage's phase always completes.
+    // Thread 0: cu_seqlens and slot of the next item to issue, copied into
+    // shared memory one refill ahead of the issue.
+    auto prefetch = [&](int64_t it) {
+        if (it >= num_items) return;
+        const int req = static_cast<int>(it / nslice / p.head_count);
+        cp_async_index(&pre[0], p.cu_seqlens, p.index_bytes[1], req);
+        cp_async_index(&pre[1], p.cu_seqlens, p.index_bytes[1], req + 1);
+        cp_async_index(&pre[2], p.indices, p.index_bytes[0], req);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // Thread 0 fills stage `st` with item `it` (a plain arrive when nothing is
+    // copied, so the stage's phase always completes), then prefetches the
+    // metadata of the item it issues next (it + stride).
     auto issue = [&](int64_t it, int st) {
         if (it >= num_items) return;
+        unsigned char *stage = ring + st * RS::kBytes;
         int64_t x = it / nslice;
-        const int h = p.head_begin + static_cast<int>(x % p.head_count);
-        const int req = static_cast<int>(x / p.head_count);
-        const int v0 = static_cast<int>(it % nslice) * kBV;
-        const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
-        if (slot > 0 && slot < p.num_slots) {
-            mbar_arrive_expect_tx(&bars[st], kTileBytes);
-            bulk_g2s(ring + static_cast<size_t>(st) * kBV * D,
-                     p.state + slot * p.state_stride[0] + h * p.state_stride[1] + static_cast<int64_t>(v0) * D,
-                     kTileBytes, &bars[st]);
+        StageMeta m;
+        m.h = p.head_begin + static_cast<int>(x % p.head_count);
+        m.req = static_cast<int>(x / p.head_count);
+        m.v0 = static_cast<int>(it % nslice) * kBV;
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        m.bos = read_index(&pre[0], p.index_bytes[1]);
+        m.eos = read_index(&pre[1], p.index_bytes[1]);
+        m.slot = read_index(&pre[2], p.index_bytes[0]);
+        m.tslot = 0;
+        m.tlen = -1;
+        m.ok = 1;
+        if (m.bos < 0 || m.eos < m.bos || m.eos > p.num_tokens) {
+            report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
+            m.ok = 0;
+        } else if (m.slot < 0 || m.slot >= p.num_slots) {
+            report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+            m.ok = 0;
+        } else if (p.track_indices != nullptr) {
+            m.tslot = load_index(p.track_indices, p.index_bytes[2], m.req);
+            if (m.tslot < 0 || m.tslot >= p.num_slots) {
+                report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+                m.ok = 0;
+            } else if (m.tslot > 0) {
+                m.tlen = load_index(p.track_lens, p.index_bytes[3], m.req);
+            }
+        }
+        *meta_of(st) = m;
+        const bool st_in = m.ok && m.slot > 0;
+        const bool tk_in = m.ok && tok_bulk && m.bos < m.eos;
+        const uint32_t bytes = (st_in ? kTileBytes : 0u) + (tk_in ? static_cast<uint32_t>(RS::kTokBytes) : 0u);
+        if (bytes > 0) {
+            mbar_arrive_expect_tx(&bars[st], bytes);
+            if (st_in)
+                bulk_g2s(stage,
+                         p.state + m.slot * p.state_stride[0] + m.h * p.state_stride[1] + static_cast<int64_t>(m.v0) * D,
+                         kTileBytes, &bars[st]);
+            if (tk_in) {
+                const int64_t row = m.bos * p.num_heads + m.h;
+                const uint8_t *gsrc = MODE == KDA_GATE_RAW ? static_cast<const uint8_t *>(p.a)
+                                                           : reinterpret_cast<const uint8_t *>(p.g);
+                bulk_g2s(stage + RS::kQ, static_cast<const uint8_t *>(p.q) + row * D * RS::QE, D * RS::QE, &bars[st]);
+                bulk_g2s(stage + RS::kK, static_cast<const uint8_t *>(p.k) + row * D * RS::QE, D * RS::QE, &bars[st]);
+                bulk_g2s(stage + RS::kG, gsrc + row * D * RS::GE, D * RS::GE, &bars[st]);
+                bulk_g2s(stage + RS::kV, static_cast<const uint8_t *>(p.v) + (row * D + m.v0) * 2, kBV * 2, &bars[st]);
+            }
         } else {
             asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&bars[st])) : "memory");
         }
+        prefetch(it + stride);
     };
 
     if (tid == 0) {
 #pragma unroll
         for (int st = 0; st < STAGES; ++st) mbar_init(&bars[st], 1);
         fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
+        prefetch(first);
 #pragma unroll
         for (int st = 0; st < STAGES; ++st) issue(first + st * stride, st);
     }
+    __syncthreads();   // the prologue stages' headers are written
 
-    int n = 0;
-    for (int64_t it = first; it < num_items; it += stride, ++n) {
-        const int st = n % STAGES;
-        const uint32_t phase = (n / STAGES) & 1;
-        Item m;
-        const bool ok = decode_item(p, it, nslice, m);
+    // beta of the first item; later items' are read one item ahead.
+    float bcur = 0.f;
+    if (first < num_items) {
+        const StageMeta m0 = *meta_of(0);
+        if (m0.ok && m0.bos < m0.eos) bcur = load_bval<MODE>(p, m0.bos, m0.h);
+    }
+    int st = 0;              // item n's stage, n % STAGES
+    uint32_t phase = 0;      // (n / STAGES) & 1
+    for (int64_t it = first; it < num_items; it += stride) {
         if (!mbar_wait(&bars[st], phase, p.status)) return;
+        const unsigned char *stage = ring + st * RS::kBytes;
+        const StageMeta sm = *meta_of(st);
+        Item m;
+        m.req = sm.req;
+        m.h = sm.h;
+        m.v0 = sm.v0;
+        m.bos = sm.bos;
+        m.eos = sm.eos;
+        m.slot = sm.slot;
+        m.tslot = sm.tslot;
+        m.tlen = sm.tlen;
+        const bool ok = sm.ok != 0;
         float s[2][D / 8];
         if (ok && m.slot > 0) {
-            const float *tile = ring + static_cast<size_t>(st) * kBV * D;
+            const float *tile = reinterpret_cast<const float *>(stage);
 #pragma unroll
             for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -371,11 +519,22 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items) {
 #pragma unroll
                 for (int e = 0; e < D / 8; ++e) s[j][e] = 0.f;
         }
-        // Every thread has its rows in registers: refill this stage now so the
-        // load overlaps this item's arithmetic.
+        // beta of the next item (its header was written and published by a
+        // barrier at least one item ago).
+        float bnext = 0.f;
+        const int st_next = st + 1 == STAGES ? 0 : st + 1;
+        if (it + stride < num_items) {
+            const StageMeta mn = *meta_of(st_next);
+            if (mn.ok && mn.bos < mn.eos) bnext = load_bval<MODE>(p, mn.bos, mn.h);
+        }
+        if (ok) run_item<D, MODE, true>(p, m, s, row0, sub, tok_bulk ? stage : nullptr, bcur);
+        // The stage's rows and token have been read: refill it, STAGES - 1
+        // items ahead of its next use.
         __syncthreads();
         if (tid == 0) issue(it + STAGES * stride, st);
-        if (ok) run_item<D, MODE, true>(p, m, s, row0, sub);
+        bcur = bnext;
+        if (st_next == 0) phase ^= 1u;
+        st = st_next;
     }
 }
 
@@ -470,7 +629,14 @@ static bool mid_fast(const KdaArgs *a) {
            a->mid_stride[0] % 4 == 0 && a->mid_stride[1] % 4 == 0 && a->mid_stride[2] % 4 == 0;
 }
 
-constexpr int kRingStages = 4;
+// Ring depth and resident CTAs per SM (three: shared memory holds three CTAs
+// of four 17 KiB stages; a three-stage ring at four CTAs per SM measured
+// slower).
+template <int MODE>
+struct RingShape {
+    static constexpr int kStages = 4;
+    static constexpr int kMinBlocks = 3;
+};
 
 struct DeviceInfo {
     int sms = 0;
@@ -494,7 +660,7 @@ static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st) {
     const int nslice = D / kBV;
     const int64_t items = static_cast<int64_t>(a->num_req) * a->head_count * nslice;
     if (fast) {
-        constexpr size_t smem = static_cast<size_t>(kRingStages) * kBV * D * sizeof(float);
+        constexpr size_t smem = static_cast<size_t>(RingShape<MODE>::kStages) * RingStage<D, MODE>::kBytes;
         // Per device: opt in to the dynamic shared memory once and cache the
         // resident-CTA count the grid is sized from (a multiple of the SMs).
         static int per_sm[64];
@@ -502,17 +668,21 @@ static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st) {
         cudaGetDevice(&dev);
         dev = (dev >= 0 && dev < 64) ? dev : 0;
         if (per_sm[dev] == 0) {
-            cudaFuncSetAttribute(recurrent_ring_kernel<D, MODE, kRingStages>,
+            cudaFuncSetAttribute(recurrent_ring_kernel<D, MODE, RingShape<MODE>::kStages, RingShape<MODE>::kMinBlocks>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
             int n = 0;
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, recurrent_ring_kernel<D, MODE, kRingStages>,
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, recurrent_ring_kernel<D, MODE, RingShape<MODE>::kStages, RingShape<MODE>::kMinBlocks>,
                                                           kRecThreads, smem);
             per_sm[dev] = n > 0 ? n : 1;
         }
         const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm[dev];
         const int64_t grid = items < cap ? items : cap;
-        recurrent_ring_kernel<D, MODE, kRingStages>
-            <<<static_cast<unsigned>(grid), kRecThreads, smem, st>>>(*a, nslice, items);
+        // The token rows ride along with the state tile when every token
+        // pointer allows a bulk copy (16-byte aligned rows).
+        const void *gate = MODE == KDA_GATE_RAW ? static_cast<const void *>(a->a) : static_cast<const void *>(a->g);
+        const int tok_bulk = aligned16(a->q) && aligned16(a->k) && aligned16(gate) && aligned16(a->v) ? 1 : 0;
+        recurrent_ring_kernel<D, MODE, RingShape<MODE>::kStages, RingShape<MODE>::kMinBlocks>
+            <<<static_cast<unsigned>(grid), kRecThreads, smem, st>>>(*a, nslice, items, tok_bulk);
     } else {
         recurrent_strided_kernel<D, MODE><<<static_cast<unsigned>(items), kRecThreads, 0, st>>>(*a, nslice);
     }
