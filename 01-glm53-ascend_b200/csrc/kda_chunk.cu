@@ -281,6 +281,13 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
     return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
            (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
+// No-swizzle K-major descriptor (layout type 0): core matrices of 8 rows x 16
+// bytes stored contiguously; lbo = byte stride between core matrices along K,
+// sbo = between core matrices along M (or N).
+__device__ __forceinline__ uint64_t sdesc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
 // Instruction descriptor: fp32 accumulate, bf16 A and B, dense.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn, bool b_neg) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((b_neg ? 1u : 0u) << 14) | ((a_mn ? 1u : 0u) << 15) |
@@ -2134,6 +2141,189 @@ __global__ void __launch_bounds__(kThreads) chunk_out_kernel(const KdaArgs p, co
     }
 }
 
+// Split path, part 3 on the tensor core (D = 128): the same outputs as
+// chunk_out_kernel, o^T = S_c^T QG^T + v'^T Aqk^T with -v'^T = -u^T + S_c^T W^T,
+// as tcgen05 products with value rows on the 128 tensor-memory lanes. The
+// scan's state split is already the no-swizzle K-major operand layout (8-row
+// x 16-byte core matrices, +128 B along the value rows, +2 KB along the keys),
+// so it feeds the tensor core straight from its bulk copy; W, QG and Aqk are
+// the record's 128-byte-swizzled tiles. -u^T goes from the record into the
+// v' accumulator by tensor-memory stores. 256 threads: warp w reads lanes
+// [32 (w % 4), +32) and token columns [32 (w / 4), +32).
+struct OutTcSmem {
+    static constexpr int D = 128;
+    static constexpr int kS = 0;                             // ScanOut: S hi, S lo (fr layout)
+    static constexpr int kW = ScanOut<D>::kBytes;            // W hi/lo, then QG hi/lo (record order)
+    static constexpr int kQG = kW + BT * D * 4;
+    static constexpr int kAQ = kQG + BT * D * 4;             // Aqk hi/lo, swizzled [64][64]
+    static constexpr int kO = kAQ + BT * BT * 4;             // bf16 [64][D] output staging
+    static constexpr int kBar = kO + BT * D * 2;             // 3 mbarriers + tensor-memory base slot
+    static constexpr int kAlloc = kBar + 64 + 1024;
+    // Tensor-memory columns (256 allocated).
+    static constexpr uint32_t cNU = 0, cO = 64, cVH = 128, cVL = 160;
+    static_assert(Rec<D>::kQG == Rec<D>::kW + BT * D * 4, "W and QG are one copy");
+    static_assert((kW & 1023) == 0 && (kQG & 1023) == 0 && (kAQ & 1023) == 0, "swizzled tiles need 1 KB alignment");
+};
+
+__global__ void __launch_bounds__(256) chunk_out_tc_kernel(const KdaArgs p, const __grid_constant__ TmaMaps maps,
+                                                          const uint8_t *rec, const uint8_t *sout,
+                                                          const int32_t *cbase) {
+    constexpr int D = 128;
+    using M = OutTcSmem;
+    using R = Rec<D>;
+    using SO = ScanOut<D>;
+    extern __shared__ __align__(1024) unsigned char sm_raw[];
+    unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
+    const uint32_t s_base = smem_addr(sm);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(sm + M::kBar);   // 0 operands, 1 W S, 2 all products
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + M::kBar + 32);
+    __nv_bfloat16 *const Ost = reinterpret_cast<__nv_bfloat16 *>(sm + M::kO);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int q4 = warp & 3, ch = warp >> 2;
+    const int row = 32 * q4 + lane;                      // value row
+    const int H = p.num_heads;
+    const int hl = blockIdx.x % p.head_count, h = p.head_begin + hl;
+    const int sl = blockIdx.x / p.head_count;
+    int req = 0;
+    while (req < p.num_req && cbase[req + 1] <= sl) ++req;
+    if (req >= p.num_req) return;
+    const int c = sl - cbase[req];
+    const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
+    const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
+    const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
+    if (bos < 0 || eos < bos || eos > p.num_tokens || slot < 0 || slot >= p.num_slots) return;   // reported by the scan
+    const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
+    const int n = static_cast<int>(eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT));
+    const int64_t rix = static_cast<int64_t>(sl) * p.head_count + hl;
+    const uint8_t *const r = rec + rix * R::kBytes;
+
+    if (warp == 0) tmem_alloc(tmem_slot, 256);
+    if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bars[0], SO::kBytes + 2 * BT * D * 4 + BT * BT * 4);
+        bulk_g2s(sm + M::kS, sout + rix * SO::kBytes, SO::kBytes, &bars[0]);
+        bulk_g2s(sm + M::kW, r + R::kW, 2 * BT * D * 4, &bars[0]);
+        bulk_g2s(sm + M::kAQ, r + R::kAQ, BT * BT * 4, &bars[0]);
+    }
+    // -u^T of value row `row`, tokens [32 ch, +32): float (t, v) of the record
+    // at ((t / 4) D + v) * 4 + t % 4, so a warp's float4 loads are 512
+    // contiguous bytes.
+    uint32_t x[32];
+    {
+        const float *us = reinterpret_cast<const float *>(r + R::kU);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 u4 = __ldg(reinterpret_cast<const float4 *>(us + ((8 * ch + k) * D + row) * 4));
+            x[4 * k] = __float_as_uint(u4.x);
+            x[4 * k + 1] = __float_as_uint(u4.y);
+            x[4 * k + 2] = __float_as_uint(u4.z);
+            x[4 * k + 3] = __float_as_uint(u4.w);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+    tmem_st<32>(tq + M::cNU + 32 * ch, x);
+    tmem_st_wait();
+    tc_fence_before();
+    __syncthreads();   // the v' accumulator holds -u^T
+    constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
+    if (tid == 0) {
+        tc_fence_after();
+        if (!mbar_wait(&bars[0], 0, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+        // -v'^T = -u^T + S^T W^T, then o^T = S^T QG^T (split-bf16: hi.hi + hi.lo + lo.hi).
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ah = sdesc_noswz(s_base + M::kS + SO::kSH + kk * 4096, 2048, 128);
+            const uint64_t al = sdesc_noswz(s_base + M::kS + SO::kSL + kk * 4096, 2048, 128);
+            const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
+            const uint64_t wh = sdesc(s_base + M::kW + off, 16, 1024);
+            const uint64_t wl = sdesc(s_base + M::kW + BT * D * 2 + off, 16, 1024);
+            umma_ss(tmem + M::cNU, al, wh, id_n64, 1u);
+            umma_ss(tmem + M::cNU, ah, wl, id_n64, 1u);
+            umma_ss(tmem + M::cNU, ah, wh, id_n64, 1u);
+        }
+        umma_commit(&bars[1]);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t ah = sdesc_noswz(s_base + M::kS + SO::kSH + kk * 4096, 2048, 128);
+            const uint64_t al = sdesc_noswz(s_base + M::kS + SO::kSL + kk * 4096, 2048, 128);
+            const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
+            const uint64_t qh = sdesc(s_base + M::kQG + off, 16, 1024);
+            const uint64_t ql = sdesc(s_base + M::kQG + BT * D * 2 + off, 16, 1024);
+            umma_ss(tmem + M::cO, al, qh, id_n64, kk > 0 ? 1u : 0u);
+            umma_ss(tmem + M::cO, ah, ql, id_n64, 1u);
+            umma_ss(tmem + M::cO, ah, qh, id_n64, 1u);
+        }
+    }
+    // -v'^T (fp32) -> v'^T hi/lo A operand, this warp's 32 token columns.
+    if (!mbar_wait(&bars[1], 0, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+    tc_fence_after();
+    {
+        uint32_t hi[16], lo[16];
+        tmem_ld<32>(tq + M::cNU + 32 * ch, x);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+            split2(-__uint_as_float(x[2 * e]), -__uint_as_float(x[2 * e + 1]), hi[e], lo[e]);
+        tmem_st<16>(tq + M::cVH + 16 * ch, hi);
+        tmem_st<16>(tq + M::cVL + 16 * ch, lo);
+        tmem_st_wait();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        tc_fence_after();
+        // o^T += v'^T Aqk^T (K = the chunk's tokens).
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t ah = tmem + M::cVH + 8 * kk, al = tmem + M::cVL + 8 * kk;
+            const uint64_t qh = sdesc(s_base + M::kAQ + kk * 32, 16, 1024);
+            const uint64_t ql = sdesc(s_base + M::kAQ + BT * BT * 2 + kk * 32, 16, 1024);
+            umma_ts(tmem + M::cO, al, qh, id_n64, 1u);
+            umma_ts(tmem + M::cO, ah, ql, id_n64, 1u);
+            umma_ts(tmem + M::cO, ah, qh, id_n64, 1u);
+        }
+        umma_commit(&bars[2]);
+    }
+    if (!mbar_wait(&bars[2], 0, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+    tc_fence_after();
+    tmem_ld<32>(tq + M::cO + 32 * ch, x);
+    tmem_ld_wait();
+    if (p.out_fp32) {
+        float *o = static_cast<float *>(p.out);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            const int t = 32 * ch + e;
+            if (t < n) o[((t0 + t) * H + h) * D + row] = __uint_as_float(x[e]);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) Ost[(32 * ch + e) * D + row] = __float2bfloat16_rn(__uint_as_float(x[e]));
+        fence_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+    if (tid == 0 && !p.out_fp32) {
+        if (n == BT) {
+            tma_store_3d(&maps.o, Ost, 0, h, static_cast<int>(t0));
+        } else {
+            __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + (t0 * H + h) * D;
+            for (int rw = 0; rw < n; ++rw) bulk_s2g(o + static_cast<int64_t>(rw) * H * D, Ost + rw * D, D * 2);
+        }
+        bulk_commit();
+        bulk_wait_all();
+    }
+}
+
 // Split-path plan, one thread per request (num_req <= 1024): the chunk slot
 // offsets cbase[r] (chunks of requests < r, num_req + 1 entries) and the
 // segmentation. The segment length is the shortest (>= kMinSegChunks) whose
@@ -2350,11 +2540,12 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
     using L = chunk::Smem<D>;
     chunk::TmaMaps maps;
     if (!encode_maps(maps, a, D, MODE == KDA_GATE_RAW)) return KDA_ERR_LAUNCH;
-    static bool opted_prep[64], opted_scan[64], opted_comb[64], opted_out[64];
+    static bool opted_prep[64], opted_scan[64], opted_comb[64], opted_out[64], opted_out_tc[64];
     if (!opt_in(chunk::chunk_kernel<D, MODE, true>, opted_prep, L::kAlloc) ||
         !opt_in(chunk::chunk_scan_kernel<D>, opted_scan, L::kAlloc) ||
         !opt_in(chunk::chunk_combine_kernel<D>, opted_comb, chunk::CombSmem<D>::kAlloc) ||
-        !opt_in(chunk::chunk_out_kernel<D>, opted_out, chunk::OutSmem<D>::kAlloc))
+        !opt_in(chunk::chunk_out_kernel<D>, opted_out, chunk::OutSmem<D>::kAlloc) ||
+        (D == 128 && !opt_in(chunk::chunk_out_tc_kernel, opted_out_tc, chunk::OutTcSmem::kAlloc)))
         return KDA_ERR_LAUNCH;
     const SplitLayout lay = split_layout(a->num_req, a->num_tokens, a->head_count, D);
     int32_t *cbase = reinterpret_cast<int32_t *>(ws + lay.cbase);
@@ -2374,8 +2565,13 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
                                      chunk::kThreads, chunk::CombSmem<D>::kAlloc, st>>>(*a, plan, states);
     chunk::chunk_scan_kernel<D><<<scan_grid, chunk::kThreads + 32, L::kAlloc, st>>>(*a, plan, 1, maps, rec, trec,
                                                                                  cbase, sout, states);
-    chunk::chunk_out_kernel<D><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads,
-                                 chunk::OutSmem<D>::kAlloc, st>>>(*a, maps, rec, sout, cbase);
+    if constexpr (D == 128) {
+        chunk::chunk_out_tc_kernel<<<static_cast<unsigned>(slots * a->head_count), 256, chunk::OutTcSmem::kAlloc,
+                                     st>>>(*a, maps, rec, sout, cbase);
+    } else {
+        chunk::chunk_out_kernel<D><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads,
+                                     chunk::OutSmem<D>::kAlloc, st>>>(*a, maps, rec, sout, cbase);
+    }
     return KDA_OK;
 }
 
