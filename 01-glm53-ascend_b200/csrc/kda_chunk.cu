@@ -253,8 +253,6 @@ __device__ __forceinline__ void bulk_s2g(void *gdst, const void *src, uint32_t b
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // This thread's committed bulk stores have finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-// ... and finished writing global memory.
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // Tiled TMA load of a 3-D box (x = key/value column, y = head, z = token)
 // into shared memory, completing on `bar`. No multicast.
@@ -1406,7 +1404,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                         bulk_s2g(tr + R::tEtr, vec + L::vEtr, D * 4);
                     }
                     bulk_commit();
-                    bulk_wait_all();
+                    bulk_wait_read();   // smem may be released; the kernel's end publishes the writes
                 }
                 continue;
             }
@@ -1494,7 +1492,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
             }
         }
-        if (tid == 0 || tid == 384) bulk_wait_all();   // output stores complete before the CTA exits
+        if (tid == 0 || tid == 384) bulk_wait_read();   // output stores have read their staging tiles
     }
     tc_fence_before();
     __syncthreads();
@@ -2137,7 +2135,7 @@ __global__ void __launch_bounds__(kThreads) chunk_out_kernel(const KdaArgs p, co
             for (int rw = 0; rw < n; ++rw) bulk_s2g(o + static_cast<int64_t>(rw) * H * D, Ost + rw * D, D * 2);
         }
         bulk_commit();
-        bulk_wait_all();
+        bulk_wait_read();
     }
 }
 
@@ -2320,7 +2318,7 @@ __global__ void __launch_bounds__(256) chunk_out_tc_kernel(const KdaArgs p, cons
             for (int rw = 0; rw < n; ++rw) bulk_s2g(o + static_cast<int64_t>(rw) * H * D, Ost + rw * D, D * 2);
         }
         bulk_commit();
-        bulk_wait_all();
+        bulk_wait_read();
     }
 }
 
