@@ -1895,20 +1895,31 @@ struct CombSmem {
     static constexpr int kAlloc = kXl + D * D * 2 + 1024;
 };
 
-// fp32 state (exchange layout) -> bf16 hi/lo swizzled row-major tile in shared memory.
+// fp32 state (exchange layout) in registers: this thread's float4 groups
+// q = tid + 512 i of the D x D state (row q % D, columns 4 (q / D) ..).
 template <int D>
-__device__ __forceinline__ void state_to_tile(const float *src, unsigned char *hi, unsigned char *lo) {
-    for (int q = threadIdx.x; q < D * D / 4; q += blockDim.x) {
-        const int row = q % D, c4 = q / D;
-        const float4 x = *reinterpret_cast<const float4 *>(src + static_cast<int64_t>(q) * 4);
-        uint32_t h0, h1, l0, l1;
-        split2(x.x, x.y, h0, l0);
-        split2(x.z, x.w, h1, l1);
-        const int o = swz<D>(row, 4 * c4) * 2;
-        *reinterpret_cast<uint2 *>(hi + o) = make_uint2(h0, h1);
-        *reinterpret_cast<uint2 *>(lo + o) = make_uint2(l0, l1);
+struct StateRegs {
+    static constexpr int N = D * D / 4 / kThreads;
+    float4 x[N];
+    __device__ __forceinline__ void load(const float *src) {
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+            x[i] = __ldg(reinterpret_cast<const float4 *>(src) + threadIdx.x + kThreads * i);
     }
-}
+    // -> bf16 hi/lo swizzled row-major tile in shared memory.
+    __device__ __forceinline__ void to_tile(unsigned char *hi, unsigned char *lo) const {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const int q = threadIdx.x + kThreads * i, row = q % D, c4 = q / D;
+            uint32_t h0, h1, l0, l1;
+            split2(x[i].x, x[i].y, h0, l0);
+            split2(x[i].z, x[i].w, h1, l1);
+            const int o = swz<D>(row, 4 * c4) * 2;
+            *reinterpret_cast<uint2 *>(hi + o) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2 *>(lo + o) = make_uint2(l0, l1);
+        }
+    }
+};
 
 template <int D>
 __global__ void __launch_bounds__(kThreads) chunk_combine_kernel(const KdaArgs p, const int32_t *plan,
@@ -1929,22 +1940,27 @@ __global__ void __launch_bounds__(kThreads) chunk_combine_kernel(const KdaArgs p
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t4 = lane & 3;
     const int mt = warp % MT, n0 = (warp / MT) * NC;
+    auto slot = [&](int which, int i) { return state_slot<D>(states, cap, p.head_count, which, i, hl); };
     float acc[NT][4];
-    state_to_tile<D>(state_slot<D>(states, cap, p.head_count, 0, sb, hl), sm + M::kSh, sm + M::kSl);
+    StateRegs<D> xr;
+    xr.load(slot(0, sb));
+    xr.to_tile(sm + M::kSh, sm + M::kSl);
+    xr.load(slot(2, sb));                      // segment 1's A
     for (int i = 1; i + 1 < P; ++i) {
-        // slot sb + i - 1 holds segment i's B and A; the result is start state i + 1
-        state_to_tile<D>(state_slot<D>(states, cap, p.head_count, 2, sb + i - 1, hl), sm + M::kXh, sm + M::kXl);
-        const float *bt = state_slot<D>(states, cap, p.head_count, 1, sb + i - 1, hl);
+        // slot sb + i - 1 holds segment i's B and A; the result is start state i + 1.
+        const float *bt = slot(1, sb + i - 1);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 const int v = 16 * mt + g + 8 * hf, k = n0 + 8 * nt + 2 * t4;
-                const float2 b = *reinterpret_cast<const float2 *>(bt + ((k >> 2) * D + v) * 4 + (k & 3));
+                const float2 b = __ldg(reinterpret_cast<const float2 *>(bt + ((k >> 2) * D + v) * 4 + (k & 3)));
                 acc[nt][2 * hf] = b.x;
                 acc[nt][2 * hf + 1] = b.y;
             }
+        xr.to_tile(sm + M::kXh, sm + M::kXl);
         __syncthreads();
+        if (i + 2 < P) xr.load(slot(2, sb + i));   // the next step's A, in flight during the products
 #pragma unroll 2
         for (int ks = 0; ks < D / 16; ++ks) {
             uint32_t ah[4], al[4];
@@ -1960,7 +1976,7 @@ __global__ void __launch_bounds__(kThreads) chunk_combine_kernel(const KdaArgs p
             }
         }
         __syncthreads();
-        float *out = state_slot<D>(states, cap, p.head_count, 0, sb + i, hl);
+        float *out = slot(0, sb + i);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1974,7 +1990,7 @@ __global__ void __launch_bounds__(kThreads) chunk_combine_kernel(const KdaArgs p
                 *reinterpret_cast<uint32_t *>(sm + M::kSh + o) = hi2;
                 *reinterpret_cast<uint32_t *>(sm + M::kSl + o) = lo2;
             }
-        // The next step's A^T conversion overwrites only the X tiles; its
+        // The next step's A conversion overwrites only the X tiles; its
         // barrier orders these S writes before the next products read them.
     }
 }
