@@ -18,12 +18,16 @@ larger than the 126 MB L2, so no flush is needed between steps.
 Also reported:
 * ``roofline``: the decode kernel alone (C-ABI launches timed with CUDA events
   on the launching stream) against the measured HBM copy bandwidth;
-* ``e2e``: the same metric through the public op with inputs copied from pinned
-  host memory each step and the output read back;
+* ``e2e``: the same metric through the public op with every step's inputs
+  copied from pinned host memory and its output read back, pipelined as a
+  serving loop runs it (``time_e2e``: the next step's inputs copy on a second
+  stream while this step computes);
 * ``cpu_baseline``: the CPU oracle (``oracle/kda_ref.py``, a port of the
   reference's PyTorch recurrence) on this host's cores, on a bounded sample;
 * ``prefill``: the chunked prefill of ``configs[2]`` (8 varlen sequences,
   33,494 tokens, H=32) with its tensor/HBM roofline;
+* ``prefill_long``: ``configs[3]`` (one 131,072-token sequence, 4 heads per
+  GPU) through the same op;
 * ``clocks``: SM clock and throttle reasons sampled by NVML during timing.
 
 ``--impl reference`` times the reference's own CPU algorithm (the oracle port;
