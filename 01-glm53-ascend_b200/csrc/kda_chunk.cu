@@ -264,6 +264,13 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// L2 prefetch of the same 3-D box (no shared-memory destination, no barrier).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap *map, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
 // Tensor maps of one launch: q, k, the gate (g fp32, or a bf16 for the raw
 // gate) as [T][H][D] boxes of 64 tokens x D, v as 64-token x 64-column
 // boxes written with the 128-byte swizzle the tensor core reads, and the bf16
@@ -693,8 +700,30 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     constexpr int SC = D / 4;                        // state columns per slice
 
     if (PREP && warp == kThreads / 32) {
-        // Prep: this CTA's one chunk of q, k, the gate and v.
-        if (lane == 0) issue_tiles(cprep, true);
+        // Prep: this CTA's one chunk of q, k, the gate and v; then an L2
+        // prefetch of the tiles of the CTA one wave later (block + SM count),
+        // which is dispatched about when a CTA of this wave retires.
+        if (lane == 0) {
+            issue_tiles(cprep, true);
+            uint32_t nsm;
+            asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+            const int64_t nb = static_cast<int64_t>(blockIdx.x) + nsm;
+            if (nb < static_cast<int64_t>(gridDim.x)) {
+                const int sl2 = static_cast<int>(nb / p.head_count);
+                const int h2 = p.head_begin + static_cast<int>(nb % p.head_count);
+                int r2 = 0;
+                while (r2 < p.num_req && cbase[r2 + 1] <= sl2) ++r2;
+                if (r2 < p.num_req) {
+                    const int t2 = static_cast<int>(load_index(p.cu_seqlens, p.index_bytes[1], r2) +
+                                                    static_cast<int64_t>(sl2 - cbase[r2]) * BT);
+                    tma_prefetch_3d(&maps.q, 0, h2, t2);
+                    tma_prefetch_3d(&maps.k, 0, h2, t2);
+                    tma_prefetch_3d(&maps.g, 0, h2, t2);
+#pragma unroll
+                    for (int blk = 0; blk < D / 64; ++blk) tma_prefetch_3d(&maps.v, 64 * blk, h2, t2);
+                }
+            }
+        }
     } else if (warp == kThreads / 32) {
         // ===== producer warp: one thread issues every tensor-core product and
         // every TMA load, in the order the consumers' signals allow =====
