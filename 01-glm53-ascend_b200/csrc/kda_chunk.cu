@@ -265,6 +265,10 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
 }
 
 // L2 prefetch of the same 3-D box (no shared-memory destination, no barrier).
+// L2 prefetch of a linear range (16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap *map, int x, int y, int z) {
     asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
                      reinterpret_cast<uint64_t>(map)),
@@ -2237,7 +2241,7 @@ __global__ void __launch_bounds__(256) chunk_out_tc_kernel(const KdaArgs p, cons
     if (bos < 0 || eos < bos || eos > p.num_tokens || slot < 0 || slot >= p.num_slots) return;   // reported by the scan
     const int64_t t0 = bos + static_cast<int64_t>(c) * BT;
     const int n = static_cast<int>(eos - t0 < BT ? eos - t0 : static_cast<int64_t>(BT));
-    const int64_t rix = static_cast<int64_t>(sl) * p.head_count + hl;
+    const int64_t rix = static_cast<int64_t>(sl) * p.head_count + hl;   // == blockIdx.x
     const uint8_t *const r = rec + rix * R::kBytes;
 
     if (warp == 0) tmem_alloc(tmem_slot, 256);
@@ -2249,6 +2253,17 @@ __global__ void __launch_bounds__(256) chunk_out_tc_kernel(const KdaArgs p, cons
         bulk_g2s(sm + M::kS, sout + rix * SO::kBytes, SO::kBytes, &bars[0]);
         bulk_g2s(sm + M::kW, r + R::kW, 2 * BT * D * 4, &bars[0]);
         bulk_g2s(sm + M::kAQ, r + R::kAQ, BT * BT * 4, &bars[0]);
+        // The CTA one wave later (block + SM count; its record index is its
+        // block index) finds its operands in L2.
+        uint32_t nsm;
+        asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+        const int64_t nb = static_cast<int64_t>(blockIdx.x) + nsm;
+        if (nb < static_cast<int64_t>(gridDim.x)) {
+            const uint8_t *r2 = rec + nb * R::kBytes;
+            bulk_prefetch_l2(sout + nb * SO::kBytes, SO::kBytes);
+            bulk_prefetch_l2(r2 + R::kW, 2 * BT * D * 4);
+            bulk_prefetch_l2(r2 + R::kU, BT * D * 4 + BT * BT * 4);
+        }
     }
     // -u^T of value row `row`, tokens [32 ch, +32): float (t, v) of the record
     // at ((t / 4) D + v) * 4 + t % 4, so a warp's float4 loads are 512
