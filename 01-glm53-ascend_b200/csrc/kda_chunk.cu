@@ -2028,6 +2028,160 @@ __global__ void __launch_bounds__(kThreads) chunk_combine_kernel(const KdaArgs p
     }
 }
 
+// The combine on the tensor core (D = 128): the same chain of start states,
+// S_start[i+1]^T = S_start[i]^T A_i^T + B_i^T, with S^T in tensor memory
+// (fp32 accumulator, and its bf16 hi/lo split as the A operand) and A_i^T as a
+// 128-byte-swizzled MN-major B operand in shared memory (rows j, 64-column
+// blocks of 128 rows x 128 B). Each step: B_i^T into the accumulator by
+// tensor-memory stores, 24 products (8 k-steps x hi.hi + hi.lo + lo.hi), then
+// the new start state out to its slot and split for the next step. 256
+// threads: warp w reads lanes [32 (w % 4), +32) and columns [64 (w / 4), +64).
+struct CombTcSmem {
+    static constexpr int D = 128;
+    static constexpr int kXh = 0;                        // A^T hi, then lo
+    static constexpr int kXl = kXh + D * D * 2;
+    static constexpr int kBar = kXl + D * D * 2;
+    static constexpr int kAlloc = kBar + 64 + 1024;
+    static constexpr uint32_t cS = 0, cSH = 128, cSL = 192;
+};
+
+__global__ void __launch_bounds__(256) chunk_combine_tc_kernel(const KdaArgs p, const int32_t *plan, float *states) {
+    constexpr int D = 128;
+    using M = CombTcSmem;
+    extern __shared__ __align__(1024) unsigned char sm_raw[];
+    unsigned char *const sm = sm_raw + ((1024u - (smem_addr(sm_raw) & 1023u)) & 1023u);
+    const uint32_t s_base = smem_addr(sm);
+    uint64_t *const bar = reinterpret_cast<uint64_t *>(sm + M::kBar);
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + M::kBar + 16);
+    const int req = blockIdx.x / p.head_count, hl = blockIdx.x % p.head_count;
+    const PlanView pv(const_cast<int32_t *>(plan), p.num_req, plan[3]);
+    const int P = pv.segs()[req];
+    if (P < 3) return;
+    const int cap = plan[0], sb = pv.sbase()[req];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int q4 = warp & 3, ch = warp >> 2;
+    const int row = 32 * q4 + lane;
+    auto slot = [&](int which, int i) { return state_slot<D>(states, cap, p.head_count, which, i, hl); };
+
+    if (warp == 0) tmem_alloc(tmem_slot, 256);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tq = tmem + (static_cast<uint32_t>(32 * q4) << 16);
+    // This thread's 64 columns of a state in the exchange layout: float4 e
+    // holds columns 64 ch + 4 e .. + 3 of row `row`.
+    auto load_row = [&](const float *src, float4 (&x)[16]) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+            x[e] = __ldg(reinterpret_cast<const float4 *>(src + ((16 * ch + e) * D + row) * 4));
+    };
+    auto split_row = [&](const float4 (&x)[16]) {
+        uint32_t hi[32], lo[32];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            split2(x[e].x, x[e].y, hi[2 * e], lo[2 * e]);
+            split2(x[e].z, x[e].w, hi[2 * e + 1], lo[2 * e + 1]);
+        }
+        tmem_st<32>(tq + M::cSH + 32 * ch, hi);
+        tmem_st<32>(tq + M::cSL + 32 * ch, lo);
+    };
+    {
+        float4 x[16];
+        load_row(slot(0, sb), x);
+        split_row(x);
+    }
+    constexpr uint32_t id = idesc_bf16(128, D, false, true, false);
+    for (int i = 1; i + 1 < P; ++i) {
+        const float *at = slot(2, sb + i - 1), *bt = slot(1, sb + i - 1);
+        if (tid == 0 && i + 2 < P) {
+            bulk_prefetch_l2(slot(2, sb + i), D * D * 4);
+            bulk_prefetch_l2(slot(1, sb + i), D * D * 4);
+        }
+        // A_i^T -> swizzled bf16 hi/lo tile: float4 groups q = tid + 256 e
+        // (row q % D, columns 4 (q / D) ..).
+#pragma unroll 4
+        for (int e = 0; e < D * D / 4 / 256; ++e) {
+            const int q = tid + 256 * e, j = q % D, k = 4 * (q / D);
+            const float4 x = __ldg(reinterpret_cast<const float4 *>(at) + q);
+            uint32_t h0, h1, l0, l1;
+            split2(x.x, x.y, h0, l0);
+            split2(x.z, x.w, h1, l1);
+            const int o = ((k >> 6) * (D * 64) + swz<64>(j, k & 63)) * 2;
+            *reinterpret_cast<uint2 *>(sm + M::kXh + o) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2 *>(sm + M::kXl + o) = make_uint2(l0, l1);
+        }
+        {
+            // B_i^T starts the accumulator.
+            float4 x[16];
+            load_row(bt, x);
+            uint32_t r[32];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    r[4 * e] = __float_as_uint(x[8 * half + e].x);
+                    r[4 * e + 1] = __float_as_uint(x[8 * half + e].y);
+                    r[4 * e + 2] = __float_as_uint(x[8 * half + e].z);
+                    r[4 * e + 3] = __float_as_uint(x[8 * half + e].w);
+                }
+                tmem_st<32>(tq + M::cS + 64 * ch + 32 * half, r);
+            }
+        }
+        fence_async_smem();
+        tmem_st_wait();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                const uint32_t ah = tmem + M::cSH + 8 * kk, al = tmem + M::cSL + 8 * kk;
+                const uint64_t xh = sdesc(s_base + M::kXh + kk * 2048, D * 128, 1024);
+                const uint64_t xl = sdesc(s_base + M::kXl + kk * 2048, D * 128, 1024);
+                umma_ts(tmem + M::cS, al, xh, id, 1u);
+                umma_ts(tmem + M::cS, ah, xl, id, 1u);
+                umma_ts(tmem + M::cS, ah, xh, id, 1u);
+            }
+            umma_commit(bar);
+        }
+        if (!mbar_wait(bar, static_cast<uint32_t>((i - 1) & 1), p.status) && tid == 0)
+            report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+        tc_fence_after();
+        {
+            // S_start[i+1]^T -> its slot and the next A operand.
+            uint32_t r[32];
+            float4 x[16];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                tmem_ld<32>(tq + M::cS + 64 * ch + 32 * half, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    x[8 * half + e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                                  __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+            }
+            float *out = slot(0, sb + i);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) *reinterpret_cast<float4 *>(out + ((16 * ch + e) * D + row) * 4) = x[e];
+            split_row(x);
+        }
+        // The next step's tile writes and accumulator stores follow this
+        // step's completed products (the barrier wait above).
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 // Split path, part 3: the outputs, one CTA per (chunk, head) on all SMs. From
 // the chunk's record (W, QG, -u^T, Aqk) and the scan's split of the
 // chunk-start state S_c: v' = u - W S_c, then o = QG S_c + Aqk v', as
@@ -2598,12 +2752,13 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
     using L = chunk::Smem<D>;
     chunk::TmaMaps maps;
     if (!encode_maps(maps, a, D, MODE == KDA_GATE_RAW)) return KDA_ERR_LAUNCH;
-    static bool opted_prep[64], opted_scan[64], opted_comb[64], opted_out[64], opted_out_tc[64];
+    static bool opted_prep[64], opted_scan[64], opted_comb[64], opted_comb_tc[64], opted_out[64], opted_out_tc[64];
     if (!opt_in(chunk::chunk_kernel<D, MODE, true>, opted_prep, L::kAlloc) ||
         !opt_in(chunk::chunk_scan_kernel<D>, opted_scan, L::kAlloc) ||
         !opt_in(chunk::chunk_combine_kernel<D>, opted_comb, chunk::CombSmem<D>::kAlloc) ||
         !opt_in(chunk::chunk_out_kernel<D>, opted_out, chunk::OutSmem<D>::kAlloc) ||
-        (D == 128 && !opt_in(chunk::chunk_out_tc_kernel, opted_out_tc, chunk::OutTcSmem::kAlloc)))
+        (D == 128 && !opt_in(chunk::chunk_out_tc_kernel, opted_out_tc, chunk::OutTcSmem::kAlloc)) ||
+        (D == 128 && !opt_in(chunk::chunk_combine_tc_kernel, opted_comb_tc, chunk::CombTcSmem::kAlloc)))
         return KDA_ERR_LAUNCH;
     const SplitLayout lay = split_layout(a->num_req, a->num_tokens, a->head_count, D);
     int32_t *cbase = reinterpret_cast<int32_t *>(ws + lay.cbase);
@@ -2619,8 +2774,13 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
     const unsigned scan_grid = static_cast<unsigned>(static_cast<int64_t>(lay.task_cap) * a->head_count);
     chunk::chunk_scan_kernel<D><<<scan_grid, chunk::kThreads + 32, L::kAlloc, st>>>(*a, plan, 0, maps, rec, trec,
                                                                                  cbase, sout, states);
-    chunk::chunk_combine_kernel<D><<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count),
-                                     chunk::kThreads, chunk::CombSmem<D>::kAlloc, st>>>(*a, plan, states);
+    if constexpr (D == 128) {
+        chunk::chunk_combine_tc_kernel<<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count), 256,
+                                         chunk::CombTcSmem::kAlloc, st>>>(*a, plan, states);
+    } else {
+        chunk::chunk_combine_kernel<D><<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count),
+                                         chunk::kThreads, chunk::CombSmem<D>::kAlloc, st>>>(*a, plan, states);
+    }
     chunk::chunk_scan_kernel<D><<<scan_grid, chunk::kThreads + 32, L::kAlloc, st>>>(*a, plan, 1, maps, rec, trec,
                                                                                  cbase, sout, states);
     if constexpr (D == 128) {
