@@ -2747,8 +2747,11 @@ static SplitLayout split_layout(int32_t num_req, int32_t num_tokens, int32_t hea
     return l;
 }
 
+// `ev` (measurement only, else null): six events recorded on the stream before
+// the plan and after prep, the scan's first pass, the combine, the rescan and
+// the outputs.
 template <int D, int MODE>
-static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
+static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st, cudaEvent_t const *ev = nullptr) {
     using L = chunk::Smem<D>;
     chunk::TmaMaps maps;
     if (!encode_maps(maps, a, D, MODE == KDA_GATE_RAW)) return KDA_ERR_LAUNCH;
@@ -2765,15 +2768,21 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
     int32_t *plan = reinterpret_cast<int32_t *>(ws + lay.plan);
     uint8_t *rec = ws + lay.rec, *trec = ws + lay.trec, *sout = ws + lay.sout;
     float *states = reinterpret_cast<float *>(ws + lay.states);
+    auto mark = [&](int i) {
+        if (ev != nullptr) cudaEventRecord(ev[i], st);
+    };
+    mark(0);
     chunk::plan_kernel<<<1, 1024, 0, st>>>(*a, cbase, plan, lay.budget, lay.task_cap, lay.slot_cap);
     const int64_t slots = static_cast<int64_t>(a->num_tokens) / chunk::BT + a->num_req;
     chunk::chunk_kernel<D, MODE, true><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads + 32,
                                          L::kAlloc, st>>>(*a, nullptr, maps, rec, trec, cbase);
+    mark(1);
     // Segmented scan: first pass, combine, rescan (CTAs past a phase's task
     // count exit at once).
     const unsigned scan_grid = static_cast<unsigned>(static_cast<int64_t>(lay.task_cap) * a->head_count);
     chunk::chunk_scan_kernel<D><<<scan_grid, chunk::kThreads + 32, L::kAlloc, st>>>(*a, plan, 0, maps, rec, trec,
                                                                                  cbase, sout, states);
+    mark(2);
     if constexpr (D == 128) {
         chunk::chunk_combine_tc_kernel<<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count), 256,
                                          chunk::CombTcSmem::kAlloc, st>>>(*a, plan, states);
@@ -2781,8 +2790,10 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
         chunk::chunk_combine_kernel<D><<<static_cast<unsigned>(static_cast<int64_t>(a->num_req) * a->head_count),
                                          chunk::kThreads, chunk::CombSmem<D>::kAlloc, st>>>(*a, plan, states);
     }
+    mark(3);
     chunk::chunk_scan_kernel<D><<<scan_grid, chunk::kThreads + 32, L::kAlloc, st>>>(*a, plan, 1, maps, rec, trec,
                                                                                  cbase, sout, states);
+    mark(4);
     if constexpr (D == 128) {
         chunk::chunk_out_tc_kernel<<<static_cast<unsigned>(slots * a->head_count), 256, chunk::OutTcSmem::kAlloc,
                                      st>>>(*a, maps, rec, sout, cbase);
@@ -2790,6 +2801,7 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st) {
         chunk::chunk_out_kernel<D><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads,
                                      chunk::OutSmem<D>::kAlloc, st>>>(*a, maps, rec, sout, cbase);
     }
+    mark(5);
     return KDA_OK;
 }
 
@@ -2804,7 +2816,11 @@ extern "C" size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens,
     return num_req <= 1024 ? kda::order_bytes(num_req) : 0;
 }
 
-extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream) {
+namespace kda {
+// Argument checks of kda_chunk_launch (KDA_OK, or the status to return;
+// *empty = nothing to launch).
+static int chunk_check(const KdaArgs *args, bool *empty) {
+    *empty = false;
     if (args == nullptr) return KDA_ERR_INVALID_ARGUMENT;
     if (args->intermediate != nullptr) return KDA_ERR_INVALID_ARGUMENT;
     if (args->gate_mode == KDA_GATE_PREPARED) return KDA_ERR_UNSUPPORTED;
@@ -2814,7 +2830,10 @@ extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t wor
         return KDA_ERR_INVALID_ARGUMENT;
     for (int i = 0; i < 4; ++i)
         if (args->index_bytes[i] != 4 && args->index_bytes[i] != 8) return KDA_ERR_INVALID_ARGUMENT;
-    if (args->num_req == 0 || args->head_count == 0) return KDA_OK;
+    if (args->num_req == 0 || args->head_count == 0) {
+        *empty = true;
+        return KDA_OK;
+    }
     if (args->state == nullptr || args->num_slots <= 0 || args->indices == nullptr || args->cu_seqlens == nullptr ||
         args->out == nullptr || args->q == nullptr || args->k == nullptr || args->v == nullptr)
         return KDA_ERR_INVALID_ARGUMENT;
@@ -2828,7 +2847,46 @@ extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t wor
     // are multiples of 16 bytes for both head dims.
     const void *rows[] = {args->q, args->k, args->v, args->gate_mode == KDA_GATE_RAW ? args->a : args->g, args->out};
     for (const void *ptr : rows)
-        if (!kda::chunk_aligned16(ptr)) return KDA_ERR_ALIGNMENT;
+        if (!chunk_aligned16(ptr)) return KDA_ERR_ALIGNMENT;
+    return KDA_OK;
+}
+}  // namespace kda
+
+// Measurement entry point (no counterpart in the reference): the split path
+// of kda_chunk_launch with `events` (6 cudaEvent_t, created by the caller)
+// recorded on the stream before the plan and after prep, the scan's first
+// pass, the combine, the rescan and the outputs. KDA_ERR_UNSUPPORTED when the
+// batch would not take the split path, KDA_ERR_WORKSPACE when the workspace
+// does not hold it.
+extern "C" int kda_chunk_launch_phases(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream,
+                                       void *const *events, int num_events) {
+    bool empty = false;
+    const int chk = kda::chunk_check(args, &empty);
+    if (chk != KDA_OK) return chk;
+    if (events == nullptr || num_events != 6) return KDA_ERR_INVALID_ARGUMENT;
+    if (empty || !kda::want_split(args->num_req, args->head_count, args->num_tokens)) return KDA_ERR_UNSUPPORTED;
+    if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 ||
+        workspace_bytes < kda::split_layout(args->num_req, args->num_tokens, args->head_count, args->head_dim).total)
+        return KDA_ERR_WORKSPACE;
+    cudaEvent_t ev[6];
+    for (int i = 0; i < 6; ++i) ev[i] = static_cast<cudaEvent_t>(events[i]);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    int rc;
+    if (args->head_dim == 128)
+        rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk_split<128, KDA_GATE_RAW>(args, ws, st, ev)
+                                             : kda::launch_chunk_split<128, KDA_GATE_LOG>(args, ws, st, ev);
+    else
+        rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk_split<64, KDA_GATE_RAW>(args, ws, st, ev)
+                                             : kda::launch_chunk_split<64, KDA_GATE_LOG>(args, ws, st, ev);
+    if (rc != KDA_OK) return rc;
+    return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+}
+
+extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream) {
+    bool empty = false;
+    const int chk = kda::chunk_check(args, &empty);
+    if (chk != KDA_OK || empty) return chk;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int rc;
     // The split path runs when it pays off and the workspace holds its records;

@@ -28,6 +28,7 @@ EXPORTED = (
     "kda_recurrent_launch",
     "kda_chunk_workspace_bytes",
     "kda_chunk_launch",
+    "kda_chunk_launch_phases",
     "kda_prepared_recurrent_launch",
     "kda_chunk_launch_no_alloc",
     "kda_commit_intermediate_launch",
@@ -115,6 +116,9 @@ def lib() -> ctypes.CDLL:
         L.kda_chunk_launch.restype = ctypes.c_int
         L.kda_chunk_launch.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
                                        ctypes.c_void_p]
+        L.kda_chunk_launch_phases.restype = ctypes.c_int
+        L.kda_chunk_launch_phases.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
+                                              ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]
         _lib = L
     return _lib
 
@@ -186,6 +190,16 @@ def chunk_launch(args: KdaArgs, workspace: Optional[torch.Tensor], workspace_byt
                  stream: Optional[torch.cuda.Stream] = None) -> int:
     return lib().kda_chunk_launch(ctypes.byref(args), _ptr(workspace), workspace_bytes,
                                   stream_handle(stream))
+
+
+def chunk_launch_phases(args: KdaArgs, workspace: torch.Tensor, workspace_bytes: int, events,
+                        stream: Optional[torch.cuda.Stream] = None) -> int:
+    """kda_chunk_launch's split path with six torch.cuda.Events (timing
+    enabled, each recorded once before) marking its phases: before the plan,
+    after prep, the scan's first pass, the combine, the rescan, the outputs."""
+    handles = (ctypes.c_void_p * 6)(*[ctypes.c_void_p(e.cuda_event) for e in events])
+    return lib().kda_chunk_launch_phases(ctypes.byref(args), _ptr(workspace), workspace_bytes,
+                                         stream_handle(stream), handles, len(events))
 
 
 def chunk_launch_no_alloc(args: KdaArgs, stream: Optional[torch.cuda.Stream] = None) -> int:

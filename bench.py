@@ -400,12 +400,38 @@ def bench_prefill_long(args, dist: Dist, steps: int, warmup: int) -> dict:
 
     ms = time_steps(step, steps, warmup, dist) / steps
     d.pool.copy_(pool0)
+
+    # The inter-chunk state pass on its own: the same launch through the C
+    # ABI's measurement hook, CUDA events between the split path's kernels.
+    from sgl_glm53_ascend_ops import abi
+    out = torch.empty_like(d.v)
+    cargs = abi.args_from_tensors(q=d.q, k=d.k, v=d.v, out=out, state=d.pool, indices=d.indices,
+                                  cu_seqlens=d.cu_seqlens, scale=d.scale, gate_mode=abi.KDA_GATE_LOG,
+                                  g=d.g, beta=d.beta)
+    nws = abi.chunk_workspace_bytes(1, w.tokens, heads, 128)
+    ws = torch.empty(nws, dtype=torch.uint8, device="cuda")
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(steps)]
+    for e in (x for row in evs for x in row):
+        e.record()                                  # creates the event handles
+    torch.cuda.synchronize()
+    for i in range(steps):
+        rc = abi.chunk_launch_phases(cargs, ws, nws, evs[i])
+        if rc != 0:
+            raise RuntimeError(f"kda_chunk_launch_phases: {abi.status_string(rc)}")
+    torch.cuda.synchronize()
+    d.pool.copy_(pool0)
+    names = ("plan_prep", "scan_first_pass", "combine", "rescan", "outputs")
+    phases = {n: round(dist.max(sum(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(steps)) / steps), 4)
+              for j, n in enumerate(names)}
+    del ws
     return {
         "metric": "KDA long-context prefill tokens/s (chunk-64, configs[3])",
         "value": round(dist.world * w.tokens * heads / (ms / 1e3), 1),
         "unit": "token-heads/s",
         "ms_per_step": round(ms, 4),
         "per_chunk_us": round(ms * 1e3 / (w.tokens / 64), 3),
+        "state_pass_ms": round(phases["scan_first_pass"] + phases["combine"] + phases["rescan"], 4),
+        "phases_ms": phases,
         "steps": steps,
         "warmup": warmup,
         "config": {"workload": f"cfg4: 1 sequence x {w.tokens} tokens, {heads} heads per GPU (of H=32), "

@@ -154,6 +154,17 @@ size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens,
 int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes,
                      void *stream);
 
+/* Measurement hook, no counterpart in the reference: the split path of
+ * kda_chunk_launch with six caller-created cudaEvent_t handles recorded on
+ * the stream -- before the plan, then after the prep kernel, the scan's
+ * first pass, the combine of the segment transfers, the rescan and the
+ * output kernel -- so a benchmark can report the inter-chunk state pass on
+ * its own. Same arguments and results as kda_chunk_launch otherwise;
+ * KDA_ERR_UNSUPPORTED when the batch would take the fused kernel,
+ * KDA_ERR_WORKSPACE when the workspace cannot hold the split path. */
+int kda_chunk_launch_phases(const KdaArgs *args, void *workspace, size_t workspace_bytes,
+                            void *stream, void *const *events, int num_events);
+
 /* Largest batch kda_chunk_launch_no_alloc accepts (its scratch capacity). */
 #define KDA_CHUNK_STATIC_MAX_REQUESTS 1024
 
