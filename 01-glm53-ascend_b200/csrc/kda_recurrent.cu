@@ -157,13 +157,11 @@ __device__ __forceinline__ bool decode_item(const KdaArgs &p, int64_t it, int ns
 // The token loop of one item with the state rows already in registers:
 // prologue, recurrence step, output, prefix/per-step checkpoints, final
 // write-back (kda_python.py:271-307).
-template <int D, int MODE>
-__device__ __forceinline__ void token_from_stage(TokenRaw<D, MODE> &r, const unsigned char *stage, float bval,
-                                                 int sub, int row0);
-
+// `cur` holds the item's first token when `staged` (read from a ring stage by
+// the caller); otherwise it is loaded here.
 template <int D, int MODE, bool FAST>
 __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float (&s)[2][D / 8], int row0, int sub,
-                                         const unsigned char *stage = nullptr, float bval = 0.f) {
+                                         TokenRaw<D, MODE> &cur, bool staged) {
     constexpr int NC = D / 32;
     constexpr int NE = D / 8;
     const int h = m.h, v0 = m.v0;
@@ -188,11 +186,8 @@ __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float 
                   (FAST ? static_cast<int64_t>(v0) * D : v0 * p.mid_stride[4])
             : nullptr;
 
-    TokenRaw<D, MODE> cur, nxt;
-    if (m.bos < m.eos) {
-        if (stage != nullptr) token_from_stage<D, MODE>(cur, stage, bval, sub, row0);
-        else load_token<D, MODE>(cur, p, m.bos, h, sub, v0 + row0);
-    }
+    TokenRaw<D, MODE> nxt;
+    if (m.bos < m.eos && !staged) load_token<D, MODE>(cur, p, m.bos, h, sub, v0 + row0);
 
     for (int64_t t = m.bos; t < m.eos; ++t) {
         if (t + 1 < m.eos) load_token<D, MODE>(nxt, p, t + 1, h, sub, v0 + row0);
@@ -321,6 +316,8 @@ __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float 
 struct StageMeta {
     int64_t bos, eos, slot, tslot, tlen;
     int req, h, v0, ok;
+    uint32_t bword;   // beta (or the 4-byte word holding the raw b) of the first token
+    int bsel;         // 0: not staged (load it); 1: bword / its low half; 2: its high half
 };
 template <int D, int MODE>
 struct RingStage {
@@ -335,10 +332,11 @@ struct RingStage {
     static constexpr int kBytes = (kMeta + static_cast<int>(sizeof(StageMeta)) + 127) / 128 * 128;
 };
 
-// The first token of an item from its ring stage (beta / raw b from `bval`).
+// The first token of an item from its ring stage (beta from the header, or a
+// global load when the producer could not stage it).
 template <int D, int MODE>
-__device__ __forceinline__ void token_from_stage(TokenRaw<D, MODE> &r, const unsigned char *stage, float bval,
-                                                 int sub, int row0) {
+__device__ __forceinline__ void token_from_stage(TokenRaw<D, MODE> &r, const KdaArgs &p, const unsigned char *stage,
+                                                 const StageMeta &sm, int sub, int row0) {
     using RS = RingStage<D, MODE>;
     constexpr int NC = D / 32;
 #pragma unroll
@@ -360,42 +358,27 @@ __device__ __forceinline__ void token_from_stage(TokenRaw<D, MODE> &r, const uns
     const uint16_t *vs = reinterpret_cast<const uint16_t *>(stage + RS::kV);
     r.vb[0] = vs[row0];
     r.vb[1] = vs[row0 + 4];
+    const int64_t bi = sm.bos * p.num_heads + sm.h;
     if constexpr (MODE == KDA_GATE_RAW)
-        r.bb = static_cast<uint16_t>(__float_as_uint(bval));
+        r.bb = sm.bsel == 0 ? static_cast<const uint16_t *>(p.b)[bi]
+                            : static_cast<uint16_t>(sm.bsel == 1 ? sm.bword & 0xffffu : sm.bword >> 16);
     else
-        r.beta = bval;
+        r.beta = sm.bsel == 0 ? __ldg(p.beta + bi) : __uint_as_float(sm.bword);
 }
 
-// beta (or the raw b bits, carried in a float) of token t, head h.
-template <int MODE>
-__device__ __forceinline__ float load_bval(const KdaArgs &p, int64_t t, int h) {
-    if constexpr (MODE == KDA_GATE_RAW)
-        return __uint_as_float(static_cast<uint32_t>(static_cast<const uint16_t *>(p.b)[t * p.num_heads + h]));
-    else
-        return __ldg(p.beta + t * p.num_heads + h);
-}
-
-// Index entry i (int32 or int64) of `base` -> shared memory, asynchronously.
-__device__ __forceinline__ void cp_async_index(int64_t *dst, const void *base, int bytes, int64_t i) {
-    const char *src = static_cast<const char *>(base) + i * bytes;
-    if (bytes == 8)
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-    else
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ int64_t read_index(const int64_t *src, int bytes) {
-    return bytes == 8 ? *src : static_cast<int64_t>(*reinterpret_cast<const int32_t *>(src));
-}
-
+// One producer warp per CTA refills the ring; the compute warps never wait for
+// a refill or for one another. Stage n % STAGES: `full` completes when its
+// copies (and the beta word) have landed, `empty` when all four compute warps
+// have read it.
 template <int D, int MODE, int STAGES, int MINB>
-__global__ void __launch_bounds__(kRecThreads, MINB)
+__global__ void __launch_bounds__(kRecThreads + 32, MINB)
 recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bulk) {
     using RS = RingStage<D, MODE>;
     constexpr int NC = D / 32;
     constexpr uint32_t kTileBytes = kBV * D * sizeof(float);
     extern __shared__ __align__(128) unsigned char ring[];    // STAGES x RS::kBytes
-    __shared__ __align__(8) uint64_t bars[STAGES];
-    __shared__ __align__(8) int64_t pre[3];                   // next issue's bos, eos, slot
+    __shared__ __align__(8) uint64_t full[STAGES];
+    __shared__ __align__(8) uint64_t empty[STAGES];
 
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -404,94 +387,120 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
     const int64_t first = blockIdx.x, stride = gridDim.x;
     auto meta_of = [&](int st) { return reinterpret_cast<StageMeta *>(ring + st * RS::kBytes + RS::kMeta); };
 
-    // Thread 0: cu_seqlens and slot of the next item to issue, copied into
-    // shared memory one refill ahead of the issue.
-    auto prefetch = [&](int64_t it) {
-        if (it >= num_items) return;
-        const int req = static_cast<int>(it / nslice / p.head_count);
-        cp_async_index(&pre[0], p.cu_seqlens, p.index_bytes[1], req);
-        cp_async_index(&pre[1], p.cu_seqlens, p.index_bytes[1], req + 1);
-        cp_async_index(&pre[2], p.indices, p.index_bytes[0], req);
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    // Thread 0 fills stage `st` with item `it` (a plain arrive when nothing is
-    // copied, so the stage's phase always completes), then prefetches the
-    // metadata of the item it issues next (it + stride).
-    auto issue = [&](int64_t it, int st) {
-        if (it >= num_items) return;
-        unsigned char *stage = ring + st * RS::kBytes;
-        int64_t x = it / nslice;
-        StageMeta m;
-        m.h = p.head_begin + static_cast<int>(x % p.head_count);
-        m.req = static_cast<int>(x / p.head_count);
-        m.v0 = static_cast<int>(it % nslice) * kBV;
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        m.bos = read_index(&pre[0], p.index_bytes[1]);
-        m.eos = read_index(&pre[1], p.index_bytes[1]);
-        m.slot = read_index(&pre[2], p.index_bytes[0]);
-        m.tslot = 0;
-        m.tlen = -1;
-        m.ok = 1;
-        if (m.bos < 0 || m.eos < m.bos || m.eos > p.num_tokens) {
-            report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
-            m.ok = 0;
-        } else if (m.slot < 0 || m.slot >= p.num_slots) {
-            report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
-            m.ok = 0;
-        } else if (p.track_indices != nullptr) {
-            m.tslot = load_index(p.track_indices, p.index_bytes[2], m.req);
-            if (m.tslot < 0 || m.tslot >= p.num_slots) {
-                report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
-                m.ok = 0;
-            } else if (m.tslot > 0) {
-                m.tlen = load_index(p.track_lens, p.index_bytes[3], m.req);
-            }
-        }
-        *meta_of(st) = m;
-        const bool st_in = m.ok && m.slot > 0;
-        const bool tk_in = m.ok && tok_bulk && m.bos < m.eos;
-        const uint32_t bytes = (st_in ? kTileBytes : 0u) + (tk_in ? static_cast<uint32_t>(RS::kTokBytes) : 0u);
-        if (bytes > 0) {
-            mbar_arrive_expect_tx(&bars[st], bytes);
-            if (st_in)
-                bulk_g2s(stage,
-                         p.state + m.slot * p.state_stride[0] + m.h * p.state_stride[1] + static_cast<int64_t>(m.v0) * D,
-                         kTileBytes, &bars[st]);
-            if (tk_in) {
-                const int64_t row = m.bos * p.num_heads + m.h;
-                const uint8_t *gsrc = MODE == KDA_GATE_RAW ? static_cast<const uint8_t *>(p.a)
-                                                           : reinterpret_cast<const uint8_t *>(p.g);
-                bulk_g2s(stage + RS::kQ, static_cast<const uint8_t *>(p.q) + row * D * RS::QE, D * RS::QE, &bars[st]);
-                bulk_g2s(stage + RS::kK, static_cast<const uint8_t *>(p.k) + row * D * RS::QE, D * RS::QE, &bars[st]);
-                bulk_g2s(stage + RS::kG, gsrc + row * D * RS::GE, D * RS::GE, &bars[st]);
-                bulk_g2s(stage + RS::kV, static_cast<const uint8_t *>(p.v) + (row * D + m.v0) * 2, kBV * 2, &bars[st]);
-            }
-        } else {
-            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&bars[st])) : "memory");
-        }
-        prefetch(it + stride);
-    };
-
     if (tid == 0) {
 #pragma unroll
-        for (int st = 0; st < STAGES; ++st) mbar_init(&bars[st], 1);
+        for (int st = 0; st < STAGES; ++st) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], kRecThreads / 32);
+        }
         fence_mbar_init();
-        prefetch(first);
-#pragma unroll
-        for (int st = 0; st < STAGES; ++st) issue(first + st * stride, st);
     }
-    __syncthreads();   // the prologue stages' headers are written
+    __syncthreads();
 
-    // beta of the first item; later items' are read one item ahead.
-    float bcur = 0.f;
-    if (first < num_items) {
-        const StageMeta m0 = *meta_of(0);
-        if (m0.ok && m0.bos < m0.eos) bcur = load_bval<MODE>(p, m0.bos, m0.h);
+    if (warp == kRecThreads / 32) {
+        // ===== producer =====
+        if (lane != 0) return;
+        int st = 0;
+        uint32_t use = 0;   // how many times stage st has been filled
+        for (int64_t it = first; it < num_items; it += stride) {
+            if (use > 0 && !mbar_wait(&empty[st], (use - 1) & 1u, p.status)) return;
+            unsigned char *stage = ring + st * RS::kBytes;
+            StageMeta *hdr = meta_of(st);
+            const int64_t x = it / nslice;
+            const int h = p.head_begin + static_cast<int>(x % p.head_count);
+            const int req = static_cast<int>(x / p.head_count);
+            const int v0 = static_cast<int>(it % nslice) * kBV;
+            const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
+            const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
+            const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
+            int ok = 1;
+            int64_t tslot = 0, tlen = -1;
+            if (bos < 0 || eos < bos || eos > p.num_tokens) {
+                report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
+                ok = 0;
+            } else if (slot < 0 || slot >= p.num_slots) {
+                report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+                ok = 0;
+            } else if (p.track_indices != nullptr) {
+                tslot = load_index(p.track_indices, p.index_bytes[2], req);
+                if (tslot < 0 || tslot >= p.num_slots) {
+                    report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+                    ok = 0;
+                } else if (tslot > 0) {
+                    tlen = load_index(p.track_lens, p.index_bytes[3], req);
+                }
+            }
+            // beta (raw b) of the first token into the header by a 4-byte
+            // cp.async that the stage's barrier also waits for (its tracking
+            // arrive precedes the expect-tx arrive, so the phase cannot
+            // complete without it). The raw b is 2 bytes: its aligned word is
+            // copied only when that word lies inside the tensor.
+            const char *bsrc = nullptr;
+            int bsel = 0;
+            if (ok && bos < eos) {
+                const int64_t bi = bos * p.num_heads + h;
+                if constexpr (MODE == KDA_GATE_RAW) {
+                    if ((bi | 1) < static_cast<int64_t>(p.num_tokens) * p.num_heads) {
+                        bsrc = reinterpret_cast<const char *>(static_cast<const uint16_t *>(p.b) + (bi & ~int64_t(1)));
+                        bsel = 1 + static_cast<int>(bi & 1);
+                    }
+                } else {
+                    bsrc = reinterpret_cast<const char *>(p.beta + bi);
+                    bsel = 1;
+                }
+            }
+            hdr->bos = bos;
+            hdr->eos = eos;
+            hdr->slot = slot;
+            hdr->tslot = tslot;
+            hdr->tlen = tlen;
+            hdr->req = req;
+            hdr->h = h;
+            hdr->v0 = v0;
+            hdr->ok = ok;
+            hdr->bsel = bsel;   // bword is written only by the copy below
+            if (bsrc != nullptr) {
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(&hdr->bword)), "l"(bsrc)
+                             : "memory");
+                asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_addr(&full[st]))
+                             : "memory");
+            }
+            const bool st_in = ok && slot > 0;
+            const bool tk_in = ok && tok_bulk && bos < eos;
+            const uint32_t bytes = (st_in ? kTileBytes : 0u) + (tk_in ? static_cast<uint32_t>(RS::kTokBytes) : 0u);
+            if (bytes > 0) {
+                mbar_arrive_expect_tx(&full[st], bytes);
+                if (st_in)
+                    bulk_g2s(stage, p.state + slot * p.state_stride[0] + h * p.state_stride[1] + static_cast<int64_t>(v0) * D,
+                             kTileBytes, &full[st]);
+                if (tk_in) {
+                    const int64_t row = bos * p.num_heads + h;
+                    const uint8_t *gsrc = MODE == KDA_GATE_RAW ? static_cast<const uint8_t *>(p.a)
+                                                               : reinterpret_cast<const uint8_t *>(p.g);
+                    bulk_g2s(stage + RS::kQ, static_cast<const uint8_t *>(p.q) + row * D * RS::QE, D * RS::QE,
+                             &full[st]);
+                    bulk_g2s(stage + RS::kK, static_cast<const uint8_t *>(p.k) + row * D * RS::QE, D * RS::QE,
+                             &full[st]);
+                    bulk_g2s(stage + RS::kG, gsrc + row * D * RS::GE, D * RS::GE, &full[st]);
+                    bulk_g2s(stage + RS::kV, static_cast<const uint8_t *>(p.v) + (row * D + v0) * 2, kBV * 2,
+                             &full[st]);
+                }
+            } else {
+                mbar_arrive(&full[st]);
+            }
+            if (++st == STAGES) {
+                st = 0;
+                ++use;
+            }
+        }
+        return;
     }
-    int st = 0;              // item n's stage, n % STAGES
-    uint32_t phase = 0;      // (n / STAGES) & 1
+
+    // ===== compute warps =====
+    int st = 0;
+    uint32_t phase = 0;
     for (int64_t it = first; it < num_items; it += stride) {
-        if (!mbar_wait(&bars[st], phase, p.status)) return;
+        if (!mbar_wait(&full[st], phase, p.status)) return;
         const unsigned char *stage = ring + st * RS::kBytes;
         const StageMeta sm = *meta_of(st);
         Item m;
@@ -519,22 +528,17 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
 #pragma unroll
                 for (int e = 0; e < D / 8; ++e) s[j][e] = 0.f;
         }
-        // beta of the next item (its header was written and published by a
-        // barrier at least one item ago).
-        float bnext = 0.f;
-        const int st_next = st + 1 == STAGES ? 0 : st + 1;
-        if (it + stride < num_items) {
-            const StageMeta mn = *meta_of(st_next);
-            if (mn.ok && mn.bos < mn.eos) bnext = load_bval<MODE>(p, mn.bos, mn.h);
+        TokenRaw<D, MODE> cur;
+        const bool staged = ok && tok_bulk && m.bos < m.eos;
+        if (staged) token_from_stage<D, MODE>(cur, p, stage, sm, sub, row0);
+        // This warp is done with the stage.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (ok) run_item<D, MODE, true>(p, m, s, row0, sub, cur, staged);
+        if (++st == STAGES) {
+            st = 0;
+            phase ^= 1u;
         }
-        if (ok) run_item<D, MODE, true>(p, m, s, row0, sub, tok_bulk ? stage : nullptr, bcur);
-        // The stage's rows and token have been read: refill it, STAGES - 1
-        // items ahead of its next use.
-        __syncthreads();
-        if (tid == 0) issue(it + STAGES * stride, st);
-        bcur = bnext;
-        if (st_next == 0) phase ^= 1u;
-        st = st_next;
     }
 }
 
@@ -567,7 +571,8 @@ recurrent_strided_kernel(const KdaArgs p, int nslice) {
 #pragma unroll
             for (int e = 0; e < NE; ++e) s[j][e] = 0.f;
     }
-    run_item<D, MODE, false>(p, m, s, row0, sub);
+    TokenRaw<D, MODE> cur;
+    run_item<D, MODE, false>(p, m, s, row0, sub, cur, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -629,13 +634,14 @@ static bool mid_fast(const KdaArgs *a) {
            a->mid_stride[0] % 4 == 0 && a->mid_stride[1] % 4 == 0 && a->mid_stride[2] % 4 == 0;
 }
 
-// Ring depth and resident CTAs per SM (three: shared memory holds three CTAs
-// of four 17 KiB stages; a three-stage ring at four CTAs per SM measured
-// slower).
+// Ring depth and resident CTAs per SM: four compute warps and a producer
+// warp per CTA at up to 168 registers allow two CTAs per SM (three would cap
+// registers at 136 and spill); shared memory then holds six 17 KiB stages per
+// CTA.
 template <int MODE>
 struct RingShape {
-    static constexpr int kStages = 4;
-    static constexpr int kMinBlocks = 3;
+    static constexpr int kStages = 6;
+    static constexpr int kMinBlocks = 2;
 };
 
 struct DeviceInfo {
@@ -672,7 +678,7 @@ static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st) {
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
             int n = 0;
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, recurrent_ring_kernel<D, MODE, RingShape<MODE>::kStages, RingShape<MODE>::kMinBlocks>,
-                                                          kRecThreads, smem);
+                                                          kRecThreads + 32, smem);
             per_sm[dev] = n > 0 ? n : 1;
         }
         const int64_t cap = static_cast<int64_t>(sm_count()) * per_sm[dev];
@@ -682,7 +688,7 @@ static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st) {
         const void *gate = MODE == KDA_GATE_RAW ? static_cast<const void *>(a->a) : static_cast<const void *>(a->g);
         const int tok_bulk = aligned16(a->q) && aligned16(a->k) && aligned16(gate) && aligned16(a->v) ? 1 : 0;
         recurrent_ring_kernel<D, MODE, RingShape<MODE>::kStages, RingShape<MODE>::kMinBlocks>
-            <<<static_cast<unsigned>(grid), kRecThreads, smem, st>>>(*a, nslice, items, tok_bulk);
+            <<<static_cast<unsigned>(grid), kRecThreads + 32, smem, st>>>(*a, nslice, items, tok_bulk);
     } else {
         recurrent_strided_kernel<D, MODE><<<static_cast<unsigned>(items), kRecThreads, 0, st>>>(*a, nslice);
     }
