@@ -19,6 +19,9 @@ _HERE = Path(__file__).resolve().parent
 LIB_PATH = _HERE / "libkda_b200.so"
 
 KDA_OK = 0
+# KdaStatus (include/kda_b200.h)
+(KDA_ERR_INVALID_ARGUMENT, KDA_ERR_UNSUPPORTED, KDA_ERR_ALIGNMENT, KDA_ERR_WORKSPACE, KDA_ERR_LAUNCH,
+ KDA_ERR_TOO_LARGE) = range(1, 7)
 KDA_GATE_RAW, KDA_GATE_LOG, KDA_GATE_PREPARED = 0, 1, 2
 
 # Entry points declared in include/kda_b200.h.

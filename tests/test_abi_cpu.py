@@ -42,6 +42,14 @@ def test_header_functions_are_exported(abi):
     assert lib.kda_abi_version() == 1
 
 
+def test_status_codes_match_header(abi):
+    """abi.py's KdaStatus constants are the header's values."""
+    codes = dict(re.findall(r"\b(KDA_(?:OK|ERR_[A-Z_]+))\s*=\s*(\d+)", HEADER.read_text()))
+    assert len(codes) == 7
+    for name, value in codes.items():
+        assert getattr(abi, name) == int(value), name
+
+
 @pytest.mark.parametrize("struct", ["KdaArgs", "KdaCommitArgs"])
 def test_struct_layout_matches_header(abi, tmp_path, struct):
     cls = getattr(abi, struct)
