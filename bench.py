@@ -66,7 +66,7 @@ DECODE_BYTES_PER_TOKEN_HEAD = 65536 * 2 + 768 + 512 + 4 + 256
 # decode at the benchmark shape; chunk prefill captured with 8 of config 3's
 # 32 heads (412,781,824 B) and scaled by 4, traffic being proportional to the
 # heads processed.
-DECODE_TRAFFIC_PER_LAUNCH = 1026374144
+DECODE_TRAFFIC_PER_LAUNCH = 1025897216
 PREFILL_TRAFFIC_PER_LAUNCH = 1651127296
 
 METRIC = "KDA tokens/s (prefill, decode) H32 d128 @1/2/4/8 B200; decode HBM GB/s vs peak"

@@ -239,6 +239,51 @@ def test_int64_metadata_bitwise(ops):
     assert torch.equal(a["initial_state_source"], b["initial_state_source"])
 
 
+def test_chunk_launch_phases_matches_launch(ops, chunk_path):
+    """The measurement hook runs the same split path: bit-identical outputs and
+    pool, six ordered events; a batch that takes the fused kernel is refused."""
+    if chunk_path != "auto":
+        pytest.skip("one run suffices")
+    from sgl_glm53_ascend_ops import abi
+    kw = _case(2, [0, 3000, 3001], [1, 2], ([3, 0], [1024, 0]), seed=41)
+    runs = []
+    for phases in (False, True):
+        d = _dev(kw)
+        pool = d["initial_state_source"]
+        out = torch.empty(d["v"].shape, dtype=torch.bfloat16, device=DEV)
+        a = abi.args_from_tensors(q=d["q"], k=d["k"], v=d["v"], out=out, state=pool,
+                                  indices=d["initial_state_indices"], cu_seqlens=d["cu_seqlens"], scale=d["scale"],
+                                  gate_mode=abi.KDA_GATE_RAW, a=d["a"], b=d["b"], A_log=d["A_log"],
+                                  dt_bias=d["dt_bias"], lower_bound=d["lower_bound"],
+                                  track_indices=d["track_state_indices"], track_lens=d["track_state_lens"])
+        n = abi.chunk_workspace_bytes(2, 3001, 2, 128)
+        ws = torch.empty(n, dtype=torch.uint8, device=DEV)
+        if phases:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            for e in ev:
+                e.record()
+            assert abi.chunk_launch_phases(a, ws, n, ev) == abi.KDA_OK
+        else:
+            assert abi.chunk_launch(a, ws, n) == abi.KDA_OK
+        torch.cuda.synchronize()
+        runs.append((out.cpu(), pool.cpu()))
+        if phases:
+            assert all(ev[i].elapsed_time(ev[i + 1]) >= 0 for i in range(5))
+    assert torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1])
+    # 64 one-chunk requests x 32 heads: the fused kernel's batch.
+    big = _dev(_case(32, [64 * i for i in range(65)], [0] * 64, seed=42))
+    a = abi.args_from_tensors(q=big["q"], k=big["k"], v=big["v"], out=torch.empty_like(big["v"]),
+                              state=big["initial_state_source"], indices=big["initial_state_indices"],
+                              cu_seqlens=big["cu_seqlens"], scale=big["scale"], gate_mode=abi.KDA_GATE_RAW,
+                              a=big["a"], b=big["b"], A_log=big["A_log"], dt_bias=big["dt_bias"],
+                              lower_bound=big["lower_bound"])
+    ws = torch.empty(1 << 20, dtype=torch.uint8, device=DEV)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in ev:
+        e.record()
+    assert abi.chunk_launch_phases(a, ws, 1 << 20, ev) == abi.KDA_ERR_UNSUPPORTED
+
+
 def test_chunk_cuda_graph_replay(ops):
     """Capture once; replay with new cu_seqlens/slots/values behind the pointers
     (test_glm53_kda_prefix_ascendc.py:185-293, chunk op, no host sync)."""
