@@ -197,19 +197,26 @@ def time_steps(fn, steps: int, warmup: int, dist: Dist, stream=None):
 def time_e2e(host: dict, run, out_shape, steps: int, warmup: int, dist: Dist):
     """Per-step device milliseconds of the op end to end from pinned host
     buffers, pipelined as a serving loop runs it: while step i computes on the
-    current stream, step i+1's inputs copy host->device on a copy stream (two
-    device input sets, each reused only after the op that read it is done),
-    and step i's bf16 output is read back into pinned host memory on a third
-    stream. The timed region holds exactly `steps` input copies and `steps`
+    current stream, step i+1's inputs copy host->device on two copy streams
+    (the inputs split between them by size, so two copy engines share the
+    link; two device input sets, each reused only after the op that read it is
+    done), and step i's bf16 output is read back into pinned host memory on a
+    further stream. The timed region holds exactly `steps` input copies and `steps`
     read-backs: it opens before the copy for the first timed step's successor
     and closes after the last copy and the last read-back have finished.
     Returns (ms per step, host->device bytes per step, device->host bytes per
     step)."""
     cs = torch.cuda.current_stream()
-    xs, ds = torch.cuda.Stream(), torch.cuda.Stream()
+    xss, ds = (torch.cuda.Stream(), torch.cuda.Stream()), torch.cuda.Stream()
     devs = [{n: torch.empty_like(t, device="cuda") for n, t in host.items()} for _ in range(2)]
     out_host = [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    copied = [torch.cuda.Event(), torch.cuda.Event()]
+    # inputs -> copy stream, largest first onto the less loaded one
+    groups, load = ([], []), [0, 0]
+    for n, t in sorted(host.items(), key=lambda kv: -kv[1].numel() * kv[1].element_size()):
+        g = 0 if load[0] <= load[1] else 1
+        groups[g].append(n)
+        load[g] += t.numel() * t.element_size()
+    copied = [[torch.cuda.Event(), torch.cuda.Event()] for _ in range(2)]   # [set][stream]
     used = [torch.cuda.Event(), torch.cuda.Event()]
     read = torch.cuda.Event()
     h2d = sum(t.numel() * t.element_size() for t in host.values())
@@ -217,16 +224,21 @@ def time_e2e(host: dict, run, out_shape, steps: int, warmup: int, dist: Dist):
     it = [0]
 
     def copy_in(b):
-        xs.wait_event(used[b])                 # the op that last read set b has finished
-        with torch.cuda.stream(xs):
-            for n, t in host.items():
-                devs[b][n].copy_(t, non_blocking=True)
-        copied[b].record(xs)
+        for k, xs in enumerate(xss):
+            xs.wait_event(used[b])             # the op that last read set b has finished
+            with torch.cuda.stream(xs):
+                for n in groups[k]:
+                    devs[b][n].copy_(host[n], non_blocking=True)
+            copied[b][k].record(xs)
+
+    def wait_copied(b):
+        for ev in copied[b]:
+            cs.wait_event(ev)
 
     def e2e_step():
         b = it[0] & 1
         copy_in(b ^ 1)                         # inputs of the next step
-        cs.wait_event(copied[b])
+        wait_copied(b)
         o = run(devs[b])
         used[b].record(cs)
         ds.wait_stream(cs)
@@ -243,13 +255,14 @@ def time_e2e(host: dict, run, out_shape, steps: int, warmup: int, dist: Dist):
     dist.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(cs)
-    xs.wait_event(start)                       # no timed copy starts before the region opens
+    for xs in xss:
+        xs.wait_event(start)                   # no timed copy starts before the region opens
     # The first timed step's own inputs were copied during the last warm-up
     # step; its successor's copy is the first of the `steps` timed copies.
-    cs.wait_event(copied[it[0] & 1])
+    wait_copied(it[0] & 1)
     for _ in range(steps):
         e2e_step()
-    cs.wait_event(copied[it[0] & 1])           # the last timed copy
+    wait_copied(it[0] & 1)                     # the last timed copy
     cs.wait_event(read)                        # the last read-back
     end.record(cs)
     torch.cuda.synchronize()
@@ -312,8 +325,8 @@ def bench_decode(args, dist: Dist, hbm_gbs: float, peak_kind: str) -> dict:
     ems, h2d, d2h = time_e2e(host, run, w.v.shape, args.steps, args.warmup, dist)
     e2e = {"value": round(dist.world * tokens / (ems / 1e3), 1), "unit": "tokens/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 4),
-           "pipelining": "step i+1's inputs copy host->device on a copy stream while step i runs "
-                         "(two device input sets); each step's output is read back on a third stream"}
+           "pipelining": "step i+1's inputs copy host->device on two copy streams while step i runs "
+                         "(two device input sets); each step's output is read back on a further stream"}
     return dict(value=value, ms_per_step=ms_per_step, roofline=roofline, e2e=e2e, clocks=clocks,
                 gpu_launches=args.steps, tokens=tokens)
 
