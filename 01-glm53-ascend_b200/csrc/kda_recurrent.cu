@@ -210,14 +210,18 @@ __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float 
                 unpack_bf4(q + c * 4, cur.qb[c]);
                 unpack_bf4(k + c * 4, cur.kb[c]);
             }
-            float sq = 0.f, sk2 = 0.f;
+            // Two partial sums per reduction (even / odd elements): shorter
+            // dependent chains for the latency-bound item loop.
+            float sq0 = 0.f, sq1 = 0.f, sk0 = 0.f, sk1 = 0.f;
 #pragma unroll
-            for (int e = 0; e < NE; ++e) {
-                sq = fmaf(q[e], q[e], sq);
-                sk2 = fmaf(k[e], k[e], sk2);
+            for (int e = 0; e < NE; e += 2) {
+                sq0 = fmaf(q[e], q[e], sq0);
+                sq1 = fmaf(q[e + 1], q[e + 1], sq1);
+                sk0 = fmaf(k[e], k[e], sk0);
+                sk1 = fmaf(k[e + 1], k[e + 1], sk1);
             }
-            sq = sum8(sq);
-            sk2 = sum8(sk2);
+            const float sq = sum8(sq0 + sq1);
+            const float sk2 = sum8(sk0 + sk1);
             // One reciprocal per row instead of a division per element; the
             // product differs from q / ||q|| by at most an ulp.
             const float rq = p.scale / sqrtf(sq + kNormEps), rk = 1.0f / sqrtf(sk2 + kNormEps);
@@ -254,13 +258,15 @@ __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float 
         float pa[2];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            float acc = 0.f;
+            float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-            for (int e = 0; e < NE; ++e) {
+            for (int e = 0; e < NE; e += 2) {
                 s[j][e] *= dec[e];
-                acc = fmaf(s[j][e], kn[e], acc);
+                s[j][e + 1] *= dec[e + 1];
+                a0 = fmaf(s[j][e], kn[e], a0);
+                a1 = fmaf(s[j][e + 1], kn[e + 1], a1);
             }
-            pa[j] = acc;
+            pa[j] = a0 + a1;
         }
         pa[0] = sum8(pa[0]);
         pa[1] = sum8(pa[1]);
@@ -269,13 +275,15 @@ __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float 
         for (int j = 0; j < 2; ++j) {
             const float vv = __uint_as_float(static_cast<uint32_t>(cur.vb[j]) << 16);
             const float d = (vv - pa[j]) * beta;
-            float acc = 0.f;
+            float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-            for (int e = 0; e < NE; ++e) {
+            for (int e = 0; e < NE; e += 2) {
                 s[j][e] = fmaf(kn[e], d, s[j][e]);
-                acc = fmaf(s[j][e], qn[e], acc);
+                s[j][e + 1] = fmaf(kn[e + 1], d, s[j][e + 1]);
+                a0 = fmaf(s[j][e], qn[e], a0);
+                a1 = fmaf(s[j][e + 1], qn[e + 1], a1);
             }
-            po[j] = acc;
+            po[j] = a0 + a1;
         }
         po[0] = sum8(po[0]);
         po[1] = sum8(po[1]);
