@@ -413,16 +413,21 @@ __device__ __forceinline__ int fr(int r, int c) { return ((c >> 3) * R + r) * 8 
 // affine, S_{c+1} = A_c S_c + B_c (A_c = diag(e^{gl}) - KD^T W, B_c = KD^T u),
 // so a long sequence is cut into P segments of about L chunks that scan side
 // by side: segment 0 from the true initial state, and segments 1..P-2 twice,
-// once from zero (their B) and once from the identity with u = 0 (their A).
-// A combine step then chains S_start[i+1] = A_i S_start[i] + B_i, and segments
-// 1..P-1 rescan from their true start states, storing the splits the output
-// kernel reads. Two segments gain nothing, so a sequence has 1 or >= 3.
+// once from zero (their B) and once from the identity with u = 0 (their A);
+// both chains also leave their state at the segment's midpoint, and the last
+// segment gets the same two chains over its first half only. A combine step
+// then chains S_start[i+1] = A_i S_start[i] + B_i, and every segment i >= 1
+// rescans as two halves side by side: the first from S_start[i], the second
+// from S_mid[i] = A_mid,i S_start[i] + B_mid,i, one product in its prologue.
+// The rescan stores the splits the output kernel reads. Two segments gain
+// nothing, so a sequence has 1 or >= 3.
 //
 // The plan (int32 words in the workspace, written by plan_kernel):
 //   [0] state-slot capacity, [1] first-pass task count, [2] rescan task
 //   count, [3] task capacity, then per request: segments P_r, segment length
 //   L_r (chunks), first state slot; then the first-pass and rescan task lists.
-// A task is req | kind << 10 | segment << 12.
+// A task is req | kind << 10 | half << 12 | segment << 13 (half: a chain over
+// the first half of a segment only, or the second half of a rescan).
 enum : int { kTaskTrue = 0, kTaskZero = 1, kTaskIdent = 2 };
 constexpr int kMinSegChunks = 8;
 struct PlanView {
@@ -437,7 +442,11 @@ struct PlanView {
         return 4 + 3 * static_cast<size_t>(num_req) + 2 * static_cast<size_t>(task_cap);
     }
 };
-__device__ __forceinline__ int32_t task_word(int req, int kind, int seg) { return req | (kind << 10) | (seg << 12); }
+__device__ __forceinline__ int32_t task_word(int req, int kind, int seg, int half = 0) {
+    return req | (kind << 10) | (half << 12) | (seg << 13);
+}
+// State-slot kinds per (request, segment >= 1, head).
+enum : int { kSlotStart = 0, kSlotB = 1, kSlotA = 2, kSlotBmid = 3, kSlotAmid = 4, kSlotKinds = 5 };
 // State exchange layout of one D x D fp32 state S^T (value row v, key column
 // k): float at ((k / 4) D + v) * 4 + k % 4, so a warp's 32 rows of one float4
 // column are 512 contiguous bytes. Slot `slot` of kind `which` (0 start
@@ -1575,7 +1584,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     if (ti >= plan[1 + phase]) return;
     const PlanView pv(const_cast<int32_t *>(plan), p.num_req, plan[3]);
     const int32_t task = pv.tasks(phase)[ti];
-    const int req = task & 1023, kind = (task >> 10) & 3, seg = task >> 12;
+    const int req = task & 1023, kind = (task >> 10) & 3, half = (task >> 12) & 1, seg = task >> 13;
     const int nseg = pv.segs()[req], seglen = pv.seglen()[req];
     const bool truth = kind == kTaskTrue;
     const int slot_cap = plan[0];
@@ -1599,11 +1608,19 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         }
         if (tslot > 0) tlen = load_index(p.track_lens, p.index_bytes[3], req);
     }
-    // This task's chunks [c0, c0 + nchunks) of the request; below, chunk
-    // indices are relative to c0.
+    // This task's chunks [c0, c0 + nchunks) of the request (below, chunk
+    // indices are relative to c0). Segment `seg` spans [seg L, seg L + len);
+    // its midpoint is `mid` chunks in. A first-pass chain covers the segment
+    // (or, with `half`, its first half) and leaves its state at the midpoint;
+    // a rescan half covers [0, mid) or [mid, len) of the segment.
     const int req_chunks = static_cast<int>((eos - bos + BT - 1) / BT);
-    const int c0 = seg * seglen;
-    const int nchunks = max(0, min(req_chunks, c0 + seglen) - c0);
+    const int seg0 = seg * seglen;
+    const int seg_len = max(0, min(req_chunks, seg0 + seglen) - seg0);
+    const int mid = (seg_len + 1) / 2;
+    const bool rescan2 = truth && seg > 0 && half;          // second half of a rescan
+    const int c0 = rescan2 ? seg0 + mid : seg0;
+    const int nchunks = truth ? (seg == 0 ? seg_len : (half ? seg_len - mid : mid)) : (half ? mid : seg_len);
+    const int mid_at = truth ? -1 : mid;                    // local chunk of the midpoint state
     const int64_t s0 = p.state_stride[0], s1 = p.state_stride[1], sk = p.state_stride[2], sv = p.state_stride[3];
     auto trk_at = [&](int c) {
         const int64_t rt = tlen - static_cast<int64_t>(c0 + c) * BT;
@@ -1638,9 +1655,28 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 
     if (warp == kThreads / 32) {
         // ===== producer =====
+        constexpr uint32_t id_kd = idesc_bf16(128, D, false, true, false);
+        if (lane == 0 && rescan2) {
+            // S_mid^T = S_start^T A_mid^T + B_mid^T: the compute warps staged
+            // S_start^T's split (tensor memory), B_mid^T (the accumulator) and
+            // A_mid^T as MN-major hi/lo tiles in the W and KD slots.
+            if (!mbar_wait(mb + 14, 0, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+                const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
+                const uint64_t xh = sdesc(s_base + L::kX + kk * 2048, D * 128, 1024);
+                const uint64_t xl = sdesc(s_base + L::kZ + kk * 2048, D * 128, 1024);
+                umma_ts(tmem + kColS, al, xh, id_kd, 1u);
+                umma_ts(tmem + kColS, ah, xl, id_kd, 1u);
+                umma_ts(tmem + kColS, ah, xh, id_kd, 1u);
+            }
+            umma_commit(mb + 0);
+            // the W and KD slots take their records once the product is done
+            if (!mbar_wait(mb + 0, 0, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+        }
         if (lane == 0 && nchunks > 0) {
             constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
-            constexpr uint32_t id_kd = idesc_bf16(128, D, false, true, false);
             auto pwait = [&](uint64_t *b, uint32_t ph) {
                 if (!mbar_wait(b, ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             };
@@ -1729,7 +1765,52 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         // Initial state S^T -> tensor memory: the pool slot (a length-0
         // checkpoint is the initial state), a segment's exchanged start state,
         // zero, or the identity.
-        {
+        if (rescan2) {
+            // Second half of a rescanned segment: stage the operands of
+            // S_mid^T = S_start^T A_mid^T + B_mid^T for the producer.
+            const bool row_ok = srow < D;
+            uint32_t r[SC], hi[SC / 2], lo[SC / 2];
+            auto load_row = [&](const float *src) {
+#pragma unroll
+                for (int e = 0; e < SC / 4; ++e) {
+                    const float4 x = row_ok ? *reinterpret_cast<const float4 *>(src + ((SC / 4 * cs + e) * D + srow) * 4)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                    r[4 * e] = __float_as_uint(x.x);
+                    r[4 * e + 1] = __float_as_uint(x.y);
+                    r[4 * e + 2] = __float_as_uint(x.z);
+                    r[4 * e + 3] = __float_as_uint(x.w);
+                }
+            };
+            load_row(xslot(kSlotStart, seg));
+#pragma unroll
+            for (int e = 0; e < SC / 2; ++e)
+                split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
+            tmem_st<SC / 2>(tq + kColSH + (SC / 2) * cs, hi);
+            tmem_st<SC / 2>(tq + kColSL + (SC / 2) * cs, lo);
+            load_row(xslot(kSlotBmid, seg));
+            tmem_st<SC>(tq + kColS + SC * cs, r);
+            // A_mid^T (rows j, columns k) -> swizzled bf16 hi/lo tiles, 64-column
+            // blocks of D rows x 128 B: hi in the W slot, lo in the KD slot.
+            const float *am = xslot(kSlotAmid, seg);
+#pragma unroll
+            for (int e = 0; e < D * D / 4 / kThreads; ++e) {
+                const int q = tid + kThreads * e, j = q % D, k = 4 * (q / D);
+                const float4 x = *reinterpret_cast<const float4 *>(am + static_cast<int64_t>(q) * 4);
+                uint32_t h0, h1, l0, l1;
+                split2(x.x, x.y, h0, l0);
+                split2(x.z, x.w, h1, l1);
+                const int o = ((k >> 6) * (D * 64) + swz<64>(j, k & 63)) * 2;
+                *reinterpret_cast<uint2 *>(sm + L::kX + o) = make_uint2(h0, h1);
+                *reinterpret_cast<uint2 *>(sm + L::kZ + o) = make_uint2(l0, l1);
+            }
+            fence_async_smem();
+            tmem_st_wait();
+            tc_fence_before();
+            nbar(1, kThreads);
+            if (tid == 0) mbar_arrive(mb + 14);
+            if (!mbar_wait(mb + 0, 0, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            tc_fence_after();
+        } else {
             const bool row_ok = srow < D;
             uint32_t r[SC];
             if (truth && seg == 0) {
@@ -1818,6 +1899,15 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                         make_uint4(lo[4 * q8], lo[4 * q8 + 1], lo[4 * q8 + 2], lo[4 * q8 + 3]);
                 }
             }
+            // A first-pass chain leaves the state at its segment's midpoint.
+            if (c == mid_at && srow < D) {
+                float *xs = xslot(kind + 2, seg);
+#pragma unroll
+                for (int e = 0; e < SC / 4; ++e)
+                    *reinterpret_cast<float4 *>(xs + ((SC / 4 * cs + e) * D + srow) * 4) =
+                        make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                    __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+            }
             cwait(lEgl, ph);
             if (!trk) {
                 const float *eg = vec + L::vEgl + SC * cs;
@@ -1887,14 +1977,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             uint32_t r[SC];
             tmem_ld<SC>(tq + kColS + SC * cs, r);
             tmem_ld_wait();
-            if (truth && seg == nseg - 1) {
-                float *hs = p.state + slot * s0 + h * s1;
-                if (slot > 0 && srow < D) {
-#pragma unroll
-                    for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
-                }
-            } else if (!truth || seg == 0) {
-                float *xs = truth ? xslot(0, 1) : xslot(kind, seg);
+            auto put = [&](float *xs) {
                 if (srow < D) {
 #pragma unroll
                     for (int e = 0; e < SC / 4; ++e)
@@ -1902,6 +1985,20 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                             make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
                                         __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
                 }
+            };
+            if (truth && seg == nseg - 1 && (nseg == 1 || half)) {
+                float *hs = p.state + slot * s0 + h * s1;
+                if (slot > 0 && srow < D) {
+#pragma unroll
+                    for (int e = 0; e < SC; ++e) hs[srow * sv + (SC * cs + e) * sk] = __uint_as_float(r[e]);
+                }
+            } else if (truth && seg == 0) {
+                put(xslot(kSlotStart, 1));
+            } else if (!truth) {
+                // a full chain ends with its B or A; a half chain's end is its
+                // midpoint state (as is a one-chunk segment's)
+                if (!half) put(xslot(kind, seg));
+                if (half || mid_at == nchunks) put(xslot(kind + 2, seg));
             }
         }
     }
@@ -2556,9 +2653,11 @@ __global__ void __launch_bounds__(1024) plan_kernel(const KdaArgs p, int32_t *cb
     if (live) cbase[r] = cb;
     if (r == 0) cbase[p.num_req] = total;
     auto segs = [&](int L) { return n <= L ? 1 : max(3, (n + L - 1) / L); };
+    // First-pass CTAs per request: segment 0, two chains per middle segment,
+    // two half chains for the last (the rescan needs 2 (P - 1), fewer).
     auto cost = [&](int L) {
         const int P = segs(L);
-        return live ? (P == 1 ? 1 : 2 * P - 3) : 0;
+        return live ? (P == 1 ? 1 : 2 * P - 1) : 0;
     };
     const int maxn = block_max(n, tmp);
     int hi = max(maxn, kMinSegChunks), lo = kMinSegChunks;
@@ -2579,19 +2678,22 @@ __global__ void __launch_bounds__(1024) plan_kernel(const KdaArgs p, int32_t *cb
     const PlanView pv(plan, p.num_req, task_cap);
     const int P = live ? segs(L) : 0;
     int na, nc;
-    const int oa = block_scan(live ? (P == 1 ? 1 : 2 * P - 3) : 0, tmp, na);
-    const int oc = block_scan(P >= 3 ? P - 1 : 0, tmp, nc);
+    const int oa = block_scan(live ? (P == 1 ? 1 : 2 * P - 1) : 0, tmp, na);
+    const int oc = block_scan(P >= 3 ? 2 * (P - 1) : 0, tmp, nc);
+    const int os = block_scan(P >= 3 ? P - 1 : 0, tmp, total);   // state slots
     if (live) {
         pv.segs()[r] = P;
         pv.seglen()[r] = (n + P - 1) / P;
-        pv.sbase()[r] = oc;
+        pv.sbase()[r] = os;
         int32_t *ta = pv.tasks(0), *tc = pv.tasks(1);
         ta[oa] = task_word(r, kTaskTrue, 0);
-        for (int sg = 1; sg + 1 < P; ++sg) {
-            ta[oa + 2 * sg - 1] = task_word(r, kTaskZero, sg);
-            ta[oa + 2 * sg] = task_word(r, kTaskIdent, sg);
+        for (int sg = 1; sg < P && P >= 3; ++sg) {
+            const int half = sg == P - 1 ? 1 : 0;
+            ta[oa + 2 * sg - 1] = task_word(r, kTaskZero, sg, half);
+            ta[oa + 2 * sg] = task_word(r, kTaskIdent, sg, half);
+            tc[oc + 2 * (sg - 1)] = task_word(r, kTaskTrue, sg, 0);
+            tc[oc + 2 * (sg - 1) + 1] = task_word(r, kTaskTrue, sg, 1);
         }
-        for (int sg = 1; sg < P && P >= 3; ++sg) tc[oc + sg - 1] = task_word(r, kTaskTrue, sg);
     }
     if (r == 0) {
         plan[0] = slot_cap;
@@ -2743,7 +2845,8 @@ static SplitLayout split_layout(int32_t num_req, int32_t num_tokens, int32_t hea
     l.trec = l.rec + slots * static_cast<size_t>(heads) * rb;
     l.sout = l.trec + static_cast<size_t>(num_req) * static_cast<size_t>(heads) * tb;
     l.states = l.sout + slots * static_cast<size_t>(heads) * ob;
-    l.total = l.states + 3 * static_cast<size_t>(l.slot_cap) * static_cast<size_t>(heads) * D * D * sizeof(float);
+    l.total = l.states + static_cast<size_t>(chunk::kSlotKinds) * static_cast<size_t>(l.slot_cap) *
+                             static_cast<size_t>(heads) * D * D * sizeof(float);
     return l;
 }
 
