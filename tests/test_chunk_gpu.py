@@ -169,15 +169,21 @@ def test_loggate_matches_oracle(ops):
 
 
 # Requests long enough (and heads few enough) that the split path cuts them
-# into segments: a first pass from zero and from the identity per segment, the
-# combine of the segment transfers, and a rescan from the true start states.
-# Mixed with short requests that stay whole; checkpoints at 0, inside segment
-# 0, on a segment boundary, inside a middle and the last segment, at the end.
+# into segments: a first pass from zero and from the identity per segment
+# (leaving midpoint states too), the combine of the segment transfers, and a
+# rescan of each segment as two halves from the true start and midpoint
+# states. Mixed with short requests that stay whole; checkpoints at 0, inside
+# segment 0, on a segment boundary, inside a middle and the last segment, in
+# either half, at the end.
 SEGMENTED = [
     (2, [0, 3000], [1], None),
     (1, [0, 3000, 3001, 5500, 6100, 8100], [1, 0, 2, 3, 7], ([4, 0, 5, 6, 0], [1024, 0, 2300, 300, 0])),
     (2, [0, 1500, 2800], [1, 2], ([3, 4], [0, 1300])),
     (3, [0, 1111, 1175], [2, 1], ([5, 6], [100, 64])),
+    # 17 chunks (checkpoint in the second half of the last segment) and 65
+    # chunks (a one-chunk last segment: its second half is empty, the final
+    # state comes from the midpoint product alone)
+    (1, [0, 1034, 5134], [1, 2], ([3, 4], [1034, 4100])),
 ]
 
 
