@@ -889,6 +889,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         if (nchunks > 0) load_beta(cprep);
 
         bool o_pending = false;   // the previous chunk's o^T waits in tensor memory
+        bool ox_busy = false;     // thread 0: an o tile store still reads the W region
         int64_t o_t0 = 0;
         int o_n = 0;
         for (int c = cprep; c < (PREP ? cprep + 1 : nchunks); ++c) {
@@ -899,7 +900,12 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             const bool has_next = !PREP && c + 1 < nchunks;
             if (!mbar_wait(&bars[2], static_cast<uint32_t>(PREP ? 0 : c & 1), p.status) && tid == 0)
                 report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
-            if (tid == 0) bulk_wait_read();   // a tracked chunk's o tile has left the W region
+            // A tracked chunk's o tile (thread 0's only store in flight) has
+            // left the W region before P2 rewrites it.
+            if (tid == 0 && ox_busy) {
+                bulk_wait_read();
+                ox_busy = false;
+            }
             if (n < BT) {
                 // The boxes cover 64 tokens; rows past this sequence's end hold the
                 // next sequence (or TMA's zero fill past T): clear them.
@@ -1493,7 +1499,10 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 o_cols(OstX, t0, n, 16 * cs, 16);
                 fence_async_smem();
                 cbar();
-                if (tid == 0) o_store(OstX, t0, n);
+                if (tid == 0) {
+                    o_store(OstX, t0, n);
+                    ox_busy = true;
+                }
                 float *ts = p.state + tslot * s0 + h * s1;
                 uint32_t r[SC];
                 tmem_ld<SC>(tq + kColTR + SC * cs, r);
