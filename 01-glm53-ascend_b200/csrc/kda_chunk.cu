@@ -338,10 +338,10 @@ struct Smem {
     static constexpr int kAp = 0;
     static constexpr int kT = kAp + BT * AS * 4;
     static constexpr int PS = 20;                          // row stride of the P scratch blocks
-    static constexpr int kP = kT + BT * AS * 4;            // fp32 [3][16][PS] inverse partial products
+    static constexpr int kP = kT + BT * AS * 4;            // fp32 [4][16][PS] inverse partial products
     // bf16 [64][D] o tile of the previous chunk, staged for its TMA store
     // while A', T and P occupy the front of the raw region.
-    static constexpr int kOst = r1k(kP + 3 * 16 * PS * 4);
+    static constexpr int kOst = r1k(kP + 4 * 16 * PS * 4);
     static constexpr int kOstEnd = kOst + BT * D * 2;
     static constexpr int kV = r1k(kRawEnd > kOstEnd ? kRawEnd : kOstEnd);   // bf16 f64 tile [j][v]
     // bf16 hi/lo f64 tiles (hi at the base, lo BT*D*2 bytes later):
@@ -1170,69 +1170,77 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
                 }
                 nbar(2, 128);
-                // Off-diagonal blocks by distance d = I - J, one block per warp:
-                // P = sum_{M=J}^{I-1} A'_IM T_MJ, then T_IJ = -T_II P, both as
-                // split-bf16 products (fp32 operands split into hi + lo).
-                float *const Pw = Pp + warp * 16 * L::PS;
+                // Off-diagonal blocks, 2x2 block-recursively: the inverse of
+                // [[M_A, 0], [A'_BA, M_B]] is [[T_A, 0], [-T_B A'_BA T_A, T_B]].
+                // Stage 1: T_10 and T_32 (the 32x32 diagonal halves); stage 2: the
+                // lower-left 32x32 quadrant, one 16x16 block per warp. Every
+                // product is split-bf16 (fp32 operands split into hi + lo).
+                // B fragments of a fp32 16x16 block at (r0, c0) of a row-major
+                // tile with row stride `ld`, columns [c0 + 8 nt, +8).
+                auto bfrag = [&](const float *base, int ld, int r0, int c0, int nt, uint32_t &bh0, uint32_t &bh1,
+                                 uint32_t &bl0, uint32_t &bl1) {
+                    const float *b = base + (r0 + 2 * t4) * ld + c0 + 8 * nt + g;
+                    split2(b[0], b[ld], bh0, bl0);
+                    split2(b[8 * ld], b[9 * ld], bh1, bl1);
+                };
+                auto afrag = [&](const float *base, int ld, int r0, int c0, uint32_t (&ah)[4], uint32_t (&al)[4]) {
+                    const float *a = base + (r0 + g) * ld + c0 + 2 * t4;
+                    const float2 a0 = *reinterpret_cast<const float2 *>(a);
+                    const float2 a1 = *reinterpret_cast<const float2 *>(a + 8 * ld);
+                    const float2 a2 = *reinterpret_cast<const float2 *>(a + 8);
+                    const float2 a3 = *reinterpret_cast<const float2 *>(a + 8 * ld + 8);
+                    split2(a0.x, a0.y, ah[0], al[0]);
+                    split2(a1.x, a1.y, ah[1], al[1]);
+                    split2(a2.x, a2.y, ah[2], al[2]);
+                    split2(a3.x, a3.y, ah[3], al[3]);
+                };
+                // acc[nt] += (16x16 block of `a` at (ar, ac)) x (block of `b` at (br, bc))
+                auto blk = [&](float (&acc)[2][4], const float *a, int lda, int ar, int ac, const float *b, int ldb,
+                               int br, int bc) {
+                    uint32_t ah[4], al[4];
+                    afrag(a, lda, ar, ac, ah, al);
 #pragma unroll
-                for (int d = 1; d <= 3; ++d) {
-                    if (warp < 4 - d) {
-                        const int J = warp, I = warp + d;
-                        // B fragments of a fp32 16x16 block at (r0, c0) of a row-major
-                        // tile with row stride `ld`, columns [c0 + 8 nt, +8).
-                        auto bfrag = [&](const float *base, int ld, int r0, int c0, int nt, uint32_t &bh0,
-                                         uint32_t &bh1, uint32_t &bl0, uint32_t &bl1) {
-                            const float *b = base + (r0 + 2 * t4) * ld + c0 + 8 * nt + g;
-                            split2(b[0], b[ld], bh0, bl0);
-                            split2(b[8 * ld], b[9 * ld], bh1, bl1);
-                        };
-                        auto afrag = [&](const float *base, int ld, int r0, int c0, uint32_t (&ah)[4],
-                                         uint32_t (&al)[4]) {
-                            const float *a = base + (r0 + g) * ld + c0 + 2 * t4;
-                            const float2 a0 = *reinterpret_cast<const float2 *>(a);
-                            const float2 a1 = *reinterpret_cast<const float2 *>(a + 8 * ld);
-                            const float2 a2 = *reinterpret_cast<const float2 *>(a + 8);
-                            const float2 a3 = *reinterpret_cast<const float2 *>(a + 8 * ld + 8);
-                            split2(a0.x, a0.y, ah[0], al[0]);
-                            split2(a1.x, a1.y, ah[1], al[1]);
-                            split2(a2.x, a2.y, ah[2], al[2]);
-                            split2(a3.x, a3.y, ah[3], al[3]);
-                        };
-                        float pacc[2][4] = {};
-#pragma unroll
-                        for (int m = 0; m < d; ++m) {
-                            const int M = J + m;
-                            uint32_t ah[4], al[4];
-                            afrag(Ap, AS, 16 * I, 16 * M, ah, al);
-#pragma unroll
-                            for (int nt = 0; nt < 2; ++nt) {
-                                uint32_t bh0, bh1, bl0, bl1;
-                                bfrag(Tm, AS, 16 * M, 16 * J, nt, bh0, bh1, bl0, bl1);
-                                mma3(pacc[nt], ah, al, bh0, bh1, bl0, bl1);
-                            }
-                        }
-#pragma unroll
-                        for (int nt = 0; nt < 2; ++nt) {
-                            *reinterpret_cast<float2 *>(Pw + g * L::PS + 8 * nt + 2 * t4) = make_float2(pacc[nt][0], pacc[nt][1]);
-                            *reinterpret_cast<float2 *>(Pw + (g + 8) * L::PS + 8 * nt + 2 * t4) =
-                                make_float2(pacc[nt][2], pacc[nt][3]);
-                        }
-                        __syncwarp();
-                        uint32_t ah[4], al[4];
-                        afrag(Tm, AS, 16 * I, 16 * I, ah, al);
-#pragma unroll
-                        for (int nt = 0; nt < 2; ++nt) {
-                            uint32_t bh0, bh1, bl0, bl1;
-                            bfrag(Pw, L::PS, 0, 0, nt, bh0, bh1, bl0, bl1);
-                            float tacc[4] = {};
-                            mma3(tacc, ah, al, bh0, bh1, bl0, bl1);
-                            float *t = Tm + (16 * I + g) * AS + 16 * J + 8 * nt + 2 * t4;
-                            *reinterpret_cast<float2 *>(t) = make_float2(-tacc[0], -tacc[1]);
-                            *reinterpret_cast<float2 *>(t + 8 * AS) = make_float2(-tacc[2], -tacc[3]);
-                        }
-                        __syncwarp();
+                    for (int nt = 0; nt < 2; ++nt) {
+                        uint32_t bh0, bh1, bl0, bl1;
+                        bfrag(b, ldb, br, bc, nt, bh0, bh1, bl0, bl1);
+                        mma3(acc[nt], ah, al, bh0, bh1, bl0, bl1);
                     }
+                };
+                auto put = [&](float *dst, int ld, const float (&acc)[2][4], float sgn) {
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        float *t = dst + g * ld + 8 * nt + 2 * t4;
+                        *reinterpret_cast<float2 *>(t) = make_float2(sgn * acc[nt][0], sgn * acc[nt][1]);
+                        *reinterpret_cast<float2 *>(t + 8 * ld) = make_float2(sgn * acc[nt][2], sgn * acc[nt][3]);
+                    }
+                };
+                float *const Pw = Pp + warp * 16 * L::PS;
+                if (warp < 2) {
+                    // T_IJ = -T_II (A'_IJ T_JJ), (I, J) = (1, 0) or (3, 2)
+                    const int J = 2 * warp, I = J + 1;
+                    float pacc[2][4] = {};
+                    blk(pacc, Ap, AS, 16 * I, 16 * J, Tm, AS, 16 * J, 16 * J);
+                    put(Pw, L::PS, pacc, 1.f);
+                    __syncwarp();
+                    float tacc[2][4] = {};
+                    blk(tacc, Tm, AS, 16 * I, 16 * I, Pw, L::PS, 0, 0);
+                    put(Tm + 16 * I * AS + 16 * J, AS, tacc, -1.f);
+                }
+                nbar(2, 128);
+                {
+                    // Block (r, cc) of the lower-left quadrant, r in {2, 3}, cc in {0, 1}:
+                    // P_r,cc = sum_{m=cc}^{1} A'_r,m T_m,cc, then
+                    // T_r,cc = -sum_{m=2}^{r} T_r,m P_m,cc (P_m,cc from warp 2 (m - 2) + cc).
+                    const int r = 2 + (warp >> 1), cc = warp & 1;
+                    float pacc[2][4] = {};
+                    blk(pacc, Ap, AS, 16 * r, 16, Tm, AS, 16, 16 * cc);
+                    if (cc == 0) blk(pacc, Ap, AS, 16 * r, 0, Tm, AS, 0, 0);
+                    put(Pw, L::PS, pacc, 1.f);
                     nbar(2, 128);
+                    float tacc[2][4] = {};
+                    blk(tacc, Tm, AS, 16 * r, 32, Pp + cc * 16 * L::PS, L::PS, 0, 0);
+                    if (r == 3) blk(tacc, Tm, AS, 48, 48, Pp + (2 + cc) * 16 * L::PS, L::PS, 0, 0);
+                    put(Tm + 16 * r * AS + 16 * cc, AS, tacc, -1.f);
                 }
             } else if (!PREP && warp >= 8) {
                 // S^T -> bf16 hi/lo A operand and S^T <- S^T e^{gl} (deferred on a
