@@ -495,10 +495,18 @@ __device__ int block_max(int x, int32_t *tmp) {
     return m;
 }
 
-// Block pair index p -> (I, J), J <= I, in the order (0,0) (1,0) (1,1) (2,0) ...
-__device__ __forceinline__ void pair_ij(int p, int &I, int &J) {
-    I = (p >= 6) ? 3 : (p >= 3) ? 2 : (p >= 1) ? 1 : 0;
-    J = p - I * (I + 1) / 2;
+// Block pair (I, J), J <= I, of P3's warp w: warps 0..9 take (1,0) (2,0)
+// (0,0) (1,1) (2,1) (3,0) (2,2) (3,3) (3,1) (3,2). The four diagonal blocks,
+// whose warps also solve T_II, sit on sub-partitions 2 and 3 (w % 4), which
+// hold two product warps each against three on sub-partitions 0 and 1.
+__device__ __forceinline__ void pair_ij(int w, int &I, int &J) {
+    // 4 bits per warp: I in bits 0-1, J in bits 2-3
+    constexpr uint64_t kPairs = 0x1ull | (0x2ull << 4) | (0x0ull << 8) | (0x5ull << 12) | (0x6ull << 16) |
+                                (0x3ull << 20) | (0xAull << 24) | (0xFull << 28) | (0x7ull << 32) |
+                                (0xBull << 36);
+    const int v = static_cast<int>((kPairs >> (4 * w)) & 0xFu);
+    I = v & 3;
+    J = v >> 2;
 }
 // Factor slot of an off-diagonal pair (J < I) in the vF table.
 __device__ __forceinline__ int fslot(int I, int J) { return I * (I - 1) / 2 + J; }
@@ -1073,7 +1081,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
             cbar();
 
-            // ---- P3: A' and Aqk, one 16x16 block pair per warp ----
+            // ---- P3: A' and Aqk, one 16x16 block pair per warp (T_II on diagonal ones) ----
             // Block (I, J) = X_I diag(e^{m_I - m_J}) Z_J^T: the factor is a power
             // of two, applied exactly to Z's bf16 hi/lo fragments.
             if (warp < 10) {
@@ -1127,6 +1135,31 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                         *reinterpret_cast<uint32_t *>(AQl + swz<BT>(i, j0)) = ql;
                     }
                 }
+                if (I == J) {
+                    // T_II = (I + A'_II)^-1 at once: lane j (and j + 16, which
+                    // repeats it) solves column j by forward substitution in fp32
+                    // (entries above the diagonal are 0, so the unpredicated sums
+                    // are exact).
+                    __syncwarp();   // the block's A' rows are in shared memory
+                    const int j = lane & 15;
+                    float col[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float *arow = Ap + (16 * I + i) * AS + 16 * I;
+                        float s0a = 0.f, s1a = 0.f;
+#pragma unroll
+                        for (int m = 0; m + 1 < i; m += 2) {
+                            s0a = fmaf(arow[m], col[m], s0a);
+                            s1a = fmaf(arow[m + 1], col[m + 1], s1a);
+                        }
+                        if (i & 1) s0a = fmaf(arow[i - 1], col[i - 1], s0a);
+                        col[i] = (i == j) ? 1.f : (i > j ? -(s0a + s1a) : 0.f);
+                    }
+                    if (lane < 16) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
+                    }
+                }
             } else if (o_pending) {
                 // Warps 10..15, beside the block products: the previous chunk's
                 // o tile leaves through the raw region's staging area (quadrants 0
@@ -1148,30 +1181,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 
             // ---- P4: T = (I + A')^-1 on warps 0-3, beside the S split on warps 8-15 ----
             if (warp < 4) {
-                // Diagonal 16x16 blocks: lane (I, j) of warps 0-1 solves column j
-                // of block I by forward substitution in fp32 (entries above the
-                // diagonal stay 0, so the unpredicated sums are exact).
-                if (warp < 2) {
-                    const int I = 2 * warp + (lane >> 4), j = lane & 15;
-                    float col[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float *arow = Ap + (16 * I + i) * AS + 16 * I;
-                        float s0a = 0.f, s1a = 0.f;
-#pragma unroll
-                        for (int m = 0; m + 1 < i; m += 2) {
-                            s0a = fmaf(arow[m], col[m], s0a);
-                            s1a = fmaf(arow[m + 1], col[m + 1], s1a);
-                        }
-                        if (i & 1) s0a = fmaf(arow[i - 1], col[i - 1], s0a);
-                        col[i] = (i == j) ? 1.f : (i > j ? -(s0a + s1a) : 0.f);
-                    }
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
-                }
-                nbar(2, 128);
-                // Off-diagonal blocks, 2x2 block-recursively: the inverse of
-                // [[M_A, 0], [A'_BA, M_B]] is [[T_A, 0], [-T_B A'_BA T_A, T_B]].
+                // The diagonal blocks T_II came with P3. Off-diagonal blocks, 2x2
+                // block-recursively: the inverse of [[M_A, 0], [A'_BA, M_B]] is
+                // [[T_A, 0], [-T_B A'_BA T_A, T_B]].
                 // Stage 1: T_10 and T_32 (the 32x32 diagonal halves); stage 2: the
                 // lower-left 32x32 quadrant, one 16x16 block per warp. Every
                 // product is split-bf16 (fp32 operands split into hi + lo).
