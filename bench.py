@@ -579,7 +579,7 @@ def main():
     dec = bench_decode(args, dist, hbm_gbs, peak_kind)
 
     pre = bench_prefill(args, dist, hbm_gbs, bf16_tf, steps=args.prefill_steps, warmup=3)
-    pre_long = bench_prefill_long(args, dist, steps=5, warmup=3)
+    pre_long = bench_prefill_long(args, dist, steps=20, warmup=3)
 
     cpu = None
     if dist.rank == 0 and dist.world == 1:
