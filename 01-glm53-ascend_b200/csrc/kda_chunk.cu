@@ -352,7 +352,7 @@ struct Smem {
     static constexpr int kTBl = kTBh + BT * BT * 2;
     static constexpr int kAQh = kTBl + BT * BT * 2;
     static constexpr int kAQl = kAQh + BT * BT * 2;
-    static constexpr int kBar = kAQl + BT * BT * 2;        // 8 mbarriers + tensor-memory base slot
+    static constexpr int kBar = kAQl + BT * BT * 2;        // 9 mbarriers + tensor-memory base slot
     static constexpr int kVec = kBar + 128;                // vectors below
     // vector offsets in 4-byte words from kVec; per (16-row block I, column k)
     // tables are [4][D]
@@ -679,6 +679,18 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 #pragma unroll
         for (int blk = 0; blk < D / 64; ++blk) tma_load_3d(Vt + blk * 4096, &maps.v, 64 * blk, h, t0c, &bars[2]);
     };
+    // Untracked chunks split the copy: q once A' (the front of the raw region)
+    // is dead, k and the gate once the rest of the region is free.
+    auto issue_q = [&](int c) {
+        const int t0c = static_cast<int>(bos + static_cast<int64_t>(c) * BT);
+        mbar_arrive_expect_tx(&bars[2], kTileBytes);
+        tma_load_3d(rawQ, &maps.q, 0, h, t0c, &bars[2]);
+    };
+    auto issue_kg = [&](int c) {
+        const int t0c = static_cast<int>(bos + static_cast<int64_t>(c) * BT);
+        tma_load_3d(rawK, &maps.k, 0, h, t0c, &bars[2]);
+        tma_load_3d(rawG, &maps.g, 0, h, t0c, &bars[2]);
+    };
     auto issue_tiles = [&](int c, bool with_v, bool expect_v = true) {
         const int t0c = static_cast<int>(bos + static_cast<int64_t>(c) * BT);
         mbar_arrive_expect_tx(&bars[2], expect_v ? kTileBytes : kTileBytes - BT * D * 2);
@@ -701,12 +713,16 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     // ---- tensor memory, mbarriers ----
     // bars: 0 = W S done (v' ready), 1 = state update done, 2 = chunk tiles
     // landed, 3 = o^T done, 4 = u product done (v tile free). sig: consumer ->
-    // producer, 0 = TB/QG/S-split ready, 1 = W/KD ready, 2 = v' hi/lo ready.
+    // producer, 0 = TB/QG/S-split ready, 1 = W/KD ready, 2 = v' hi/lo ready;
+    // sig_a = A' read for the last time (P4 done). (The tensor-memory slot
+    // sits between bars[7] and sig_a.)
     uint64_t *const sig = bars + 5;
+    uint64_t *const sig_a = bars + 9;
     if (!PREP && warp == 0) tmem_alloc(tmem_slot, kTmemCols);
     if (tid == 0) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
+        mbar_init(sig_a, 1);
         fence_mbar_init();
     }
     tc_fence_before();
@@ -761,9 +777,11 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 const int64_t rt = tlen - static_cast<int64_t>(c) * BT;
                 const bool trk = tslot > 0 && rt > 0 && rt <= BT;
                 const bool nxt = c + 1 < nchunks;
+                pwait(sig_a, ph);
+                if (nxt && !trk) issue_q(c + 1);    // A' is dead: q's part of the raw region is free
                 pwait(&sig[0], ph);
                 tc_fence_after();
-                if (nxt && !trk) issue_tiles(c + 1, false);   // the raw region is free
+                if (nxt && !trk) issue_kg(c + 1);   // the raw region is free
                 // NU = -u^T = -(TB v)^T (needs neither S nor v')
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
@@ -1291,6 +1309,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 tc_fence_before();
             }
             cbar();
+            if (!PREP && tid == 0) mbar_arrive(sig_a);   // A' is dead: the next q tile may land
 
             // ---- P5: TB = T diag(beta) hi/lo; Aqk's upper blocks zeroed ----
             // One 8-column chunk of one row per thread.
