@@ -42,7 +42,9 @@
 //     leave idle.
 //   * the next chunk's q/k/g (and v) tiles are fetched by TMA (one tensor
 //     map each, the v tile written in the 128-byte swizzle the tensor core
-//     reads) while this chunk runs; output tiles leave by TMA stores.
+//     reads) while this chunk runs, each as soon as its shared-memory region
+//     is dead (q after the inverse, k and g after TB, v after u = TB v);
+//     output tiles leave by TMA stores.
 //   * any sequence length: a partial last chunk is zero-filled (k = q = v =
 //     g = beta = 0), which leaves the state and the real rows unchanged.
 //   * every mbarrier wait is bounded; tensor memory is freed on every path.
