@@ -613,6 +613,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     __nv_bfloat16 *const OstR = reinterpret_cast<__nv_bfloat16 *>(sm + L::kOst);
     uint64_t *const bars = reinterpret_cast<uint64_t *>(sm + L::kBar);
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 64);
+    // CTA-wide give-up word of the bounded waits (between the tensor-memory
+    // slot and sig_a)
+    volatile int32_t *const abort_w = reinterpret_cast<volatile int32_t *>(sm + L::kBar + 68);
     float *const vec = reinterpret_cast<float *>(sm + L::kVec);
     const uint32_t s_base = smem_addr(sm);
 
@@ -725,6 +728,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) mbar_init(&bars[i], 1);
         mbar_init(sig_a, 1);
+        *abort_w = 0;
         fence_mbar_init();
     }
     tc_fence_before();
@@ -771,7 +775,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
             constexpr uint32_t id_kd = idesc_bf16(128, D, false, true, false);
             auto pwait = [&](uint64_t *b, uint32_t ph) {
-                if (!mbar_wait(b, ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                if (!mbar_wait(b, ph, p.status, abort_w)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             };
             issue_tiles(0, true);
             for (int c = 0; c < nchunks; ++c) {
@@ -926,7 +930,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             const int64_t rtrack = tlen - static_cast<int64_t>(c) * BT;
             const bool track_here = tslot > 0 && rtrack > 0 && rtrack <= BT;
             const bool has_next = !PREP && c + 1 < nchunks;
-            if (!mbar_wait(&bars[2], static_cast<uint32_t>(PREP ? 0 : c & 1), p.status) && tid == 0)
+            if (!mbar_wait(&bars[2], static_cast<uint32_t>(PREP ? 0 : c & 1), p.status, abort_w) && tid == 0)
                 report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             // A tracked chunk's o tile (thread 0's only store in flight) has
             // left the W region before P2 rewrites it.
@@ -1067,7 +1071,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             // chunk rewrites: wait for them (bars[3] tracks all three) before the
             // tiles below; the factor tables above touch none of them.
             if (!PREP && c > 0) {
-                if (!mbar_wait(&bars[3], static_cast<uint32_t>((c - 1) & 1), p.status) && tid == 0)
+                if (!mbar_wait(&bars[3], static_cast<uint32_t>((c - 1) & 1), p.status, abort_w) && tid == 0)
                     report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
                 tc_fence_after();
             }
@@ -1184,7 +1188,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 // Warps 10..15, beside the block products: the previous chunk's
                 // o tile leaves through the raw region's staging area (quadrants 0
                 // and 1 have one warp each, 2 and 3 two).
-                if (!mbar_wait(&bars[3], static_cast<uint32_t>((c - 1) & 1), p.status) && lane == 0)
+                if (!mbar_wait(&bars[3], static_cast<uint32_t>((c - 1) & 1), p.status, abort_w) && lane == 0)
                     report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
                 tc_fence_after();
                 const bool pair = q4 >= 2;
@@ -1278,7 +1282,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 // S^T -> bf16 hi/lo A operand and S^T <- S^T e^{gl} (deferred on a
                 // tracked chunk): two warps per lane quadrant, half the columns each.
                 if (c > 0) {
-                    if (!mbar_wait(&bars[1], static_cast<uint32_t>((c - 1) & 1), p.status) && lane == 0)
+                    if (!mbar_wait(&bars[1], static_cast<uint32_t>((c - 1) & 1), p.status, abort_w) && lane == 0)
                         report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
                     tc_fence_after();
                 }
@@ -1500,7 +1504,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             if (tid == 0) mbar_arrive(&sig[1]);   // W, QG, KD (and K_r) are in place: W S and QG S may start
 
             // ---- P9: the state scan: -v'^T (fp32) -> v'^T hi/lo A operand, 16 columns per warp ----
-            if (!mbar_wait(&bars[0], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
+            if (!mbar_wait(&bars[0], static_cast<uint32_t>(c & 1), p.status, abort_w) && tid == 0)
                 report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
             {
@@ -1534,7 +1538,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             if (track_here) {
                 // A tracked chunk finishes here: the checkpoint leaves tensor memory
                 // before the next S split reuses its columns; the o tile goes too.
-                if (!mbar_wait(&bars[3], static_cast<uint32_t>(c & 1), p.status) && tid == 0)
+                if (!mbar_wait(&bars[3], static_cast<uint32_t>(c & 1), p.status, abort_w) && tid == 0)
                     report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
                 tc_fence_after();
                 o_cols(OstX, t0, n, 16 * cs, 16);
@@ -1563,14 +1567,14 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
         if (!PREP && nchunks > 0) {
             const uint32_t lph = static_cast<uint32_t>((nchunks - 1) & 1);
             if (o_pending) {
-                if (!mbar_wait(&bars[3], lph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                if (!mbar_wait(&bars[3], lph, p.status, abort_w) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
                 tc_fence_after();
                 o_cols(OstX, o_t0, o_n, 16 * cs, 16);
                 fence_async_smem();
                 cbar();
                 if (tid == 0) o_store(OstX, o_t0, o_n);
             }
-            if (!mbar_wait(&bars[1], lph, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (!mbar_wait(&bars[1], lph, p.status, abort_w) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
         }
         // Final state S^T -> pool slot (padding slot 0 is never written).
@@ -1585,6 +1589,18 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
         }
         if (tid == 0 || tid == 384) bulk_wait_read();   // output stores have read their staging tiles
+    }
+    // After an expired wait the CTA's waits gave up early: before the CTA
+    // frees its tensor memory and exits, thread 0 waits (bounded, without the
+    // shortcut) for the last chunk's tile copies and tensor-core products,
+    // which complete every earlier phase of their barriers.
+    if (*abort_w != 0 && tid == 0 && nchunks > 0) {
+        const uint32_t lph = PREP ? 0u : static_cast<uint32_t>((nchunks - 1) & 1);
+        mbar_wait(&bars[2], lph, nullptr);
+        if (!PREP) {
+            mbar_wait(&bars[1], lph, nullptr);
+            mbar_wait(&bars[3], lph, nullptr);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -1626,6 +1642,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     // compute warps -> producer
     uint64_t *const sSplit = mb + 12, *const sConv = mb + 13;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(sm + L::kBar + 120);
+    volatile int32_t *const abort_w = reinterpret_cast<volatile int32_t *>(sm + L::kBar + 124);   // give-up word
     const uint32_t s_base = smem_addr(sm);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1693,6 +1710,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     if (tid == 0) {
 #pragma unroll
         for (int i = 0; i < 15; ++i) mbar_init(&mb[i], 1);
+        *abort_w = 0;
         fence_mbar_init();
     }
     tc_fence_before();
@@ -1710,7 +1728,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             // S_mid^T = S_start^T A_mid^T + B_mid^T: the compute warps staged
             // S_start^T's split (tensor memory), B_mid^T (the accumulator) and
             // A_mid^T as MN-major hi/lo tiles in the W and KD slots.
-            if (!mbar_wait(mb + 14, 0, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (!mbar_wait(mb + 14, 0, p.status, abort_w)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < KS; ++kk) {
@@ -1723,12 +1741,12 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
             umma_commit(mb + 0);
             // the W and KD slots take their records once the product is done
-            if (!mbar_wait(mb + 0, 0, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (!mbar_wait(mb + 0, 0, p.status, abort_w)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
         }
         if (lane == 0 && nchunks > 0) {
             constexpr uint32_t id_n64 = idesc_bf16(128, 64, false, false, false);
             auto pwait = [&](uint64_t *b, uint32_t ph) {
-                if (!mbar_wait(b, ph, p.status)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+                if (!mbar_wait(b, ph, p.status, abort_w)) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             };
             auto load = [&](uint64_t *bar, void *dst, const uint8_t *src, uint32_t bytes) {
                 mbar_arrive_expect_tx(bar, bytes);
@@ -1858,7 +1876,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tc_fence_before();
             nbar(1, kThreads);
             if (tid == 0) mbar_arrive(mb + 14);
-            if (!mbar_wait(mb + 0, 0, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (!mbar_wait(mb + 0, 0, p.status, abort_w) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
         } else {
             const bool row_ok = srow < D;
@@ -1893,7 +1911,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tmem_st_wait();
         }
         auto cwait = [&](uint64_t *bar, uint32_t phase) {
-            if (!mbar_wait(bar, phase, p.status) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
+            if (!mbar_wait(bar, phase, p.status, abort_w) && tid == 0) report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
         };
         // NU <- -u^T of chunk c (this warp's 16 token columns of value row srow);
         // the copy reaches G2 through the wait, fence and barrier before sSplit.
@@ -2016,7 +2034,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             }
         }
         if (nchunks > 0) {
-            if (!mbar_wait(bG4, static_cast<uint32_t>((nchunks - 1) & 1), p.status) && tid == 0)
+            if (!mbar_wait(bG4, static_cast<uint32_t>((nchunks - 1) & 1), p.status, abort_w) && tid == 0)
                 report(p.status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
             tc_fence_after();
         }
@@ -2050,6 +2068,21 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 if (!half) put(xslot(kind, seg));
                 if (half || mid_at == nchunks) put(xslot(kind + 2, seg));
             }
+        }
+    }
+    // After an expired wait: thread 0 waits (bounded, without the shortcut)
+    // for the last state update and the last chunk's operand copies before
+    // the CTA frees its tensor memory and exits.
+    if (*abort_w != 0 && tid == 0 && nchunks > 0) {
+        const uint32_t lph = static_cast<uint32_t>((nchunks - 1) & 1);
+        mbar_wait(bG4, lph, nullptr);
+        mbar_wait(lW, lph, nullptr);
+        mbar_wait(lKD, lph, nullptr);
+        mbar_wait(lEgl, lph, nullptr);
+        if (use_u) {
+            const int n0c = (nchunks + 1) / 2, n1c = nchunks / 2;   // copies into U slot 0 and 1
+            mbar_wait(lU0, static_cast<uint32_t>((n0c - 1) & 1), nullptr);
+            if (n1c > 0) mbar_wait(lU1, static_cast<uint32_t>((n1c - 1) & 1), nullptr);
         }
     }
     tc_fence_before();
@@ -2846,7 +2879,6 @@ static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
 // few chains (a long context over a few heads) most SMs would idle, so the
 // split path first computes every chunk's intra-chunk operands with one CTA
 // per (chunk, head) on all SMs, then runs only the serial scan per chain.
-// KDA_CHUNK_PATH=fused|split overrides the choice.
 
 static int sm_count() {
     static int count[64];
@@ -2861,12 +2893,13 @@ static int sm_count() {
     return count[dev];
 }
 
+static bool split_ok(int32_t num_req) { return num_req > 0 && num_req <= 1024; }
+
+// The library's own choice: the split path when the (sequence, head) chains
+// fill at most half the SMs and the sequences average >= 8 chunks.
 static bool want_split(int32_t num_req, int32_t heads, int32_t num_tokens) {
-    const char *env = getenv("KDA_CHUNK_PATH");
-    if (env != nullptr && strcmp(env, "fused") == 0) return false;
-    if (env != nullptr && strcmp(env, "split") == 0) return num_req > 0 && num_req <= 1024;
     const int64_t chains = static_cast<int64_t>(num_req) * heads;
-    return num_req > 0 && num_req <= 1024 && chains * 2 <= sm_count() &&
+    return split_ok(num_req) && chains * 2 <= sm_count() &&
            static_cast<int64_t>(num_tokens) >= static_cast<int64_t>(num_req) * chunk::BT * 8;
 }
 
@@ -2960,13 +2993,27 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st, cu
 
 }  // namespace kda
 
+namespace kda {
+// Workspace bytes of a chunk launch that takes `path` (KdaChunkPath).
+static size_t chunk_ws_bytes(int32_t num_req, int32_t num_tokens, int32_t heads, int32_t head_dim, int path) {
+    if (num_req <= 0) return 0;
+    const bool dims_ok = (head_dim == 64 || head_dim == 128) && num_tokens >= 0 && heads > 0;
+    const bool split = path == KDA_CHUNK_SPLIT ? split_ok(num_req)
+                                               : path == KDA_CHUNK_AUTO && want_split(num_req, heads, num_tokens);
+    if (dims_ok && split) return split_layout(num_req, num_tokens, heads, head_dim).total;
+    return num_req <= 1024 ? order_bytes(num_req) : 0;
+}
+}  // namespace kda
+
 extern "C" size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens, int32_t num_heads,
                                             int32_t head_dim) {
-    if (num_req <= 0) return 0;
-    if ((head_dim == 64 || head_dim == 128) && num_tokens >= 0 && num_heads > 0 &&
-        kda::want_split(num_req, num_heads, num_tokens))
-        return kda::split_layout(num_req, num_tokens, num_heads, head_dim).total;
-    return num_req <= 1024 ? kda::order_bytes(num_req) : 0;
+    return kda::chunk_ws_bytes(num_req, num_tokens, num_heads, head_dim, KDA_CHUNK_AUTO);
+}
+
+extern "C" size_t kda_chunk_path_workspace_bytes(int32_t num_req, int32_t num_tokens, int32_t num_heads,
+                                                 int32_t head_dim, int32_t path) {
+    if (path != KDA_CHUNK_AUTO && path != KDA_CHUNK_FUSED && path != KDA_CHUNK_SPLIT) return 0;
+    return kda::chunk_ws_bytes(num_req, num_tokens, num_heads, head_dim, path);
 }
 
 namespace kda {
@@ -3036,30 +3083,41 @@ extern "C" int kda_chunk_launch_phases(const KdaArgs *args, void *workspace, siz
     return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
 }
 
-extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream) {
+namespace kda {
+// kda_chunk_launch with the path given: AUTO takes the split path when the
+// library chooses it and the workspace holds it, else the fused kernel; FUSED
+// always takes the fused kernel; SPLIT takes the split path or returns
+// KDA_ERR_WORKSPACE (never falls back).
+static int chunk_launch_path(const KdaArgs *args, void *workspace, size_t workspace_bytes, cudaStream_t st,
+                             int path) {
     bool empty = false;
-    const int chk = kda::chunk_check(args, &empty);
+    const int chk = chunk_check(args, &empty);
     if (chk != KDA_OK || empty) return chk;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     int rc;
-    // The split path runs when it pays off and the workspace holds its records;
-    // otherwise the fused kernel, which needs only the request order.
-    const bool split = kda::want_split(args->num_req, args->head_count, args->num_tokens) && workspace != nullptr &&
-                       (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
-                       workspace_bytes >=
-                           kda::split_layout(args->num_req, args->num_tokens, args->head_count, args->head_dim).total;
+    const bool ws_split = workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
+                          workspace_bytes >=
+                              split_layout(args->num_req, args->num_tokens, args->head_count, args->head_dim).total;
+    bool split = false;
+    if (path == KDA_CHUNK_SPLIT) {
+        if (!split_ok(args->num_req) || !ws_split) return KDA_ERR_WORKSPACE;
+        split = true;
+    } else if (path == KDA_CHUNK_AUTO) {
+        split = want_split(args->num_req, args->head_count, args->num_tokens) && ws_split;
+    }
     if (split) {
         uint8_t *ws = static_cast<uint8_t *>(workspace);
         if (args->head_dim == 128)
-            rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk_split<128, KDA_GATE_RAW>(args, ws, st)
-                                                 : kda::launch_chunk_split<128, KDA_GATE_LOG>(args, ws, st);
+            rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk_split<128, KDA_GATE_RAW>(args, ws, st)
+                                                 : launch_chunk_split<128, KDA_GATE_LOG>(args, ws, st);
         else
-            rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk_split<64, KDA_GATE_RAW>(args, ws, st)
-                                                 : kda::launch_chunk_split<64, KDA_GATE_LOG>(args, ws, st);
+            rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk_split<64, KDA_GATE_RAW>(args, ws, st)
+                                                 : launch_chunk_split<64, KDA_GATE_LOG>(args, ws, st);
         if (rc != KDA_OK) return rc;
         return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
     }
-    const size_t need = args->num_req <= 1024 ? kda::order_bytes(args->num_req) : 0;
+    // The fused kernel needs only the longest-first request order (batches
+    // of more than 1024 requests run in batch order, with no workspace).
+    const size_t need = args->num_req <= 1024 ? order_bytes(args->num_req) : 0;
     int32_t *order = nullptr;
     if (need > 0) {
         if (workspace == nullptr || workspace_bytes < need) return KDA_ERR_WORKSPACE;
@@ -3067,13 +3125,24 @@ extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t wor
         order = static_cast<int32_t *>(workspace);
     }
     if (args->head_dim == 128)
-        rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk<128, KDA_GATE_RAW>(args, order, st)
-                                             : kda::launch_chunk<128, KDA_GATE_LOG>(args, order, st);
+        rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk<128, KDA_GATE_RAW>(args, order, st)
+                                             : launch_chunk<128, KDA_GATE_LOG>(args, order, st);
     else
-        rc = args->gate_mode == KDA_GATE_RAW ? kda::launch_chunk<64, KDA_GATE_RAW>(args, order, st)
-                                             : kda::launch_chunk<64, KDA_GATE_LOG>(args, order, st);
+        rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk<64, KDA_GATE_RAW>(args, order, st)
+                                             : launch_chunk<64, KDA_GATE_LOG>(args, order, st);
     if (rc != KDA_OK) return rc;
     return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+}
+}  // namespace kda
+
+extern "C" int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream) {
+    return kda::chunk_launch_path(args, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), KDA_CHUNK_AUTO);
+}
+
+extern "C" int kda_chunk_launch_path(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream,
+                                     int32_t path) {
+    if (path != KDA_CHUNK_AUTO && path != KDA_CHUNK_FUSED && path != KDA_CHUNK_SPLIT) return KDA_ERR_INVALID_ARGUMENT;
+    return kda::chunk_launch_path(args, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), path);
 }
 
 // ---------------------------------------------------------------------------
@@ -3122,6 +3191,9 @@ extern "C" int kda_chunk_launch_no_alloc(const KdaArgs *args, void *stream) {
         if (rc != KDA_OK) return rc;
     }
     // The order kernel rewrites entries [0, num_req) on every call, so the
-    // array needs no clearing; only concurrent calls would interfere.
-    return kda_chunk_launch(args, scratch, sizeof(int32_t) * KDA_CHUNK_STATIC_MAX_REQUESTS, stream);
+    // array needs no clearing; only concurrent calls would interfere. The
+    // array holds the request order alone, so this entry point always runs
+    // the fused kernel (the split path's records need a caller workspace).
+    return kda::chunk_launch_path(args, scratch, sizeof(int32_t) * KDA_CHUNK_STATIC_MAX_REQUESTS,
+                                  static_cast<cudaStream_t>(stream), KDA_CHUNK_FUSED);
 }

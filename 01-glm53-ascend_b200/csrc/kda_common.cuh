@@ -76,22 +76,37 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
-// Returns false (and records the timeout) if the phase did not complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int32_t *status) {
+// One poll of an mbarrier phase. The suspend-time hint lets a waiting warp
+// sleep instead of spinning, leaving issue slots to the warps that do the work.
+__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t phase) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(phase), "r"(kWaitSuspendNs)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for `phase` of `bar` for at most `polls` polls. Returns false (and
+// records KDA_DEVICE_ERR_WAIT_TIMEOUT) if the phase did not complete.
+// `abort`, when given, is a CTA-wide shared-memory word (zeroed at kernel
+// start): the first wait of the CTA that expires sets it, and from then on
+// every wait of the CTA that does not complete at its first poll gives up at
+// once. A CTA whose wait expired therefore runs to its end (through its
+// barriers, freeing its tensor memory) in about one wait's time instead of
+// one expiry per remaining wait; its results are undefined and the status
+// word says so.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int32_t *status,
+                                          volatile int32_t *abort = nullptr, uint32_t polls = kMaxWaitPolls) {
     const uint32_t addr = smem_addr(bar);
-    for (uint32_t i = 0; i < kMaxWaitPolls; ++i) {
-        uint32_t done;
-        // The suspend-time hint lets a waiting warp sleep instead of spinning,
-        // leaving issue slots to the warps that do the work.
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(done)
-            : "r"(addr), "r"(phase), "r"(kWaitSuspendNs)
-            : "memory");
-        if (done) return true;
+    for (uint32_t i = 0; i < polls; ++i) {
+        if (mbar_try(addr, phase)) return true;
+        if (abort != nullptr && *abort != 0) return false;
     }
+    if (abort != nullptr) *abort = 1;
     report(status, KDA_DEVICE_ERR_WAIT_TIMEOUT);
     return false;
 }

@@ -199,7 +199,7 @@ void set_intermediate(KdaArgs &a, const c10::optional<at::Tensor> &mid) {
 cudaStream_t current_stream(const at::Tensor &q) { return at::cuda::getCurrentCUDAStream(q.device().index()).stream(); }
 
 void launch_chunk(KdaArgs &a, const at::Tensor &v) {
-    const size_t ws_bytes = kda_chunk_workspace_bytes(a.num_req, a.num_tokens, a.num_heads, a.head_dim);
+    const size_t ws_bytes = kda_chunk_workspace_bytes(a.num_req, a.num_tokens, a.head_count, a.head_dim);
     at::Tensor ws = at::empty({static_cast<int64_t>(ws_bytes > 0 ? ws_bytes : 1)}, v.options().dtype(at::kByte));
     check_kda(kda_chunk_launch(&a, ws.data_ptr(), ws_bytes, current_stream(v)), "kda_varlen_chunk");
 }

@@ -23,6 +23,7 @@ KDA_OK = 0
 (KDA_ERR_INVALID_ARGUMENT, KDA_ERR_UNSUPPORTED, KDA_ERR_ALIGNMENT, KDA_ERR_WORKSPACE, KDA_ERR_LAUNCH,
  KDA_ERR_TOO_LARGE) = range(1, 7)
 KDA_GATE_RAW, KDA_GATE_LOG, KDA_GATE_PREPARED = 0, 1, 2
+KDA_CHUNK_AUTO, KDA_CHUNK_FUSED, KDA_CHUNK_SPLIT = 0, 1, 2
 
 # Entry points declared in include/kda_b200.h.
 EXPORTED = (
@@ -32,9 +33,12 @@ EXPORTED = (
     "kda_chunk_workspace_bytes",
     "kda_chunk_launch",
     "kda_chunk_launch_phases",
+    "kda_chunk_launch_path",
+    "kda_chunk_path_workspace_bytes",
     "kda_prepared_recurrent_launch",
     "kda_chunk_launch_no_alloc",
     "kda_commit_intermediate_launch",
+    "kda_selftest_wait_timeout",
 )
 
 
@@ -119,6 +123,14 @@ def lib() -> ctypes.CDLL:
         L.kda_chunk_launch.restype = ctypes.c_int
         L.kda_chunk_launch.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
                                        ctypes.c_void_p]
+        L.kda_chunk_launch_path.restype = ctypes.c_int
+        L.kda_chunk_launch_path.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
+                                            ctypes.c_void_p, ctypes.c_int32]
+        L.kda_chunk_path_workspace_bytes.restype = ctypes.c_size_t
+        L.kda_chunk_path_workspace_bytes.argtypes = [ctypes.c_int32] * 5
+        L.kda_selftest_wait_timeout.restype = ctypes.c_int
+        L.kda_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                                ctypes.c_int32, ctypes.c_void_p]
         L.kda_chunk_launch_phases.restype = ctypes.c_int
         L.kda_chunk_launch_phases.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
                                               ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]
@@ -195,6 +207,17 @@ def chunk_launch(args: KdaArgs, workspace: Optional[torch.Tensor], workspace_byt
                                   stream_handle(stream))
 
 
+def chunk_path_workspace_bytes(num_req: int, num_tokens: int, num_heads: int, head_dim: int, path: int) -> int:
+    return lib().kda_chunk_path_workspace_bytes(num_req, num_tokens, num_heads, head_dim, path)
+
+
+def chunk_launch_path(args: KdaArgs, workspace: Optional[torch.Tensor], workspace_bytes: int, path: int,
+                      stream: Optional[torch.cuda.Stream] = None) -> int:
+    """kda_chunk_launch with the internal path forced (KDA_CHUNK_AUTO/FUSED/SPLIT)."""
+    return lib().kda_chunk_launch_path(ctypes.byref(args), _ptr(workspace), workspace_bytes,
+                                       stream_handle(stream), path)
+
+
 def chunk_launch_phases(args: KdaArgs, workspace: torch.Tensor, workspace_bytes: int, events,
                         stream: Optional[torch.cuda.Stream] = None) -> int:
     """kda_chunk_launch's split path with six torch.cuda.Events (timing
@@ -231,6 +254,13 @@ def commit_args_from_tensors(dst, src, dst_indices, src_indices, step_indices,
 
 def commit_launch(args: KdaCommitArgs, stream: Optional[torch.cuda.Stream] = None) -> int:
     return lib().kda_commit_intermediate_launch(ctypes.byref(args), stream_handle(stream))
+
+
+def selftest_wait_timeout(status: torch.Tensor, expired: torch.Tensor, polls: int, waits: int, give_up: bool,
+                          stream: Optional[torch.cuda.Stream] = None) -> int:
+    """Waits that must run out (see kda_selftest_wait_timeout in the header)."""
+    return lib().kda_selftest_wait_timeout(_ptr(status), _ptr(expired), polls, waits, int(give_up),
+                                           stream_handle(stream))
 
 
 def status_string(code: int) -> str:

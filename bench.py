@@ -68,6 +68,8 @@ DECODE_BYTES_PER_TOKEN_HEAD = 65536 * 2 + 768 + 512 + 4 + 256
 # heads processed.
 DECODE_TRAFFIC_PER_LAUNCH = 1025897216
 PREFILL_TRAFFIC_PER_LAUNCH = 1651127296
+# configs[3] (4 heads), all kernels of one split-path call; None until captured.
+PREFILL_LONG_TRAFFIC_PER_LAUNCH = None
 
 METRIC = "KDA tokens/s (prefill, decode) H32 d128 @1/2/4/8 B200; decode HBM GB/s vs peak"
 
@@ -114,6 +116,23 @@ class Dist:
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
+
+    def all_true(self, ok: bool) -> bool:
+        if self.pg is None:
+            return ok
+        t = torch.tensor([0.0 if ok else 1.0], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item()) == 0.0
+
+    def gather_heads(self, x: torch.Tensor, dim: int) -> torch.Tensor:
+        """One NCCL all-gather of every rank's head shard `x` (same shape on all
+        ranks), reassembled along the head dimension `dim` in rank order."""
+        if self.pg is None:
+            return x
+        x = x.contiguous()
+        buf = torch.empty((self.world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        self.pg.all_gather_into_tensor(buf, x)
+        return torch.cat(list(buf.unbind(0)), dim=dim)
 
     def close(self):
         if self.pg is not None:
@@ -192,6 +211,32 @@ def time_steps(fn, steps: int, warmup: int, dist: Dist, stream=None):
     torch.cuda.synchronize()
     dist.barrier()
     return dist.max(start.elapsed_time(end))
+
+
+_FLUSH = None
+
+
+def time_flushed(fn, iters: int, warmup: int, dist: Dist):
+    """Per-call device milliseconds of a small workload that fits in L2: before
+    every call a 256 MiB buffer (twice the 126 MB L2) is rewritten, so the call
+    reads its inputs from HBM; CUDA events bracket the call alone, on the
+    launching stream. Returns the max over ranks of the per-rank median."""
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        fn()
+    dist.barrier()
+    s = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for a, b in ev:
+        _FLUSH.fill_(1)
+        a.record(s)
+        fn()
+        b.record(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return dist.max(statistics.median(a.elapsed_time(b) for a, b in ev))
 
 
 def time_e2e(host: dict, run, out_shape, steps: int, warmup: int, dist: Dist):
@@ -275,7 +320,8 @@ def time_e2e(host: dict, run, out_shape, steps: int, warmup: int, dist: Dist):
 # ---------------------------------------------------------------------------
 
 def bench_decode(args, dist: Dist, hbm_gbs: float, peak_kind: str) -> dict:
-    from sgl_glm53_ascend_ops import abi, ops, workloads
+    import kda_workloads as workloads
+    from sgl_glm53_ascend_ops import abi, ops
 
     w = workloads.config2(seed=1000 + dist.rank)
     d = w.to("cuda")
@@ -344,7 +390,8 @@ PREFILL_BYTES_PER_TOKEN_HEAD = 768 + 512 + 4 + 256
 
 
 def bench_prefill(args, dist: Dist, hbm_gbs: float, bf16_tf: float, steps: int, warmup: int) -> dict:
-    from sgl_glm53_ascend_ops import abi, ops, workloads
+    import kda_workloads as workloads
+    from sgl_glm53_ascend_ops import abi, ops
 
     w = workloads.config3(seed=2000 + dist.rank)
     d = w.to("cuda")
@@ -400,7 +447,8 @@ def bench_prefill_long(args, dist: Dist, steps: int, warmup: int) -> dict:
     configuration shards H=32 as 4 heads on each of 8 GPUs), fp32 initial
     state from the pool. Every chunk of a head follows the previous one, so
     this measures the serial inter-chunk state pass."""
-    from sgl_glm53_ascend_ops import ops, workloads
+    import kda_workloads as workloads
+    from sgl_glm53_ascend_ops import ops
 
     heads = 4
     w = workloads.config4(seed=3000 + dist.rank, heads=heads)
@@ -437,8 +485,21 @@ def bench_prefill_long(args, dist: Dist, steps: int, warmup: int) -> dict:
     phases = {n: round(dist.max(sum(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(steps)) / steps), 4)
               for j, n in enumerate(names)}
     del ws
+    hbm_gbs, bf16_tf = args.peaks[0], args.peaks[1]
+    flops = w.tokens * heads * PREFILL_FLOPS_PER_TOKEN_HEAD
+    min_bytes = w.tokens * heads * PREFILL_BYTES_PER_TOKEN_HEAD + 2 * heads * 65536
+    floor_ms = max(flops / (bf16_tf * 1e12), min_bytes / (hbm_gbs * 1e9)) * 1e3
+    gbs = min_bytes / (ms / 1e3) / 1e9
+    tflops = flops / (ms / 1e3) / 1e12
     return {
         "metric": "KDA long-context prefill tokens/s (chunk-64, configs[3])",
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_gbs, "unit": "GB/s",
+                     "frac": round(gbs / hbm_gbs, 4), "traffic": PREFILL_LONG_TRAFFIC_PER_LAUNCH,
+                     "algorithmic_bytes": min_bytes, "algorithmic_flops": flops,
+                     "tensor_tflops": round(tflops, 1), "tensor_frac": round(tflops / bf16_tf, 4),
+                     "attainable_frac": round(floor_ms / ms, 4),
+                     "note": "one call of the op (plan, prep, scan, combine, rescan, outputs); traffic = DRAM "
+                             "bytes of all its kernels per call"},
         "value": round(dist.world * w.tokens * heads / (ms / 1e3), 1),
         "unit": "token-heads/s",
         "ms_per_step": round(ms, 4),
@@ -453,10 +514,230 @@ def bench_prefill_long(args, dist: Dist, steps: int, warmup: int) -> dict:
     }
 
 
+# ---------------------------------------------------------------------------
+# Head-sharded lines (BASELINE configs[2] strong-scaled, configs[4] mixed)
+# ---------------------------------------------------------------------------
+
+def _bf16_out_err(got: torch.Tensor, ref: torch.Tensor) -> float:
+    """max |got - ref| / rms(ref) with one bf16 ulp of ref credited (both
+    sides are bf16 outputs of the operator)."""
+    got, ref = got.float(), ref.float()
+    rms = ref.pow(2).mean().sqrt().clamp_min(1e-30)
+    _, e = torch.frexp(ref)
+    credit = torch.ldexp(torch.ones_like(ref), e - 8)
+    return float(((got - ref).abs() - credit).clamp_min(0).max() / rms)
+
+
+def bench_head_sharded(w, steps: int, warmup: int, dist: Dist, hbm_gbs: float, bf16_tf: float) -> dict:
+    """The global workload `w` (all H heads) split H/N heads per rank, as
+    tensor parallelism by heads places it: rank r owns heads [r H/N, (r+1) H/N)
+    of the token tensors and that slice of the state pool. A step is one call
+    of the chunk op (`kda_varlen_chunk_g`) on every rank; value = the global
+    workload's tokens / the max-over-ranks device time, so the total work is
+    the same at every N (strong scaling).
+
+    Verification, outside the timed region: every rank reruns its shard from
+    the initial pool and checks that the slots no request names are
+    bit-identical; the shards' outputs and updated slots are assembled on rank
+    0 with one NCCL all-gather each and compared with one GPU running all H
+    heads in a single call."""
+    from sgl_glm53_ascend_ops import ops
+
+    N, H = dist.world, w.heads
+    sh = w.head_shard(dist.rank, N) if N > 1 else w
+    d = sh.to("cuda")
+    pool0 = d.pool.clone()
+    kw = d.kwargs()
+
+    def step():
+        ops.kda_varlen_chunk_g(**kw, prefill=True)
+
+    ms = time_steps(step, steps, warmup, dist) / steps
+
+    d.pool.copy_(pool0)
+    out = ops.kda_varlen_chunk_g(**kw, prefill=True)
+    touched = sorted({int(x) for x in w.indices.tolist()} - {0})
+    tidx = torch.tensor(touched, dtype=torch.long, device="cuda")
+    other = torch.ones(d.pool.shape[0], dtype=torch.bool, device="cuda")
+    other[tidx] = False
+    untouched_ok = dist.all_true(bool(torch.equal(d.pool[other], pool0[other])))
+    out_all = dist.gather_heads(out, dim=2)
+    st_all = dist.gather_heads(d.pool[tidx], dim=1)
+    del d, pool0, out, kw
+    verify = {"untouched_slots_bit_equal": untouched_ok, "assembled": "NCCL all_gather on rank 0, outside timing"}
+    if dist.rank == 0:
+        full = w.to("cuda")
+        ref = ops.kda_varlen_chunk_g(**full.kwargs(), prefill=True)
+        ref_st = full.pool[tidx]
+        oe = _bf16_out_err(out_all, ref)
+        se = float((st_all - ref_st).norm() / ref_st.norm().clamp_min(1e-30))
+        verify.update({"vs_one_gpu_all_heads": {"bit_equal": bool(torch.equal(out_all, ref) and
+                                                                   torch.equal(st_all, ref_st)),
+                                                "out_err": oe, "state_err": se},
+                       "ok": bool(untouched_ok and oe <= 5e-3 and se <= 1e-3)})
+        del full, ref, ref_st
+    del out_all, st_all
+    torch.cuda.empty_cache()
+
+    tokens, reqs = w.tokens, len(w.lengths)
+    flops = tokens * H * PREFILL_FLOPS_PER_TOKEN_HEAD
+    min_bytes = tokens * H * PREFILL_BYTES_PER_TOKEN_HEAD + 2 * reqs * H * 65536
+    gpu_s = N * ms / 1e3                          # GPU-seconds per step, all ranks
+    tflops = flops / gpu_s / 1e12
+    gbs = min_bytes / gpu_s / 1e9
+    floor_s = max(flops / (bf16_tf * 1e12), min_bytes / (hbm_gbs * 1e9))
+    return {
+        "value": round(tokens / (ms / 1e3), 1),
+        "unit": "tokens/s",
+        "ms_per_step": round(ms, 4),
+        "steps": steps,
+        "warmup": warmup,
+        "n_gpus": N,
+        "heads_per_gpu": H // N,
+        "scaling": "strong",
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_gbs, "unit": "GB/s",
+                     "frac": round(gbs / hbm_gbs, 4), "tensor_tflops": round(tflops, 1),
+                     "tensor_frac": round(tflops / bf16_tf, 4), "attainable_frac": round(floor_s * N / gpu_s, 4),
+                     "algorithmic_bytes": min_bytes, "algorithmic_flops": flops,
+                     "note": "per-GPU average: global work / (N x max-over-ranks time)"},
+        "verify": verify,
+    }
+
+
+def bench_prefill_strong(args, dist: Dist, hbm_gbs: float, bf16_tf: float, steps: int, warmup: int) -> dict:
+    import kda_workloads as workloads
+
+    w = workloads.config3(seed=2000)
+    r = bench_head_sharded(w, steps, warmup, dist, hbm_gbs, bf16_tf)
+    r["metric"] = "KDA prefill tokens/s, configs[2] head-sharded (32/N heads per GPU)"
+    r["config"] = {"workload": f"cfg3: 8 varlen sequences {w.lengths} (total {w.tokens}), H=32 split "
+                               f"{32 // dist.world} per GPU, K=V=128, zero initial state, log-gate op",
+                   "parallelism": f"tp{dist.world} by heads, no collective on the data path",
+                   "l2": "inputs larger than L2 at every N (>= 170 MB per rank per step), no flush"}
+    return r
+
+
+def bench_mixed(args, dist: Dist, hbm_gbs: float, bf16_tf: float, steps: int, warmup: int) -> dict:
+    import kda_workloads as workloads
+
+    w = workloads.config5(seed=5000)
+    r = bench_head_sharded(w, steps, warmup, dist, hbm_gbs, bf16_tf)
+    r["metric"] = "KDA mixed-batch tokens/s, configs[4] head-sharded (32/N heads per GPU)"
+    r["config"] = {"workload": "cfg5: 64 one-token decode requests + 4 x 2048-token prefills resumed from "
+                               "nonzero pooled states (1024-slot pool, 68 distinct slots), H=32 split "
+                               f"{32 // dist.world} per GPU, K=V=128, one chunk-op call, log-gate op",
+                   "parallelism": f"tp{dist.world} by heads, no collective on the data path",
+                   "l2": "inputs larger than L2 at every N, no flush"}
+    return r
+
+
+# ---------------------------------------------------------------------------
+# The reference's published shapes (Ascend 910B numbers, context only)
+# ---------------------------------------------------------------------------
+
+# Raw-gate bytes per (token, head): q, k, v, a bf16 (4 x 256), b bf16, out bf16.
+RAW_TOKEN_BYTES = 4 * 256 + 2 + 256
+
+# bench/kda_recurrent/DISCARDED-cann-recurrent-kda.md:22-30 (ascendc column, ms)
+PUBLISHED_DECODE_MS = {(16, 1): 0.121, (16, 32): 0.133, (16, 128): 0.303, (32, 1): 0.118, (32, 32): 0.146,
+                       (32, 128): 0.633, (64, 1): 0.140, (64, 32): 0.301, (64, 128): 1.225}
+# bench/kda_recurrent/bench_kda_varlen_recurrent.py:90-114 (label, heads, requests),
+# 4 draft tokens per request; published at
+# sgl-glm53-ascend-ops/csrc/kda/recurrent/kda_varlen_recurrent_decode.h:807-808.
+VERIFY_SHAPES = (("256K DP4TP2", 32, 2), ("256K DP2TP4", 16, 3), ("256K DP8TP1", 64, 1),
+                 ("512K DP4TP2", 32, 1), ("512K DP2TP4", 16, 1))
+PUBLISHED_VERIFY_US = {"512K DP4TP2": 23.8, "512K DP2TP4": 19.7}
+DRAFT_TOKENS = 4
+# bench/kda_chunk/README.md:35-39 (H8 C64, ascendc column, ms)
+PUBLISHED_CHUNK_MS = {1024: 2.03, 2048: 3.83, 4096: 7.36}
+
+
+def _raw_case(heads: int, lengths, slots: int, seed: int):
+    """The reference benches' inputs (bench_kda_varlen_recurrent.py make_case,
+    bench_kda_chunk.py): q, k, v, a ~ 0.2 N(0,1) bf16, b ~ N(0,1) bf16, A_log and
+    dt_bias ~ 0.1 N(0,1), pool ~ 0.1 N(0,1) K-contiguous, requests in slots 1..B."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    T, D = sum(lengths), 128
+    kw = {n: (torch.randn(1, T, heads, D, generator=g, device="cuda") * 0.2).bfloat16() for n in "qkva"}
+    kw["b"] = torch.randn(1, T, heads, generator=g, device="cuda").bfloat16()
+    kw["A_log"] = torch.randn(heads, generator=g, device="cuda") * 0.1
+    kw["dt_bias"] = torch.randn(heads * D, generator=g, device="cuda") * 0.1
+    kw["initial_state_source"] = (torch.randn(slots, heads, D, D, generator=g, device="cuda") * 0.1).transpose(-1, -2)
+    kw["initial_state_indices"] = torch.arange(1, len(lengths) + 1, dtype=torch.int32, device="cuda")
+    cu = [0]
+    for n in lengths:
+        cu.append(cu[-1] + n)
+    kw["cu_seqlens"] = torch.tensor(cu, dtype=torch.int32, device="cuda")
+    kw["lower_bound"] = -5.0
+    kw["scale"] = D ** -0.5
+    return kw
+
+
+def bench_published_shapes(args, dist: Dist, hbm_gbs: float, bf16_tf: float, iters: int, warmup: int) -> dict:
+    """Each shape the reference publishes an Ascend time for, through the
+    reference's own raw-gate ops on one GPU (every rank runs the same shapes;
+    the max over ranks is reported). Each call is timed alone with CUDA events
+    after an L2 flush (the inputs fit in L2); the median of `iters` calls."""
+    from sgl_glm53_ascend_ops import ops
+
+    decode = []
+    for H in (16, 32, 64):
+        for B in (1, 32, 128):
+            kw = _raw_case(H, [1] * B, B + 1, seed=H * 1000 + B)
+            ms = time_flushed(lambda: ops.kda_varlen_recurrent(**kw, prefill=False), iters, warmup, dist)
+            nbytes = B * H * (2 * 65536 + RAW_TOKEN_BYTES)
+            pub = PUBLISHED_DECODE_MS[(H, B)]
+            decode.append({"heads": H, "batch": B, "us": round(ms * 1e3, 2), "tokens_per_s": round(B / (ms / 1e3), 1),
+                           "hbm_gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                           "hbm_frac": round(nbytes / (ms / 1e3) / 1e9 / hbm_gbs, 4),
+                           "ascend_910b_ms": pub, "speedup_vs_ascend": round(pub / ms, 2)})
+            del kw
+    verify = []
+    for label, H, R in VERIFY_SHAPES:
+        kw = _raw_case(H, [DRAFT_TOKENS] * R, R + 1, seed=H * 100 + R)
+        mid = (torch.randn(R, DRAFT_TOKENS, H, 128, 128, device="cuda") * 0.1).transpose(-1, -2)
+        ms = time_flushed(lambda: ops.kda_varlen_recurrent(**kw, intermediate_state=mid, prefill=False),
+                          iters, warmup, dist)
+        # Commit: every request accepts its step 2 (dst = the pool's physical
+        # [layers=1, slots, H, V, K] view, src = the checkpoints').
+        dst = kw["initial_state_source"].unsqueeze(0).transpose(-1, -2)
+        src = mid.unsqueeze(0).transpose(-1, -2)
+        di = kw["initial_state_indices"]
+        si = torch.arange(R, dtype=torch.int32, device="cuda")
+        st = torch.full((R,), 2, dtype=torch.int32, device="cuda")
+        cms = time_flushed(lambda: ops.move_intermediate_cache_kda(dst, src, di, si, st), iters, warmup, dist)
+        vbytes = R * H * (65536 + DRAFT_TOKENS * 65536 + DRAFT_TOKENS * RAW_TOKEN_BYTES)
+        cbytes = R * H * 2 * 65536
+        row = {"shape": label, "heads": H, "requests": R, "draft_tokens": DRAFT_TOKENS,
+               "verify_us": round(ms * 1e3, 2), "verify_hbm_gbs": round(vbytes / (ms / 1e3) / 1e9, 1),
+               "verify_hbm_frac": round(vbytes / (ms / 1e3) / 1e9 / hbm_gbs, 4),
+               "commit_us": round(cms * 1e3, 2), "commit_hbm_gbs": round(cbytes / (cms / 1e3) / 1e9, 1)}
+        if label in PUBLISHED_VERIFY_US:
+            row["ascend_910b_us"] = PUBLISHED_VERIFY_US[label]
+            row["speedup_vs_ascend"] = round(PUBLISHED_VERIFY_US[label] / (ms * 1e3), 2)
+        verify.append(row)
+        del kw, mid
+    chunk = []
+    for T in (1024, 2048, 4096):
+        kw = _raw_case(8, [T], 2, seed=T)
+        ms = time_flushed(lambda: ops.kda_varlen_chunk(**kw, prefill=True), iters, warmup, dist)
+        flops = T * 8 * PREFILL_FLOPS_PER_TOKEN_HEAD
+        pub = PUBLISHED_CHUNK_MS[T]
+        chunk.append({"heads": 8, "tokens": T, "ms": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
+                      "tensor_tflops": round(flops / (ms / 1e3) / 1e12, 1),
+                      "ascend_910b_ms": pub, "speedup_vs_ascend": round(pub / ms, 2)})
+        del kw
+    torch.cuda.empty_cache()
+    return {"note": "the reference's published Ascend 910B shapes, raw-gate ops, per-call median after an L2 "
+                    "flush; the Ascend times are other hardware, context only",
+            "iters": iters, "warmup": warmup,
+            "decode": decode, "verify": verify, "chunk_prefill": chunk}
+
+
 def cpu_prefill_rate(tokens: int, budget_s: float, seed: int = 8):
     """tokens/s of the CPU chunk oracle on one sequence of `tokens` tokens, H=32."""
     from oracle import kda_ref
-    from sgl_glm53_ascend_ops import workloads
+    import kda_workloads as workloads
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -479,7 +760,7 @@ def cpu_decode_rate(requests: int, budget_s: float, seed: int = 7):
     """tokens/s of the CPU oracle on `requests` cfg2-shaped requests; repeats
     until `budget_s` seconds of work. Returns (rate, threads, sample text)."""
     from oracle import kda_ref
-    from sgl_glm53_ascend_ops import workloads
+    import kda_workloads as workloads
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -495,18 +776,26 @@ def cpu_decode_rate(requests: int, budget_s: float, seed: int = 7):
 
 
 def run_reference(args, dist: Dist):
+    """The reference arm: the reference's own algorithm for the path on this
+    host's cores. The reference is a PyTorch oracle plus Ascend-only kernels,
+    so what runs here is its CPU restatement (oracle/kda_ref.py, the
+    reference's kda_recur_torch with the packed-index fix), on the headline's
+    exact workload: every step is all 256 requests of config 2, H=32, D=128,
+    one token each, against the 512-slot pool, updated in place. Only torch,
+    the oracle and the input generator are imported: no library of this
+    repository is loaded into this process."""
     if dist.rank != 0:
         return
     from oracle import kda_ref
-    from sgl_glm53_ascend_ops import workloads
+    import kda_workloads as workloads
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    sample_req = 8
-    w = workloads.config2(seed=11, requests=sample_req, slots=sample_req + 1)
+    w = workloads.config2(seed=1000)
+    kw = w.kwargs()
 
     def step():
-        kda_ref.kda_varlen_recurrent_g(**w.kwargs(), out_fp32=True)
+        kda_ref.kda_varlen_recurrent_g(**kw, out_fp32=True)
 
     for _ in range(args.warmup):
         step()
@@ -515,13 +804,14 @@ def run_reference(args, dist: Dist):
         step()
     el = time.perf_counter() - t0
     value = args.steps * w.tokens / el
-    sample = f"each step: {sample_req} of config 2's 256 requests x 32 heads (oracle port, fp32)"
+    sample = ("every step: all 256 requests of config 2 x 32 heads against the 512-slot pool "
+              "(oracle port of the reference's kda_recur_torch, fp32)")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "cfg2 decode: 256 req x 1 tok, H=32, K=V=128, pool 512 slots (sampled)",
-                       "parallelism": "host cores"},
+            "config": {"workload": DECODE_WORKLOAD, "global_batch": 256, "per_gpu_batch": 256,
+                       "parallelism": "host cores (rank 0 only)"},
             "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -531,6 +821,11 @@ def run_reference(args, dist: Dist):
 
 # ---------------------------------------------------------------------------
 
+DECODE_WORKLOAD = ("cfg2 decode: 256 req x 1 tok, H=32, K=V=128, fp32 pool 512 slots, "
+                   "256 distinct slots updated in place (log-gate op)")
+LINES = ("prefill", "strong", "mixed", "long", "shapes")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -539,6 +834,8 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-oracle work")
     ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--lines", default=",".join(LINES),
+                    help="secondary lines to run besides the headline decode: " + ",".join(LINES))
     ap.add_argument("--mode", choices=("full", "kernel", "prefill-kernel", "prefill-long"), default="full",
                     help="kernel / prefill-kernel: only the timed decode / chunk op loop (profiler captures)")
     ap.add_argument("--prefill-heads", type=int, default=32,
@@ -546,6 +843,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    lines = {x for x in args.lines.split(",") if x}
+    if not lines <= set(LINES):
+        ap.error(f"--lines: unknown {sorted(lines - set(LINES))}")
 
     dist = Dist()
     if args.impl == "reference":
@@ -554,8 +854,10 @@ def main():
 
     dist.init_gpu()
     hbm_gbs, bf16_tf, bf16_tf_sus, peak_kind = _peaks()
+    args.peaks = (hbm_gbs, bf16_tf)
     if args.mode == "prefill-kernel":
-        from sgl_glm53_ascend_ops import ops, workloads
+        import kda_workloads as workloads
+        from sgl_glm53_ascend_ops import ops
         kw = workloads.config3(seed=2000 + dist.rank, heads=args.prefill_heads).to("cuda").kwargs()
         ms = time_steps(lambda: ops.kda_varlen_chunk_g(**kw, prefill=True), args.steps, args.warmup, dist)
         if dist.rank == 0:
@@ -569,7 +871,8 @@ def main():
         dist.close()
         return
     if args.mode == "kernel":
-        from sgl_glm53_ascend_ops import ops, workloads
+        import kda_workloads as workloads
+        from sgl_glm53_ascend_ops import ops
         kw = workloads.config2(seed=1000 + dist.rank).to("cuda").kwargs()
         ms = time_steps(lambda: ops.kda_varlen_recurrent_g(**kw, prefill=False), args.steps, args.warmup, dist)
         if dist.rank == 0:
@@ -577,17 +880,31 @@ def main():
         dist.close()
         return
     dec = bench_decode(args, dist, hbm_gbs, peak_kind)
+    torch.cuda.empty_cache()
 
-    pre = bench_prefill(args, dist, hbm_gbs, bf16_tf, steps=args.prefill_steps, warmup=3)
-    pre_long = bench_prefill_long(args, dist, steps=20, warmup=3)
+    extra = {}
+    if "prefill" in lines:
+        extra["prefill"] = bench_prefill(args, dist, hbm_gbs, bf16_tf, steps=args.prefill_steps, warmup=3)
+        torch.cuda.empty_cache()
+    if "strong" in lines:
+        extra["prefill_strong"] = bench_prefill_strong(args, dist, hbm_gbs, bf16_tf, steps=args.prefill_steps,
+                                                       warmup=3)
+    if "mixed" in lines:
+        extra["mixed"] = bench_mixed(args, dist, hbm_gbs, bf16_tf, steps=args.prefill_steps, warmup=3)
+    if "long" in lines:
+        extra["prefill_long"] = bench_prefill_long(args, dist, steps=20, warmup=3)
+        torch.cuda.empty_cache()
+    if "shapes" in lines:
+        extra["published_shapes"] = bench_published_shapes(args, dist, hbm_gbs, bf16_tf, iters=20, warmup=3)
 
     cpu = None
     if dist.rank == 0 and dist.world == 1:
         rate, threads, sample = cpu_decode_rate(32, args.cpu_budget)
         cpu = {"value": round(rate, 2), "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
-        prate, pthreads, psample = cpu_prefill_rate(512, args.cpu_budget)
-        pre["cpu_baseline"] = {"value": round(prate, 2), "unit": "tokens/s", "cores": pthreads, "kind": "port",
-                               "sample": psample}
+        if "prefill" in extra:
+            prate, pthreads, psample = cpu_prefill_rate(512, args.cpu_budget)
+            extra["prefill"]["cpu_baseline"] = {"value": round(prate, 2), "unit": "tokens/s", "cores": pthreads,
+                                                "kind": "port", "sample": psample}
 
     if dist.rank == 0:
         line = {
@@ -603,8 +920,7 @@ def main():
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": "cfg2 decode: 256 req x 1 tok, H=32, K=V=128, fp32 pool 512 slots, "
-                                   "256 distinct slots updated in place (log-gate op)",
+            "config": {"workload": DECODE_WORKLOAD,
                        "global_batch": 256 * dist.world, "per_gpu_batch": 256,
                        "l2": "inputs larger than L2 (1 GiB of state traffic per step), no flush",
                        "parallelism": f"dp{dist.world} (independent request batches, no collective)"},
@@ -613,8 +929,7 @@ def main():
             "e2e": dec["e2e"],
             "gpu_launches": dec["gpu_launches"],
             "clocks": dec["clocks"],
-            "prefill": pre,
-            "prefill_long": pre_long,
+            **extra,
         }
         print(json.dumps(line), flush=True)
     dist.close()

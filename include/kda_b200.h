@@ -130,14 +130,16 @@ const char *kda_status_string(int code);
 int kda_recurrent_launch(const KdaArgs *args, void *stream);
 
 /* Bytes of device workspace kda_chunk_launch needs for these sizes (replaces
- * kda_chunk::kWorkspaceFloatsPerBlock, kda_varlen_chunk.h:79-116). For batches
- * of few long sequences (requests x heads at most half the SM count) this is
- * the size of the split path's per-chunk records and state splits, ~210 KB
- * per chunk and head at D = 128 (plus a few MB of segment-boundary states);
- * otherwise a few bytes per request. The split-path size depends on the SM
- * count of the current device, so query it on the device that launches. */
-size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens,
-                                 int32_t num_heads, int32_t head_dim);
+ * kda_chunk::kWorkspaceFloatsPerBlock, kda_varlen_chunk.h:79-116).
+ * `num_heads` is the number of heads ONE launch processes, i.e. the
+ * `head_count` the launch's KdaArgs will carry (not the H of the tensors).
+ * For batches of few long sequences (requests x heads at most half the SM
+ * count, >= 8 chunks per request on average) this is the size of the split
+ * path's per-chunk records and state splits, ~210 KB per chunk and head at
+ * D = 128 (plus a few MB of segment-boundary states); otherwise a few bytes
+ * per request. The split-path size depends on the SM count of the current
+ * device, so query it on the device that launches. */
+size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens, int32_t num_heads, int32_t head_dim);
 
 /* Chunk-64 WY/UT prefill over a varlen batch, any sequence lengths. The
  * workspace must be at least kda_chunk_workspace_bytes(...) bytes; its
@@ -148,11 +150,29 @@ size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens,
  * few long sequences, a split path: a prep kernel over all (chunk, head)
  * pairs, a state scan that cuts long sequences into segments scanned side by
  * side and then chained, and an output kernel over all (chunk, head) pairs.
- * The split path runs only when the workspace holds it (256-byte aligned).
- * The environment variable KDA_CHUNK_PATH=fused or =split overrides the
- * choice. */
-int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes,
-                     void *stream);
+ * The choice depends only on the call's sizes and the device's SM count; the
+ * split path runs only when the workspace holds it (256-byte aligned), else
+ * the fused kernel. */
+int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Which internal path a chunk launch takes (kda_chunk_launch_path). */
+typedef enum KdaChunkPath {
+    KDA_CHUNK_AUTO = 0,   /* the library's choice, as kda_chunk_launch */
+    KDA_CHUNK_FUSED = 1,  /* always the fused kernel */
+    KDA_CHUNK_SPLIT = 2   /* always the split path (at most 1024 requests) */
+} KdaChunkPath;
+
+/* Verification hook, no counterpart in the reference: kda_chunk_launch with
+ * the path forced, so tests can run every case on both paths. A forced split
+ * whose workspace is smaller than kda_chunk_path_workspace_bytes(...,
+ * KDA_CHUNK_SPLIT) returns KDA_ERR_WORKSPACE instead of falling back. */
+int kda_chunk_launch_path(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream,
+                          int32_t path);
+
+/* Workspace bytes kda_chunk_launch_path needs for `path` (0 for an unknown
+ * path); for KDA_CHUNK_AUTO the same as kda_chunk_workspace_bytes. */
+size_t kda_chunk_path_workspace_bytes(int32_t num_req, int32_t num_tokens, int32_t num_heads, int32_t head_dim,
+                                      int32_t path);
 
 /* Measurement hook, no counterpart in the reference: the split path of
  * kda_chunk_launch with six caller-created cudaEvent_t handles recorded on
@@ -171,7 +191,13 @@ int kda_chunk_launch_phases(const KdaArgs *args, void *workspace, size_t workspa
 /* kda_chunk_launch for callers that cannot provide device memory: the same
  * prefill, with its only scratch (the longest-first request order, one int32
  * per request) kept in an array compiled into the library, so this entry
- * point never allocates. It serves callers whose device memory is already
+ * point never allocates. It always runs the fused kernel: the split path
+ * that kda_chunk_launch picks for few long sequences keeps per-chunk records
+ * in the caller's workspace, which this entry point does not have. Results
+ * agree with kda_chunk_launch within the fp32 tolerances on every batch, but
+ * a batch of few long sequences (e.g. one 128K-token context over 4 heads)
+ * runs several times slower here than through kda_chunk_launch with a full
+ * workspace. It serves callers whose device memory is already
  * fully claimed by their own pools, or hosts reaching the library through an
  * FFI with no device allocator. No counterpart in the reference, which always
  * allocates its workspace per call.
@@ -222,6 +248,19 @@ typedef struct KdaCommitArgs {
 } KdaCommitArgs;
 
 int kda_commit_intermediate_launch(const KdaCommitArgs *args, void *stream);
+
+/* Self-test of the bounded waits, no counterpart in the reference (whose
+ * kernels wait without a limit). One CTA of 64 threads makes `waits` (1..64)
+ * successive waits, of at most `polls` polls each (a poll suspends for up to
+ * ~1 us), on an mbarrier that nothing arrives on: the same bounded wait every
+ * kernel of this library uses. With `give_up` nonzero the CTA-wide give-up
+ * word is used, as the chunk kernels use it: after the first expiry the
+ * remaining waits give up at their first poll. Each expired wait writes
+ * KDA_DEVICE_ERR_WAIT_TIMEOUT into *status (first error wins) and adds one to
+ * *expired (both device int32); the kernel then ends normally and the context
+ * stays usable. */
+int kda_selftest_wait_timeout(int32_t *status, int32_t *expired, int32_t polls, int32_t waits, int32_t give_up,
+                              void *stream);
 
 #ifdef __cplusplus
 }

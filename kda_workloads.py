@@ -1,6 +1,10 @@
 """Seeded synthetic inputs with the shapes and value distributions of the
 benchmark configurations (the reference publishes no dataset for this path).
 
+Test and benchmark infrastructure, not part of the operator package: it
+imports only torch, so the benchmark's CPU reference arm can use it without
+loading any library of this repository.
+
 Every tensor is drawn on the CPU with ``torch.manual_seed`` so a workload is
 the same on any machine, then moved to ``device``:
 

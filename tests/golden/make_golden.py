@@ -40,7 +40,8 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
+# The reference checkout: given by the caller, never assumed.
+REF_ROOT = Path(os.environ["REF_ROOT"]) if os.environ.get("REF_ROOT") else None
 
 
 def _stub(name, **attrs):
@@ -52,6 +53,9 @@ def _stub(name, **attrs):
 
 
 def _load_reference():
+    if REF_ROOT is None or not REF_ROOT.is_dir():
+        raise SystemExit("set REF_ROOT to the reference checkout (the directory holding bench/ and "
+                         "sgl-glm53-ascend-ops/)")
     _stub("torch_npu")
     pkg = _stub("sgl_glm53_ascend_ops")
     pkg.__path__ = []

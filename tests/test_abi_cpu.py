@@ -109,6 +109,24 @@ def test_commit_arguments_rejected_without_launch(abi):
 def test_workspace_size_is_queryable(abi):
     n = abi.chunk_workspace_bytes(8, 33494, 32, 128)
     assert n >= 0
+    assert abi.chunk_path_workspace_bytes(8, 33494, 32, 128, abi.KDA_CHUNK_AUTO) == n
+    fused = abi.chunk_path_workspace_bytes(8, 33494, 32, 128, abi.KDA_CHUNK_FUSED)
+    split = abi.chunk_path_workspace_bytes(8, 33494, 32, 128, abi.KDA_CHUNK_SPLIT)
+    assert 0 < fused <= 256 < split              # the request order alone vs. per-chunk records
+    assert abi.chunk_path_workspace_bytes(8, 33494, 32, 128, 7) == 0
+    assert abi.chunk_path_workspace_bytes(2000, 33494, 32, 128, abi.KDA_CHUNK_FUSED) == 0   # > 1024 requests
+
+
+def test_forced_path_and_selftest_arguments_rejected_without_launch(abi):
+    lib = abi.lib()
+    a = abi.KdaArgs()
+    a.head_dim, a.num_heads = 128, 1
+    a.index_bytes[:] = [4, 4, 4, 4]
+    assert lib.kda_chunk_launch_path(ctypes.byref(a), None, 0, None, 3) == abi.KDA_ERR_INVALID_ARGUMENT
+    assert lib.kda_chunk_launch_path(ctypes.byref(a), None, 0, None, abi.KDA_CHUNK_SPLIT) == abi.KDA_OK  # empty
+    a.num_req, a.head_count = 2, 1
+    assert lib.kda_chunk_launch_path(ctypes.byref(a), None, 0, None, abi.KDA_CHUNK_SPLIT) == 1   # null pointers
+    assert lib.kda_selftest_wait_timeout(None, None, 16, 1, 1, None) == abi.KDA_ERR_INVALID_ARGUMENT
 
 
 def test_plugin_registers_prepared_recurrent():

@@ -5,21 +5,24 @@ chunks and sequences, the zero slot, tracked checkpoints before, inside, on the
 boundary of and at the end of a chunk; untouched slots) and adds what the B200
 op supports beyond it: lengths that are not multiples of 64, any head count,
 K = V = 64, the log-gate entry point, BASELINE config 3 at full size, int64
-metadata and CUDA-graph replay. Every test runs twice: with the library's own
-choice between the fused kernel and the split path (prep + scan kernels), and
-with the split path forced (KDA_CHUNK_PATH=split), so both are covered.
-BASELINE config 4 (one 131,072-token sequence) runs on the split path at full
-size. Tolerances: tests/kda_checks.py.
+metadata and CUDA-graph replay. Every oracle test runs twice: through the
+torch op with the library's own choice between the fused kernel and the split
+path (prep + scan kernels), and through the C ABI with the split path forced
+(kda_chunk_launch_path), so both are covered. BASELINE configs 3 and 4 are
+checked on every head against the oracle, and configs 3, 5 and a tracked case
+also through the kernel's fp32 pre-cast output, at the output bar with no
+rounding credit. Tolerances: tests/kda_checks.py.
 """
-
-import os
 
 import pytest
 import torch
 
+from chunk_abi import chunk_via_abi
 from golden_io import bf16, expected_pool, kcontig, load, raw_kwargs
 from kda_checks import assert_out_close, assert_state_close, assert_untouched, clone_pool
 from oracle import kda_ref
+
+KDA_CHUNK_AUTO, KDA_CHUNK_FUSED, KDA_CHUNK_SPLIT = 0, 1, 2   # KdaChunkPath
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -32,15 +35,22 @@ def ops():
     return _ops
 
 
-@pytest.fixture(autouse=True, params=["auto", "split"])
-def chunk_path(request, monkeypatch):
-    """Selects the chunk prefill path through the variable the library reads
-    on every launch; "auto" leaves the library's own choice."""
-    if request.param == "auto":
-        monkeypatch.delenv("KDA_CHUNK_PATH", raising=False)
-    else:
-        monkeypatch.setenv("KDA_CHUNK_PATH", request.param)
+@pytest.fixture(params=["auto", "split"])
+def chunk_path(request):
+    """"auto": the torch op, with the library's own path choice; "split": the
+    C ABI with the split path forced."""
     return request.param
+
+
+def _run(ops, dkw, path):
+    """One chunk prefill on device kwargs: the torch op (raw or log gate) for
+    "auto", kda_chunk_launch_path with the split path forced for "split"."""
+    if path == "split":
+        return chunk_via_abi(dkw, KDA_CHUNK_SPLIT)
+    op = ops.kda_varlen_chunk if "a" in dkw else ops.kda_varlen_chunk_g
+    out = op(**dkw, prefill=True)
+    torch.cuda.synchronize()
+    return out
 
 
 def _dev(kw):
@@ -72,10 +82,9 @@ def _case(heads, cu_seqlens, slots, track=None, seed=0, D=128, lower_bound=-5.0)
     return kw
 
 
-def _check(ops, kw, touched):
+def _check(ops, kw, touched, path):
     dkw = _dev(kw)
-    out = ops.kda_varlen_chunk(**dkw, prefill=True)
-    torch.cuda.synchronize()
+    out = _run(ops, dkw, path)
     ref_pool = clone_pool(kw["initial_state_source"])
     ref = kda_ref.kda_varlen_chunk(**dict(kw, initial_state_source=ref_pool), out_fp32=True)
     got = dkw["initial_state_source"].cpu()
@@ -101,15 +110,15 @@ CASES = [
 
 
 @pytest.mark.parametrize("label,heads,cu_seqlens,slots,track", CASES, ids=[c[0].replace(" ", "-") for c in CASES])
-def test_chunk_matches_oracle(ops, label, heads, cu_seqlens, slots, track):
+def test_chunk_matches_oracle(ops, chunk_path, label, heads, cu_seqlens, slots, track):
     kw = _case(heads, cu_seqlens, slots, track, seed=len(label))
     touched = {s for s in slots if s > 0} | ({track[0][0]} if track else set())
-    _check(ops, kw, touched)
+    _check(ops, kw, touched, chunk_path)
 
 
-def test_chunk_leaves_other_slots_untouched(ops):
+def test_chunk_leaves_other_slots_untouched(ops, chunk_path):
     kw = _case(2, [0, 128], [3])
-    _check(ops, kw, {3})
+    _check(ops, kw, {3}, chunk_path)
 
 
 # Lengths the reference rejects (kda_varlen_chunk.cpp:139-142): any length.
@@ -124,21 +133,20 @@ RAGGED = [
 
 @pytest.mark.parametrize("cu_seqlens,slots,track", RAGGED, ids=lambda x: str(x))
 @pytest.mark.parametrize("D", (64, 128))
-def test_ragged_lengths_match_oracle(ops, cu_seqlens, slots, track, D):
+def test_ragged_lengths_match_oracle(ops, chunk_path, cu_seqlens, slots, track, D):
     kw = _case(3, cu_seqlens, slots, track, seed=sum(cu_seqlens), D=D)
     touched = {s for s in slots if s > 0} | ({s for s in track[0] if s > 0} if track else set())
-    _check(ops, kw, touched)
+    _check(ops, kw, touched, chunk_path)
 
 
 @pytest.mark.parametrize("name", ["chunk_raw_tracked", "chunktest_ragged_varlen", "chunktest_zero_slot",
                                   "chunktest_track_at_0", "chunktest_track_mid_chunk", "chunktest_track_at_end"])
-def test_chunk_matches_reference_golden(ops, name):
+def test_chunk_matches_reference_golden(ops, chunk_path, name):
     f = load(name)
     kw = raw_kwargs(f)
     kw["initial_state_source"] = kcontig(f["pool_in"])
     dkw = _dev(kw)
-    out = ops.kda_varlen_chunk(**dkw, prefill=True)
-    torch.cuda.synchronize()
+    out = _run(ops, dkw, chunk_path)
     ref_out = torch.from_numpy(f["out"])
     if name == "chunk_raw_tracked":
         ref_out = ref_out.bfloat16()              # kda_chunk_torch returned bf16
@@ -149,19 +157,18 @@ def test_chunk_matches_reference_golden(ops, name):
 
 
 @pytest.mark.parametrize("lower_bound", (-1.0, -5.0, -10.0))
-def test_gate_strength(ops, lower_bound):
+def test_gate_strength(ops, chunk_path, lower_bound):
     """Gates down to -10 per step: the 16-row anchors keep every factor in range."""
     kw = _case(2, [0, 200, 328], [1, 2], seed=3, lower_bound=lower_bound)
-    _check(ops, kw, {1, 2})
+    _check(ops, kw, {1, 2}, chunk_path)
 
 
-def test_loggate_matches_oracle(ops):
-    from sgl_glm53_ascend_ops import workloads
+def test_loggate_matches_oracle(ops, chunk_path):
+    import kda_workloads as workloads
     w = workloads.config3(heads=4, lengths=[700, 64, 1, 333])
     w.pool = (torch.randn(w.pool.shape[0], 4, 128, 128) * 0.1).transpose(-1, -2)
     d = w.to(DEV)
-    out = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
-    torch.cuda.synchronize()
+    out = _run(ops, d.kwargs(), chunk_path)
     ref_pool = clone_pool(w.pool)
     ref = kda_ref.kda_varlen_chunk_g(**dict(w.kwargs(), initial_state_source=ref_pool), out_fp32=True)
     assert_out_close(out.cpu(), ref)
@@ -189,35 +196,52 @@ SEGMENTED = [
 
 @pytest.mark.parametrize("heads,cu_seqlens,slots,track", SEGMENTED, ids=lambda x: str(x))
 @pytest.mark.parametrize("D", (64, 128))
-def test_segmented_scan_matches_oracle(ops, heads, cu_seqlens, slots, track, D):
+def test_segmented_scan_matches_oracle(ops, chunk_path, heads, cu_seqlens, slots, track, D):
     kw = _case(heads, cu_seqlens, slots, track, seed=len(cu_seqlens) + D, D=D)
     touched = {s for s in slots if s > 0} | ({s for s in track[0] if s > 0} if track else set())
-    _check(ops, kw, touched)
+    _check(ops, kw, touched, chunk_path)
 
 
-def test_cfg3_full_size(ops):
-    """8 sequences (33,494 tokens, none a multiple of 64), H=32.
-
-    The oracle runs on the token recurrence for heads 0..3 (it is exact and
-    fast on the CPU); the kernel output and final states of those heads are
-    checked, and the remaining heads through their own size-independent
-    properties (finite, deterministic across two runs)."""
-    from sgl_glm53_ascend_ops import workloads
+@pytest.fixture(scope="module")
+def cfg3_oracle():
+    """BASELINE config 3 (8 sequences, 33,494 tokens, none a multiple of 64,
+    H=32) and the oracle's fp32 output and final states for all 32 heads (the
+    token recurrence, exact and fast enough on the CPU)."""
+    import kda_workloads as workloads
     w = workloads.config3()
+    ref_pool = clone_pool(w.pool)
+    ref = kda_ref.kda_varlen_recurrent_g(**dict(w.kwargs(), initial_state_source=ref_pool), out_fp32=True)
+    return w, ref, ref_pool
+
+
+@pytest.mark.parametrize("path", ["auto", "split"])
+def test_cfg3_full_size(ops, cfg3_oracle, path):
+    """Config 3 at full size, every head: output and the 8 final states against
+    the oracle; a second run from the same pool is bit-identical."""
+    w, ref, ref_pool = cfg3_oracle
     d = w.to(DEV)
     pool0 = clone_pool(d.pool)
-    out = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
+    out = _run(ops, d.kwargs(), path)
     pool_a = clone_pool(d.pool)
     d.pool.copy_(pool0)
-    out_b = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
-    torch.cuda.synchronize()
+    out_b = _run(ops, d.kwargs(), path)
     assert torch.equal(out, out_b) and torch.equal(pool_a, d.pool), "not deterministic"
-    assert torch.isfinite(out.float()).all()
-    sub = w.head_shard(0, 8)                          # heads 0..3
-    ref_pool = clone_pool(sub.pool)
-    ref = kda_ref.kda_varlen_recurrent_g(**dict(sub.kwargs(), initial_state_source=ref_pool), out_fp32=True)
-    assert_out_close(out[:, :, 0:4].cpu(), ref)
-    assert_state_close(pool_a[1:, 0:4].cpu(), ref_pool[1:])
+    got = out.cpu()
+    for h0 in range(0, 32, 4):
+        assert_out_close(got[:, :, h0:h0 + 4], ref[:, :, h0:h0 + 4], what=f"output heads {h0}..{h0 + 3}")
+    assert_state_close(pool_a[1:].cpu(), ref_pool[1:])
+
+
+@pytest.mark.parametrize("path", [KDA_CHUNK_FUSED, KDA_CHUNK_SPLIT], ids=["fused", "split"])
+def test_cfg3_fp32_output(ops, cfg3_oracle, path):
+    """Config 3, every head, through the kernel's fp32 pre-cast output: max-abs
+    error <= 5e-3 of the output RMS with no rounding credit."""
+    w, ref, ref_pool = cfg3_oracle
+    d = w.to(DEV)
+    out = chunk_via_abi(d.kwargs(), path, out_fp32=True)
+    assert out.dtype == torch.float32
+    assert_out_close(out.cpu(), ref, what="fp32 output")
+    assert_state_close(d.pool.cpu()[1:], ref_pool[1:])
 
 
 def test_chunk_equals_recurrent_kernel(ops):
@@ -245,11 +269,9 @@ def test_int64_metadata_bitwise(ops):
     assert torch.equal(a["initial_state_source"], b["initial_state_source"])
 
 
-def test_chunk_launch_phases_matches_launch(ops, chunk_path):
+def test_chunk_launch_phases_matches_launch(ops):
     """The measurement hook runs the same split path: bit-identical outputs and
     pool, six ordered events; a batch that takes the fused kernel is refused."""
-    if chunk_path != "auto":
-        pytest.skip("one run suffices")
     from sgl_glm53_ascend_ops import abi
     kw = _case(2, [0, 3000, 3001], [1, 2], ([3, 0], [1024, 0]), seed=41)
     runs = []
@@ -326,14 +348,13 @@ def test_chunk_cuda_graph_replay(ops):
     del graph
 
 
-def test_cfg4_long_context(ops, chunk_path):
+def test_cfg4_long_context(ops):
     """one 131,072-token sequence (2048 chunks), here 4 heads
-    with an fp32 initial state. Head 0 is checked against the oracle's token
-    recurrence over the whole sequence; the fused kernel and the split path
-    agree; the run is deterministic."""
-    if chunk_path != "auto":
-        pytest.skip("config 4 already takes the split path by itself")
-    from sgl_glm53_ascend_ops import workloads
+    with an fp32 initial state. The op takes the split path by itself; every
+    head's output and final state are checked against the oracle's token
+    recurrence over the whole sequence, the run is deterministic, and the
+    fused kernel (forced through the C ABI) agrees with it."""
+    import kda_workloads as workloads
     w = workloads.config4(seed=4, heads=4)
     d = w.to(DEV)
     pool0 = clone_pool(d.pool)
@@ -343,38 +364,72 @@ def test_cfg4_long_context(ops, chunk_path):
     out_b = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
     torch.cuda.synchronize()
     assert torch.equal(out, out_b) and torch.equal(pool_split, d.pool), "not deterministic"
-    os.environ["KDA_CHUNK_PATH"] = "fused"
-    try:
-        d.pool.copy_(pool0)
-        out_f = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
-        torch.cuda.synchronize()
-    finally:
-        del os.environ["KDA_CHUNK_PATH"]
+    d.pool.copy_(pool0)
+    out_f = chunk_via_abi(d.kwargs(), KDA_CHUNK_FUSED)
     assert_out_close(out_f.cpu(), out.cpu())          # both bf16: one-ulp credit
     assert_state_close(d.pool.cpu()[1:], pool_split.cpu()[1:])
-    sub = w.head_shard(0, 4)                          # head 0
-    ref_pool = clone_pool(sub.pool)
-    ref = kda_ref.kda_varlen_recurrent_g(**dict(sub.kwargs(), initial_state_source=ref_pool), out_fp32=True)
-    assert_out_close(out[:, :, 0:1].cpu(), ref)
-    assert_state_close(pool_split[1:, 0:1].cpu(), ref_pool[1:])
+    got = out.cpu()
+    ref_pool = clone_pool(w.pool)
+    ref = kda_ref.kda_varlen_recurrent_g(**dict(w.kwargs(), initial_state_source=ref_pool), out_fp32=True)
+    for h in range(4):
+        assert_out_close(got[:, :, h:h + 1], ref[:, :, h:h + 1], what=f"output head {h}")
+        assert_state_close(pool_split[1:, h:h + 1].cpu(), ref_pool[1:, h:h + 1], what=f"state head {h}")
 
 
-def test_cfg5_mixed_batch(ops):
-    """BASELINE config 5 in one chunk-op call: 64 one-token requests and 4
-    resumed 2048-token prefills (68 distinct slots of a 1024-slot pool, nonzero
-    states), H=32. Outputs and the 68 updated slots against the oracle; the
-    955 other slots bit-equal."""
-    from sgl_glm53_ascend_ops import workloads
+@pytest.fixture(scope="module")
+def cfg5_oracle():
+    """64 one-token requests and 4 resumed 2048-token
+    prefills (68 distinct slots of a 1024-slot pool, nonzero states), H=32,
+    with the oracle's fp32 output and pool."""
+    import kda_workloads as workloads
     w = workloads.config5()
     before = clone_pool(w.pool)
+    ref_pool = clone_pool(w.pool)
+    ref = kda_ref.kda_varlen_recurrent_g(**dict(w.kwargs(), initial_state_source=ref_pool), out_fp32=True)
+    return w, before, ref, ref_pool
+
+
+def test_cfg5_mixed_batch(ops, cfg5_oracle):
+    """Config 5 in one chunk-op call: outputs and the 68 updated slots against
+    the oracle; the 955 other slots bit-equal."""
+    w, before, ref, ref_pool = cfg5_oracle
     d = w.to(DEV)
     out = ops.kda_varlen_chunk_g(**d.kwargs(), prefill=True)
     torch.cuda.synchronize()
     got = d.pool.cpu()
     del d
-    ref_pool = clone_pool(w.pool)
-    ref = kda_ref.kda_varlen_recurrent_g(**dict(w.kwargs(), initial_state_source=ref_pool), out_fp32=True)
     assert_out_close(out.cpu(), ref)
     touched = [int(s) for s in w.indices]
     assert_state_close(got[touched], ref_pool[touched])
     assert_untouched(got, before, touched)
+
+
+def test_cfg5_fp32_output(ops, cfg5_oracle):
+    """Config 5 through the kernel's fp32 pre-cast output (C ABI): the output
+    bar with no rounding credit, the updated slots, the untouched slots."""
+    w, before, ref, ref_pool = cfg5_oracle
+    d = w.to(DEV)
+    out = chunk_via_abi(d.kwargs(), KDA_CHUNK_AUTO, out_fp32=True)
+    got = d.pool.cpu()
+    del d
+    assert_out_close(out.cpu(), ref, what="fp32 output")
+    touched = [int(s) for s in w.indices]
+    assert_state_close(got[touched], ref_pool[touched])
+    assert_untouched(got, before, touched)
+
+
+@pytest.mark.parametrize("path", [KDA_CHUNK_FUSED, KDA_CHUNK_SPLIT], ids=["fused", "split"])
+def test_tracked_fp32_output(ops, path):
+    """Tracked checkpoints (before, inside, on the boundary of and at the end
+    of a chunk, and in a segmented request) through the fp32 pre-cast output."""
+    kw = _case(2, [0, 63, 65, 265, 3465], [1, 2, 5, 3], ([4, 0, 6, 7], [63, 0, 135, 1700]), seed=77)
+    dkw = _dev(kw)
+    out = chunk_via_abi(dkw, path, out_fp32=True)
+    ref_pool = clone_pool(kw["initial_state_source"])
+    ref = kda_ref.kda_varlen_chunk(**dict(kw, initial_state_source=ref_pool), out_fp32=True)
+    assert_out_close(out.cpu(), ref, what="fp32 output")
+    got = dkw["initial_state_source"].cpu()
+    touched = {1, 2, 5, 3, 4, 6, 7}
+    for s in touched:
+        assert_state_close(got[s], ref_pool[s], what=f"slot {s}")
+    assert_untouched(got, kw["initial_state_source"], touched)

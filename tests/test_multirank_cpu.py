@@ -33,7 +33,7 @@ def _worker(rank: int, world: int, port: int, result_path: str):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from oracle import kda_ref
-        from sgl_glm53_ascend_ops.workloads import Workload, config2
+        from kda_workloads import Workload, config2
 
         torch.set_num_threads(1)
         w = config2(requests=6, heads=4, slots=9)
@@ -57,7 +57,7 @@ def _worker(rank: int, world: int, port: int, result_path: str):
 def test_head_shards_reassemble_on_two_gloo_ranks(tmp_path):
     sys.path[:0] = [str(ROOT / "01-glm53-ascend_b200")]
     from oracle import kda_ref
-    from sgl_glm53_ascend_ops.workloads import config2
+    from kda_workloads import config2
 
     result = tmp_path / "r.pt"
     mp.start_processes(_worker, args=(2, _free_port(), str(result)), nprocs=2, start_method="spawn")
@@ -72,7 +72,7 @@ def test_head_shards_reassemble_on_two_gloo_ranks(tmp_path):
 
 def test_head_shard_layout():
     sys.path[:0] = [str(ROOT / "01-glm53-ascend_b200")]
-    from sgl_glm53_ascend_ops.workloads import config3
+    from kda_workloads import config3
 
     w = config3(heads=8, lengths=[5, 3])
     s = w.head_shard(1, 4)

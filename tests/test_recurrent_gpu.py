@@ -179,7 +179,7 @@ def test_decode_checkpoints_match_oracle(ops, heads, lengths):
 
 def test_cfg2_decode_full_size(ops):
     """BASELINE config 2 at full size: 256 requests, H=32, pool of 512 slots."""
-    from sgl_glm53_ascend_ops import workloads
+    import kda_workloads as workloads
     w = workloads.config2()
     before = clone_pool(w.pool)
     d = w.to(DEV)
@@ -202,7 +202,7 @@ def test_cfg5_mixed_batch_recurrent(ops):
     """BASELINE config 5 through the recurrent op in its prefill regime (the
     whole mixed batch of 64 one-token and 4 resumed 2048-token requests in one
     call): outputs and updated slots against the oracle, other slots bit-equal."""
-    from sgl_glm53_ascend_ops import workloads
+    import kda_workloads as workloads
     w = workloads.config5(seed=1)
     before = clone_pool(w.pool)
     d = w.to(DEV)
@@ -219,7 +219,7 @@ def test_cfg5_mixed_batch_recurrent(ops):
 
 
 def test_abi_fp32_output_meets_bar(abi):
-    from sgl_glm53_ascend_ops import workloads
+    import kda_workloads as workloads
     w = workloads.config2(requests=64, heads=8, slots=80)
     d = w.to(DEV)
     out32 = torch.empty(d.v.shape, dtype=torch.float32, device=DEV)
@@ -256,7 +256,7 @@ def test_abi_matches_torch_op_bitwise(ops, abi):
 
 def test_abi_reports_bad_slot_without_touching_memory(abi):
     """An out-of-range slot index is caught by the kernel's bounds check."""
-    from sgl_glm53_ascend_ops import workloads
+    import kda_workloads as workloads
     w = workloads.config2(requests=4, heads=2, slots=8)
     d = w.to(DEV)
     d.indices[2] = 8                                   # one past the pool

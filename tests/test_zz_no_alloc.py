@@ -6,7 +6,10 @@ allocator. This entry point serves them by keeping the chunk prefill's only
 scratch (the request order) in an array compiled into the library. The test
 calls it through the C ABI twice in a row, with different batches, and checks
 each result against `kda_chunk_launch` given a workspace, at the tolerances of
-tests/kda_checks.py; it also checks the capacity limit. The file name sorts
+tests/kda_checks.py; it also checks the capacity limit. A third call uses a
+batch of one long sequence over two heads, for which `kda_chunk_launch` with
+a full workspace takes its split path while this entry point (no room for the
+split path's records) always runs the fused kernel: the two paths must agree. The file name sorts
 last so that a run stopping at the first failure has run everything else.
 """
 
@@ -20,7 +23,7 @@ DEV = "cuda"
 
 
 def _batch(lengths, heads, seed):
-    from sgl_glm53_ascend_ops import workloads
+    import kda_workloads as workloads
     w = workloads.config3(seed=seed, heads=heads, lengths=lengths)
     w.pool = (torch.randn(w.pool.shape[0], heads, 128, 128) * 0.1).transpose(-1, -2)
     return w.to(DEV)
@@ -35,11 +38,13 @@ def _args(abi, d, out, pool):
 def test_no_alloc_matches_workspace_entry_point_twice():
     from sgl_glm53_ascend_ops import abi
 
-    for lengths, heads, seed in (([300, 64, 1, 129, 70], 4, 11), ([65, 200], 2, 12)):
+    for lengths, heads, seed in (([300, 64, 1, 129, 70], 4, 11), ([65, 200], 2, 12), ([2048], 2, 14)):
         d = _batch(lengths, heads, seed)
         pool_ref, pool_new = clone_pool(d.pool), clone_pool(d.pool)
         out_ref, out_new = torch.empty_like(d.v), torch.empty_like(d.v)
         nws = abi.chunk_workspace_bytes(d.indices.numel(), d.tokens, heads, 128)
+        if lengths == [2048]:
+            assert nws > 4096, "the workspace entry point should take its split path here"
         ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=DEV)
         assert abi.chunk_launch(_args(abi, d, out_ref, pool_ref), ws, nws) == abi.KDA_OK
         assert abi.chunk_launch_no_alloc(_args(abi, d, out_new, pool_new)) == abi.KDA_OK
