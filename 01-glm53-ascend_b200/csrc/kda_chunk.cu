@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(1024) order_kernel(const KdaArgs p, int32_t *o
 template <int D, int MODE, bool PREP>
 __global__ void __launch_bounds__(kThreads + 32, 1)
     chunk_kernel(const KdaArgs p, const int32_t *order, const __grid_constant__ TmaMaps maps, uint8_t *rec,
-                 uint8_t *trec, const int32_t *cbase) {
+                 uint8_t *trec, const int32_t *cbase, int32_t skip_hi) {
     using L = Smem<D>;
     constexpr int KS = D / 16;              // k-steps over the key dim
     constexpr int ELEM = 4 * D;             // threads of the column-per-thread passes
@@ -640,6 +640,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
     const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
     const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
     const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
+    // Requests of 1..skip_hi tokens went to the token recurrence of the same
+    // launch (kda_chunk_launch's fused path): nothing to do here.
+    if (eos - bos >= 1 && eos - bos <= skip_hi) return;
     if (bos < 0 || eos < bos || eos > p.num_tokens) {
         if (tid == 0) report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
         return;
@@ -2859,7 +2862,7 @@ static bool opt_in(K kernel, bool (&done)[64], int bytes) {
 }
 
 template <int D, int MODE>
-static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
+static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st, int32_t skip_hi) {
     using L = chunk::Smem<D>;
     chunk::TmaMaps maps;
     if (!encode_maps(maps, a, D, MODE == KDA_GATE_RAW)) return KDA_ERR_LAUNCH;
@@ -2868,7 +2871,7 @@ static int launch_chunk(const KdaArgs *a, int32_t *order, cudaStream_t st) {
     if (order != nullptr) chunk::order_kernel<<<1, 1024, 0, st>>>(*a, order);
     const int64_t grid = static_cast<int64_t>(a->num_req) * a->head_count;
     chunk::chunk_kernel<D, MODE, false><<<static_cast<unsigned>(grid), chunk::kThreads + 32, L::kAlloc, st>>>(
-        *a, order, maps, nullptr, nullptr, nullptr);
+        *a, order, maps, nullptr, nullptr, nullptr, skip_hi);
     return KDA_OK;
 }
 
@@ -2894,6 +2897,9 @@ static int sm_count() {
 }
 
 static bool split_ok(int32_t num_req) { return num_req > 0 && num_req <= 1024; }
+
+// Longest request the fused path hands to the token recurrence.
+constexpr int32_t kShortLen = 16;
 
 // The library's own choice: the split path when the (sequence, head) chains
 // fill at most half the SMs and the sequences average >= 8 chunks.
@@ -2961,7 +2967,7 @@ static int launch_chunk_split(const KdaArgs *a, uint8_t *ws, cudaStream_t st, cu
     chunk::plan_kernel<<<1, 1024, 0, st>>>(*a, cbase, plan, lay.budget, lay.task_cap, lay.slot_cap);
     const int64_t slots = static_cast<int64_t>(a->num_tokens) / chunk::BT + a->num_req;
     chunk::chunk_kernel<D, MODE, true><<<static_cast<unsigned>(slots * a->head_count), chunk::kThreads + 32,
-                                         L::kAlloc, st>>>(*a, nullptr, maps, rec, trec, cbase);
+                                         L::kAlloc, st>>>(*a, nullptr, maps, rec, trec, cbase, 0);
     mark(1);
     // Segmented scan: first pass, combine, rescan (CTAs past a phase's task
     // count exit at once).
@@ -3124,12 +3130,23 @@ static int chunk_launch_path(const KdaArgs *args, void *workspace, size_t worksp
         if ((reinterpret_cast<uintptr_t>(workspace) & 3u) != 0) return KDA_ERR_ALIGNMENT;
         order = static_cast<int32_t *>(workspace);
     }
+    // The library's own choice hands requests of 1..kShortLen tokens (decode
+    // and verify requests in a mixed batch) to the token recurrence, where a
+    // token costs one step instead of a whole 64-row chunk; the chunk kernel
+    // skips them. A forced fused path runs every request through the chunk
+    // kernel.
+    int32_t skip_hi = 0;
+    if (path == KDA_CHUNK_AUTO) {
+        rc = recurrent_launch_range(args, 1, kShortLen, st);
+        if (rc != KDA_OK) return rc;
+        skip_hi = kShortLen;
+    }
     if (args->head_dim == 128)
-        rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk<128, KDA_GATE_RAW>(args, order, st)
-                                             : launch_chunk<128, KDA_GATE_LOG>(args, order, st);
+        rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk<128, KDA_GATE_RAW>(args, order, st, skip_hi)
+                                             : launch_chunk<128, KDA_GATE_LOG>(args, order, st, skip_hi);
     else
-        rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk<64, KDA_GATE_RAW>(args, order, st)
-                                             : launch_chunk<64, KDA_GATE_LOG>(args, order, st);
+        rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk<64, KDA_GATE_RAW>(args, order, st, skip_hi)
+                                             : launch_chunk<64, KDA_GATE_LOG>(args, order, st, skip_hi);
     if (rc != KDA_OK) return rc;
     return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
 }

@@ -111,6 +111,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int32_t
     return false;
 }
 
+// Host side (kda_recurrent.cu): the recurrence over the requests whose length
+// lies in [len_lo, len_hi]; the other requests are neither read nor written.
+int recurrent_launch_range(const KdaArgs *args, int32_t len_lo, int32_t len_hi, cudaStream_t st);
+
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // Both addresses 16-byte aligned, bytes a multiple of 16. No multicast.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

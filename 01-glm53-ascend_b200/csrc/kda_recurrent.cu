@@ -159,22 +159,35 @@ __device__ __forceinline__ bool decode_item(const KdaArgs &p, int64_t it, int ns
 // write-back (kda_python.py:271-307).
 // `cur` holds the item's first token when `staged` (read from a ring stage by
 // the caller); otherwise it is loaded here.
+// The raw gate's per-head parameters a lane needs: A_log[h] and the four
+// dt_bias entries of its own key group (group (lane / 8) % (D / 32), keys
+// group * 32 + sub * 4 .. + 3), loaded ahead of use by the caller.
+struct RawGateParams {
+    float4 dtb;
+    float a_log;
+};
+template <int D>
+__device__ __forceinline__ RawGateParams load_raw_params(const KdaArgs &p, int h, int sub) {
+    const int grp = ((threadIdx.x & 31) >> 3) % (D / 32);
+    return RawGateParams{load_f32x4(p.dt_bias, h * D + grp * 32 + sub * 4), __ldg(p.A_log + h)};
+}
+
 template <int D, int MODE, bool FAST>
 __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float (&s)[2][D / 8], int row0, int sub,
-                                         TokenRaw<D, MODE> &cur, bool staged) {
+                                         TokenRaw<D, MODE> &cur, bool staged, const RawGateParams &rp) {
     constexpr int NC = D / 32;
     constexpr int NE = D / 8;
     const int h = m.h, v0 = m.v0;
     const int64_t sk = p.state_stride[2], sv = p.state_stride[3];
     const int64_t row_off = FAST ? static_cast<int64_t>(v0) * D : v0 * sv;
 
-    float dtb[NE];
+    // Raw gate: the decay of a key depends on (token, head, key) only, so the
+    // four 8-lane row groups of a warp split the key groups between them
+    // (group (lane / 8) % NC), compute their decays once and share them by
+    // shuffles, instead of each lane evaluating all of its D / 8 keys.
+    const int grp = ((threadIdx.x & 31) >> 3) % NC;
     float expA = 0.f;
-    if constexpr (MODE == KDA_GATE_RAW) {
-        expA = expf(__ldg(p.A_log + h));
-#pragma unroll
-        for (int c = 0; c < NC; ++c) unpack4<D>(dtb + c * 4, load_f32x4(p.dt_bias, h * D + c * 32 + sub * 4));
-    }
+    if constexpr (MODE == KDA_GATE_RAW) expA = expf(rp.a_log);
 
     float *const track_state =
         (m.tslot > 0) ? p.state + m.tslot * p.state_stride[0] + h * p.state_stride[1] + row_off : nullptr;
@@ -240,16 +253,22 @@ __device__ __forceinline__ void run_item(const KdaArgs &p, const Item &m, float 
                 }
                 beta = cur.beta;
             } else {
+                uint2 ab = cur.ab[0];
 #pragma unroll
-                for (int c = 0; c < NC; ++c) {
-                    float a4[4];
-                    unpack_bf4(a4, cur.ab[c]);
+                for (int c = 1; c < NC; ++c)
+                    if (grp == c) ab = cur.ab[c];
+                float a4[4], mine[4];
+                unpack_bf4(a4, ab);
+                const float dtb[4] = {rp.dtb.x, rp.dtb.y, rp.dtb.z, rp.dtb.w};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float gate = expA * (a4[e] + dtb[c * 4 + e]);
-                        dec[c * 4 + e] = expf(p.lower_bound * sigmoidf_(gate));
-                    }
+                for (int e = 0; e < 4; ++e) {
+                    const float gate = expA * (a4[e] + dtb[e]);
+                    mine[e] = expf(p.lower_bound * sigmoidf_(gate));
                 }
+#pragma unroll
+                for (int c = 0; c < NC; ++c)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) dec[c * 4 + e] = __shfl_sync(0xffffffffu, mine[e], c * 8 + sub);
                 beta = sigmoidf_(__uint_as_float(static_cast<uint32_t>(cur.bb) << 16));
             }
         }
@@ -380,7 +399,8 @@ __device__ __forceinline__ void token_from_stage(TokenRaw<D, MODE> &r, const Kda
 // have read it.
 template <int D, int MODE, int STAGES, int MINB>
 __global__ void __launch_bounds__(kRecThreads + 32, MINB)
-recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bulk) {
+recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bulk, int32_t len_lo,
+                      int32_t len_hi) {
     using RS = RingStage<D, MODE>;
     constexpr int NC = D / 32;
     constexpr uint32_t kTileBytes = kBV * D * sizeof(float);
@@ -438,6 +458,9 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
                     tlen = load_index(p.track_lens, p.index_bytes[3], req);
                 }
             }
+            // A request outside [len_lo, len_hi] belongs to another kernel of
+            // the same launch: nothing is read or written for it here.
+            if (ok && (eos - bos < len_lo || eos - bos > len_hi)) ok = 0;
             // beta (raw b) of the first token into the header by a 4-byte
             // cp.async that the stage's barrier also waits for (its tracking
             // arrive precedes the expect-tx arrive, so the phase cannot
@@ -507,7 +530,17 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
     // ===== compute warps =====
     int st = 0;
     uint32_t phase = 0;
+    // Raw gate: the next item's A_log and dt_bias are loaded one item ahead
+    // (an item's head follows from its index), off the item's critical path.
+    auto head_of = [&](int64_t it) { return p.head_begin + static_cast<int>((it / nslice) % p.head_count); };
+    RawGateParams rp{}, rp_next{};
+    if constexpr (MODE == KDA_GATE_RAW) {
+        if (first < num_items) rp = load_raw_params<D>(p, head_of(first), sub);
+    }
     for (int64_t it = first; it < num_items; it += stride) {
+        if constexpr (MODE == KDA_GATE_RAW) {
+            if (it + stride < num_items) rp_next = load_raw_params<D>(p, head_of(it + stride), sub);
+        }
         if (!mbar_wait(&full[st], phase, p.status)) return;
         const unsigned char *stage = ring + st * RS::kBytes;
         const StageMeta sm = *meta_of(st);
@@ -542,7 +575,8 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
         // This warp is done with the stage.
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
-        if (ok) run_item<D, MODE, true>(p, m, s, row0, sub, cur, staged);
+        if (ok) run_item<D, MODE, true>(p, m, s, row0, sub, cur, staged, rp);
+        rp = rp_next;
         if (++st == STAGES) {
             st = 0;
             phase ^= 1u;
@@ -554,7 +588,7 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
 // pool (used by prepared_recurrent on a [K,V]-contiguous state).
 template <int D, int MODE>
 __global__ void __launch_bounds__(kRecThreads, 3)
-recurrent_strided_kernel(const KdaArgs p, int nslice) {
+recurrent_strided_kernel(const KdaArgs p, int nslice, int32_t len_lo, int32_t len_hi) {
     constexpr int NE = D / 8;
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -562,6 +596,7 @@ recurrent_strided_kernel(const KdaArgs p, int nslice) {
     const int row0 = warp * kRowsPerWarp + rq;
     Item m;
     if (!decode_item(p, blockIdx.x, nslice, m)) return;
+    if (m.eos - m.bos < len_lo || m.eos - m.bos > len_hi) return;   // another kernel's request
     const int64_t sk = p.state_stride[2], sv = p.state_stride[3];
     float s[2][NE];
     if (m.slot > 0) {
@@ -580,7 +615,9 @@ recurrent_strided_kernel(const KdaArgs p, int nslice) {
             for (int e = 0; e < NE; ++e) s[j][e] = 0.f;
     }
     TokenRaw<D, MODE> cur;
-    run_item<D, MODE, false>(p, m, s, row0, sub, cur, false);
+    RawGateParams rp{};
+    if constexpr (MODE == KDA_GATE_RAW) rp = load_raw_params<D>(p, m.h, sub);
+    run_item<D, MODE, false>(p, m, s, row0, sub, cur, false, rp);
 }
 
 // ---------------------------------------------------------------------------
@@ -670,7 +707,7 @@ static int sm_count() {
 }
 
 template <int D, int MODE>
-static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st) {
+static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st, int32_t len_lo, int32_t len_hi) {
     const int nslice = D / kBV;
     const int64_t items = static_cast<int64_t>(a->num_req) * a->head_count * nslice;
     if (fast) {
@@ -696,19 +733,36 @@ static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st) {
         const void *gate = MODE == KDA_GATE_RAW ? static_cast<const void *>(a->a) : static_cast<const void *>(a->g);
         const int tok_bulk = aligned16(a->q) && aligned16(a->k) && aligned16(gate) && aligned16(a->v) ? 1 : 0;
         recurrent_ring_kernel<D, MODE, RingShape<MODE>::kStages, RingShape<MODE>::kMinBlocks>
-            <<<static_cast<unsigned>(grid), kRecThreads + 32, smem, st>>>(*a, nslice, items, tok_bulk);
+            <<<static_cast<unsigned>(grid), kRecThreads + 32, smem, st>>>(*a, nslice, items, tok_bulk, len_lo, len_hi);
     } else {
-        recurrent_strided_kernel<D, MODE><<<static_cast<unsigned>(items), kRecThreads, 0, st>>>(*a, nslice);
+        recurrent_strided_kernel<D, MODE>
+            <<<static_cast<unsigned>(items), kRecThreads, 0, st>>>(*a, nslice, len_lo, len_hi);
     }
 }
 
 template <int D>
-static void dispatch_mode(const KdaArgs *a, bool fast, cudaStream_t st) {
+static void dispatch_mode(const KdaArgs *a, bool fast, cudaStream_t st, int32_t len_lo = 0,
+                          int32_t len_hi = INT32_MAX) {
     switch (a->gate_mode) {
-        case KDA_GATE_RAW: launch_rec<D, KDA_GATE_RAW>(a, fast, st); break;
-        case KDA_GATE_LOG: launch_rec<D, KDA_GATE_LOG>(a, fast, st); break;
-        default: launch_rec<D, KDA_GATE_PREPARED>(a, fast, st); break;
+        case KDA_GATE_RAW: launch_rec<D, KDA_GATE_RAW>(a, fast, st, len_lo, len_hi); break;
+        case KDA_GATE_LOG: launch_rec<D, KDA_GATE_LOG>(a, fast, st, len_lo, len_hi); break;
+        default: launch_rec<D, KDA_GATE_PREPARED>(a, fast, st, len_lo, len_hi); break;
     }
+}
+
+// The recurrence over the requests of length len_lo..len_hi only (the others
+// are left untouched): the chunk prefill hands its shortest requests to this
+// kernel, where a token costs a step rather than a 64-row chunk.
+int recurrent_launch_range(const KdaArgs *args, int32_t len_lo, int32_t len_hi, cudaStream_t st) {
+    const int rc = validate_common(args);
+    if (rc != KDA_OK) return rc;
+    if (args->num_req == 0 || args->head_count == 0) return KDA_OK;
+    const bool fast = state_fast(args) && mid_fast(args);
+    if (args->head_dim == 128)
+        dispatch_mode<128>(args, fast, st, len_lo, len_hi);
+    else
+        dispatch_mode<64>(args, fast, st, len_lo, len_hi);
+    return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
 }
 
 }  // namespace kda

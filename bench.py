@@ -139,6 +139,31 @@ class Dist:
             self.pg.destroy_process_group()
 
 
+def bind_local_cpus(device: int):
+    """Pins this process to the CPUs NVML reports as local to `device` (its
+    NUMA node), as a serving process is pinned, so the pinned host buffers of
+    the end-to-end line are allocated and first touched on the GPU's own node.
+    Returns (previous CPU set, local CPU list), or None when NVML cannot say."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+        try:
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            h = pynvml.nvmlDeviceGetHandleByIndex(device)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, 16)
+        local = [64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1]
+        prev = os.sched_getaffinity(0)
+        local = sorted(set(local) & prev)
+        if not local:
+            return None
+        os.sched_setaffinity(0, local)
+        return prev, local
+    except Exception:
+        return None
+
+
 # ---------------------------------------------------------------------------
 # Clock sampling (NVML) during the timed region
 # ---------------------------------------------------------------------------
@@ -231,6 +256,9 @@ def time_flushed(fn, iters: int, warmup: int, dist: Dist):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
     for a, b in ev:
         _FLUSH.fill_(1)
+        # Keep the GPU busy while the host enqueues the call, so the interval
+        # holds device time only (no host launch latency).
+        torch.cuda._sleep(200_000)
         a.record(s)
         fn()
         b.record(s)
@@ -739,7 +767,7 @@ def cpu_prefill_rate(tokens: int, budget_s: float, seed: int = 8):
     from oracle import kda_ref
     import kda_workloads as workloads
 
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     torch.set_num_threads(threads)
     w = workloads.config3(seed=seed, lengths=[tokens])
     reps, t0 = 0, time.perf_counter()
@@ -762,7 +790,7 @@ def cpu_decode_rate(requests: int, budget_s: float, seed: int = 7):
     from oracle import kda_ref
     import kda_workloads as workloads
 
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     torch.set_num_threads(threads)
     w = workloads.config2(seed=seed, requests=requests, slots=requests + 1)
     reps, t0 = 0, time.perf_counter()
@@ -789,7 +817,7 @@ def run_reference(args, dist: Dist):
     from oracle import kda_ref
     import kda_workloads as workloads
 
-    threads = os.cpu_count() or 1
+    threads = len(os.sched_getaffinity(0)) or 1
     torch.set_num_threads(threads)
     w = workloads.config2(seed=1000)
     kw = w.kwargs()
@@ -853,6 +881,7 @@ def main():
         return
 
     dist.init_gpu()
+    bound = bind_local_cpus(dist.local)
     hbm_gbs, bf16_tf, bf16_tf_sus, peak_kind = _peaks()
     args.peaks = (hbm_gbs, bf16_tf)
     if args.mode == "prefill-kernel":
@@ -899,6 +928,8 @@ def main():
 
     cpu = None
     if dist.rank == 0 and dist.world == 1:
+        if bound is not None:
+            os.sched_setaffinity(0, bound[0])   # the CPU baseline gets every core again
         rate, threads, sample = cpu_decode_rate(32, args.cpu_budget)
         cpu = {"value": round(rate, 2), "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
         if "prefill" in extra:
@@ -929,6 +960,8 @@ def main():
             "e2e": dec["e2e"],
             "gpu_launches": dec["gpu_launches"],
             "clocks": dec["clocks"],
+            "host_cpus": ({"bound_to_gpu_local": len(bound[1]), "of": len(bound[0])} if bound is not None
+                          else "unbound (NVML gave no CPU affinity)"),
             **extra,
         }
         print(json.dumps(line), flush=True)

@@ -139,6 +139,31 @@ def test_ragged_lengths_match_oracle(ops, chunk_path, cu_seqlens, slots, track, 
     _check(ops, kw, touched, chunk_path)
 
 
+# The op's own choice hands requests of 1..16 tokens to the token recurrence
+# and the rest to the chunk kernel, in one call: lengths on both sides of the
+# boundary, an empty request, the padding slot and prefix checkpoints in short
+# requests (at 0, inside, at the end) and in a long one.
+ROUTED = [
+    ([0, 1, 17, 33, 49, 129], [1, 2, 3, 4, 5], None),
+    ([0, 16, 16, 31, 32, 200], [1, 0, 2, 3, 4], ([6, 0, 7, 0, 5], [0, 0, 15, 0, 100])),
+    ([0, 3, 7, 23, 87, 91], [2, 1, 3, 4, 5], ([6, 7, 0, 0, 0], [3, 2, 0, 0, 0])),
+]
+
+
+@pytest.mark.parametrize("cu_seqlens,slots,track", ROUTED, ids=lambda x: str(x))
+@pytest.mark.parametrize("D", (64, 128))
+def test_short_requests_routed_to_recurrence(ops, cu_seqlens, slots, track, D):
+    kw = _case(4, cu_seqlens, slots, track, seed=sum(cu_seqlens) + D, D=D)
+    touched = {s for s in slots if s > 0} | ({s for s in track[0] if s > 0} if track else set())
+    _check(ops, kw, touched, "auto")
+    # the forced fused kernel (every request through the chunk kernel) agrees
+    a, b = _dev(kw), _dev(kw)
+    oa = _run(ops, a, "auto")
+    ob = chunk_via_abi(b, KDA_CHUNK_FUSED)
+    assert_out_close(oa.cpu(), ob.cpu())
+    assert_state_close(a["initial_state_source"].cpu(), b["initial_state_source"].cpu())
+
+
 @pytest.mark.parametrize("name", ["chunk_raw_tracked", "chunktest_ragged_varlen", "chunktest_zero_slot",
                                   "chunktest_track_at_0", "chunktest_track_mid_chunk", "chunktest_track_at_end"])
 def test_chunk_matches_reference_golden(ops, chunk_path, name):
