@@ -922,6 +922,11 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             tmem_st_wait();
         }
         if (nchunks > 0) load_beta(cprep);
+        // TB's and Aqk's strictly-upper 16x16 blocks are never computed but are
+        // read by the full-width products: zero both tiles once (the chunks
+        // rewrite only their lower blocks).
+        for (int e = tid; e < 4 * BT * BT / 8; e += kThreads)
+            reinterpret_cast<uint4 *>(TBh)[e] = make_uint4(0u, 0u, 0u, 0u);   // TBh, TBl, AQh, AQl are contiguous
 
         bool o_pending = false;   // the previous chunk's o^T waits in tensor memory
         bool ox_busy = false;     // thread 0: an o tile store still reads the W region
@@ -1183,8 +1188,17 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                         col[i] = (i == j) ? 1.f : (i > j ? -(s0a + s1a) : 0.f);
                     }
                     if (lane < 16) {
+                        // T_II (fp32, for the off-diagonal blocks) and TB_II = T_II diag(beta)
+                        // as bf16 hi/lo, the operand of u = TB v and W.
+                        const float bj = vec[L::vBeta + 16 * I + j];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
+                        for (int i = 0; i < 16; ++i) {
+                            Tm[(16 * I + i) * AS + 16 * I + j] = col[i];
+                            uint16_t hi, lo;
+                            split1(col[i] * bj, hi, lo);
+                            TBh[swz<BT>(16 * I + i, 16 * I + j)] = hi;
+                            TBl[swz<BT>(16 * I + i, 16 * I + j)] = lo;
+                        }
                     }
                 }
             } else if (o_pending) {
@@ -1253,6 +1267,21 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                         *reinterpret_cast<float2 *>(t + 8 * ld) = make_float2(sgn * acc[nt][2], sgn * acc[nt][3]);
                     }
                 };
+                // -acc as block (r0, c0) of T, and of TB = T diag(beta) as bf16 hi/lo.
+                auto put_t = [&](int r0, int c0, const float (&acc)[2][4]) {
+                    put(Tm + r0 * AS + c0, AS, acc, -1.f);
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {
+                            const int i = r0 + g + 8 * hf, j0 = c0 + 8 * nt + 2 * t4;
+                            uint32_t hi, lo;
+                            split2(-acc[nt][2 * hf] * vec[L::vBeta + j0], -acc[nt][2 * hf + 1] * vec[L::vBeta + j0 + 1],
+                                   hi, lo);
+                            *reinterpret_cast<uint32_t *>(TBh + swz<BT>(i, j0)) = hi;
+                            *reinterpret_cast<uint32_t *>(TBl + swz<BT>(i, j0)) = lo;
+                        }
+                };
                 float *const Pw = Pp + warp * 16 * L::PS;
                 if (warp < 2) {
                     // T_IJ = -T_II (A'_IJ T_JJ), (I, J) = (1, 0) or (3, 2)
@@ -1263,7 +1292,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     __syncwarp();
                     float tacc[2][4] = {};
                     blk(tacc, Tm, AS, 16 * I, 16 * I, Pw, L::PS, 0, 0);
-                    put(Tm + 16 * I * AS + 16 * J, AS, tacc, -1.f);
+                    put_t(16 * I, 16 * J, tacc);
                 }
                 nbar(2, 128);
                 {
@@ -1279,7 +1308,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                     float tacc[2][4] = {};
                     blk(tacc, Tm, AS, 16 * r, 32, Pp + cc * 16 * L::PS, L::PS, 0, 0);
                     if (r == 3) blk(tacc, Tm, AS, 48, 48, Pp + (2 + cc) * 16 * L::PS, L::PS, 0, 0);
-                    put(Tm + 16 * r * AS + 16 * cc, AS, tacc, -1.f);
+                    put_t(16 * r, 16 * cc, tacc);
                 }
             } else if (!PREP && warp >= 8) {
                 // S^T -> bf16 hi/lo A operand and S^T <- S^T e^{gl} (deferred on a
@@ -1291,66 +1320,39 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 }
                 const int cb = ((warp >> 2) & 1) * (D / 2);
 #pragma unroll
-                for (int c32 = 0; c32 < D / 64; ++c32) {
-                    const int col = cb + 32 * c32;
-                    uint32_t r[32], hi[16], lo[16];
-                    tmem_ld32(tq + kColS + col, r);
+                for (int c16 = 0; c16 < D / 32; ++c16) {
+                    const int col = cb + 16 * c16;
+                    uint32_t r[16], hi[8], lo[8];
+                    tmem_ld16(tq + kColS + col, r);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e)
+                    for (int e = 0; e < 8; ++e)
                         split2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), hi[e], lo[e]);
-                    tmem_st16(tq + kColSH + col / 2, hi);
-                    tmem_st16(tq + kColSL + col / 2, lo);
+                    tmem_st8(tq + kColSH + col / 2, hi);
+                    tmem_st8(tq + kColSL + col / 2, lo);
                     if (!track_here) {
                         const float4 *eg = reinterpret_cast<const float4 *>(vec + L::vEgl + col);
 #pragma unroll
-                        for (int e4 = 0; e4 < 8; ++e4) {
+                        for (int e4 = 0; e4 < 4; ++e4) {
                             const float4 f = eg[e4];
                             r[4 * e4] = __float_as_uint(__uint_as_float(r[4 * e4]) * f.x);
                             r[4 * e4 + 1] = __float_as_uint(__uint_as_float(r[4 * e4 + 1]) * f.y);
                             r[4 * e4 + 2] = __float_as_uint(__uint_as_float(r[4 * e4 + 2]) * f.z);
                             r[4 * e4 + 3] = __float_as_uint(__uint_as_float(r[4 * e4 + 3]) * f.w);
                         }
-                        tmem_st32(tq + kColS + col, r);
+                        tmem_st16(tq + kColS + col, r);
                     }
                 }
                 tmem_st_wait();
                 tc_fence_before();
             }
+            // TB came with the T blocks (P3's diagonal solves, P4's stages).
+            fence_async_smem();   // TB tiles written by threads -> read by the tensor core
             cbar();
-            if (!PREP && tid == 0) mbar_arrive(sig_a);   // A' is dead: the next q tile may land
-
-            // ---- P5: TB = T diag(beta) hi/lo; Aqk's upper blocks zeroed ----
-            // One 8-column chunk of one row per thread.
-            {
-                const int j = tid >> 3, c8 = (tid & 7) * 8;
-                uint4 hv = make_uint4(0u, 0u, 0u, 0u), lv = make_uint4(0u, 0u, 0u, 0u);
-                if (c8 <= j) {
-                    const float4 t0v = *reinterpret_cast<const float4 *>(Tm + j * AS + c8);
-                    const float4 t1v = *reinterpret_cast<const float4 *>(Tm + j * AS + c8 + 4);
-                    const float4 b0v = *reinterpret_cast<const float4 *>(vec + L::vBeta + c8);
-                    const float4 b1v = *reinterpret_cast<const float4 *>(vec + L::vBeta + c8 + 4);
-                    const float x[8] = {t0v.x * b0v.x, t0v.y * b0v.y, t0v.z * b0v.z, t0v.w * b0v.w,
-                                        t1v.x * b1v.x, t1v.y * b1v.y, t1v.z * b1v.z, t1v.w * b1v.w};
-                    uint32_t hw[4], lw[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        split2(c8 + 2 * e <= j ? x[2 * e] : 0.f, c8 + 2 * e + 1 <= j ? x[2 * e + 1] : 0.f, hw[e], lw[e]);
-                    hv = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                    lv = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-                }
-                *reinterpret_cast<uint4 *>(TBh + swz<BT>(j, c8)) = hv;
-                *reinterpret_cast<uint4 *>(TBl + swz<BT>(j, c8)) = lv;
-                // Aqk's strictly-upper 16x16 blocks are never computed but are read
-                // by the full-width tensor-core product: make them zero.
-                if ((c8 >> 4) > (j >> 4)) {
-                    *reinterpret_cast<uint4 *>(AQh + swz<BT>(j, c8)) = make_uint4(0u, 0u, 0u, 0u);
-                    *reinterpret_cast<uint4 *>(AQl + swz<BT>(j, c8)) = make_uint4(0u, 0u, 0u, 0u);
-                }
+            if (!PREP && tid == 0) {
+                mbar_arrive(sig_a);    // A' is dead: the next q tile may land
+                mbar_arrive(&sig[0]);  // u = TB v may start
             }
-            fence_async_smem();   // tiles written by threads -> read by the tensor core
-            cbar();
-            if (!PREP && tid == 0) mbar_arrive(&sig[0]);   // u = TB v may start
             if (has_next) load_beta(c + 1);
 
             // ---- P7 (warps 0..D/16-1): W = TB (kn e^{gc}), 16 key columns per warp ----

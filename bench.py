@@ -68,8 +68,10 @@ DECODE_BYTES_PER_TOKEN_HEAD = 65536 * 2 + 768 + 512 + 4 + 256
 # heads processed.
 DECODE_TRAFFIC_PER_LAUNCH = 1025897216
 PREFILL_TRAFFIC_PER_LAUNCH = 1651127296
-# configs[3] (4 heads), all kernels of one split-path call; None until captured.
-PREFILL_LONG_TRAFFIC_PER_LAUNCH = None
+# configs[3] (4 heads), all six kernels of one split-path call (plan, prep,
+# scan, combine, rescan, outputs): captured at 32,768 tokens (1,318,200,832 B)
+# and scaled by 4, the traffic being proportional to the chunks processed.
+PREFILL_LONG_TRAFFIC_PER_LAUNCH = 5272803328
 
 METRIC = "KDA tokens/s (prefill, decode) H32 d128 @1/2/4/8 B200; decode HBM GB/s vs peak"
 
@@ -343,6 +345,37 @@ def time_e2e(host: dict, run, out_shape, steps: int, warmup: int, dist: Dist):
     return dist.max(start.elapsed_time(end)) / steps, h2d, d2h
 
 
+def h2d_link_gbs(host: dict, reps: int) -> float:
+    """Host->device copy rate of the end-to-end line's own pinned buffers
+    (same two copy streams, nothing else running): the link bound that the
+    end-to-end number is read against."""
+    xss = (torch.cuda.Stream(), torch.cuda.Stream())
+    dev = {n: torch.empty_like(t, device="cuda") for n, t in host.items()}
+    names = sorted(host, key=lambda n: -host[n].numel() * host[n].element_size())
+    groups, load = ([], []), [0, 0]
+    for n in names:
+        g = 0 if load[0] <= load[1] else 1
+        groups[g].append(n)
+        load[g] += host[n].numel() * host[n].element_size()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cs = torch.cuda.current_stream()
+    start.record(cs)
+    for xs in xss:
+        xs.wait_event(start)
+    for _ in range(reps):
+        for k, xs in enumerate(xss):
+            with torch.cuda.stream(xs):
+                for n in groups[k]:
+                    dev[n].copy_(host[n], non_blocking=True)
+    for xs in xss:
+        cs.wait_stream(xs)
+    end.record(cs)
+    torch.cuda.synchronize()
+    nbytes = reps * sum(t.numel() * t.element_size() for t in host.values())
+    return nbytes / (start.elapsed_time(end) / 1e3) / 1e9
+
+
 # ---------------------------------------------------------------------------
 # Decode (headline)
 # ---------------------------------------------------------------------------
@@ -397,8 +430,10 @@ def bench_decode(args, dist: Dist, hbm_gbs: float, peak_kind: str) -> dict:
                                           cu_seqlens=dev["cu"], scale=d.scale, prefill=False)
 
     ems, h2d, d2h = time_e2e(host, run, w.v.shape, args.steps, args.warmup, dist)
+    link = h2d_link_gbs(host, max(args.steps, 20))
     e2e = {"value": round(dist.world * tokens / (ems / 1e3), 1), "unit": "tokens/s",
            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ems, 4),
+           "h2d_link_gbs": round(link, 1), "h2d_frac_of_link": round(h2d / (ems / 1e3) / 1e9 / link, 4),
            "pipelining": "step i+1's inputs copy host->device on two copy streams while step i runs "
                          "(two device input sets); each step's output is read back on a further stream"}
     return dict(value=value, ms_per_step=ms_per_step, roofline=roofline, e2e=e2e, clocks=clocks,
@@ -479,7 +514,7 @@ def bench_prefill_long(args, dist: Dist, steps: int, warmup: int) -> dict:
     from sgl_glm53_ascend_ops import ops
 
     heads = 4
-    w = workloads.config4(seed=3000 + dist.rank, heads=heads)
+    w = workloads.config4(seed=3000 + dist.rank, heads=heads, tokens=getattr(args, "long_tokens", 131072))
     d = w.to("cuda")
     kw = d.kwargs()
     pool0 = d.pool.clone()
@@ -868,6 +903,8 @@ def main():
                     help="kernel / prefill-kernel: only the timed decode / chunk op loop (profiler captures)")
     ap.add_argument("--prefill-heads", type=int, default=32,
                     help="prefill-kernel mode: heads of config 3 (fewer keeps a full ncu capture small)")
+    ap.add_argument("--long-tokens", type=int, default=131072,
+                    help="prefill-long mode: sequence length of config 4 (shorter keeps an ncu capture small)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
