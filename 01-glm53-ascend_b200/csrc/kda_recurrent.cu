@@ -166,10 +166,18 @@ struct RawGateParams {
     float4 dtb;
     float a_log;
 };
+// The loads are volatile asm so the compiler issues them where they are
+// written (one item ahead) instead of sinking them next to their first use.
 template <int D>
 __device__ __forceinline__ RawGateParams load_raw_params(const KdaArgs &p, int h, int sub) {
     const int grp = ((threadIdx.x & 31) >> 3) % (D / 32);
-    return RawGateParams{load_f32x4(p.dt_bias, h * D + grp * 32 + sub * 4), __ldg(p.A_log + h)};
+    RawGateParams r;
+    const float *d = p.dt_bias + h * D + grp * 32 + sub * 4;
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(r.dtb.x), "=f"(r.dtb.y), "=f"(r.dtb.z), "=f"(r.dtb.w)
+                 : "l"(d));
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(r.a_log) : "l"(p.A_log + h));
+    return r;
 }
 
 template <int D, int MODE, bool FAST>
@@ -345,6 +353,7 @@ struct StageMeta {
     int req, h, v0, ok;
     uint32_t bword;   // beta (or the 4-byte word holding the raw b) of the first token
     int bsel;         // 0: not staged (load it); 1: bword / its low half; 2: its high half
+    float a_log;      // raw gate: A_log[h]
 };
 template <int D, int MODE>
 struct RingStage {
@@ -355,7 +364,10 @@ struct RingStage {
     static constexpr int kG = kK + D * QE;
     static constexpr int kV = kG + D * GE;                         // bf16 v slice (kBV values)
     static constexpr int kTokBytes = kV + kBV * 2 - kQ;
-    static constexpr int kMeta = (kV + kBV * 2 + 15) / 16 * 16;
+    // raw gate: the item's head's dt_bias row (D fp32), copied with the tiles
+    static constexpr int kDtb = (kV + kBV * 2 + 15) / 16 * 16;
+    static constexpr int kDtbBytes = MODE == KDA_GATE_RAW ? D * 4 : 0;
+    static constexpr int kMeta = kDtb + kDtbBytes;
     static constexpr int kBytes = (kMeta + static_cast<int>(sizeof(StageMeta)) + 127) / 128 * 128;
 };
 
@@ -490,6 +502,7 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
             hdr->v0 = v0;
             hdr->ok = ok;
             hdr->bsel = bsel;   // bword is written only by the copy below
+            if constexpr (MODE == KDA_GATE_RAW) hdr->a_log = ok ? __ldg(p.A_log + h) : 0.f;
             if (bsrc != nullptr) {
                 asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(&hdr->bword)), "l"(bsrc)
                              : "memory");
@@ -498,9 +511,12 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
             }
             const bool st_in = ok && slot > 0;
             const bool tk_in = ok && tok_bulk && bos < eos;
-            const uint32_t bytes = (st_in ? kTileBytes : 0u) + (tk_in ? static_cast<uint32_t>(RS::kTokBytes) : 0u);
+            const bool dt_in = MODE == KDA_GATE_RAW && ok;
+            const uint32_t bytes = (st_in ? kTileBytes : 0u) + (tk_in ? static_cast<uint32_t>(RS::kTokBytes) : 0u) +
+                                   (dt_in ? static_cast<uint32_t>(RS::kDtbBytes) : 0u);
             if (bytes > 0) {
                 mbar_arrive_expect_tx(&full[st], bytes);
+                if (dt_in) bulk_g2s(stage + RS::kDtb, p.dt_bias + static_cast<int64_t>(h) * D, RS::kDtbBytes, &full[st]);
                 if (st_in)
                     bulk_g2s(stage, p.state + slot * p.state_stride[0] + h * p.state_stride[1] + static_cast<int64_t>(v0) * D,
                              kTileBytes, &full[st]);
@@ -530,17 +546,7 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
     // ===== compute warps =====
     int st = 0;
     uint32_t phase = 0;
-    // Raw gate: the next item's A_log and dt_bias are loaded one item ahead
-    // (an item's head follows from its index), off the item's critical path.
-    auto head_of = [&](int64_t it) { return p.head_begin + static_cast<int>((it / nslice) % p.head_count); };
-    RawGateParams rp{}, rp_next{};
-    if constexpr (MODE == KDA_GATE_RAW) {
-        if (first < num_items) rp = load_raw_params<D>(p, head_of(first), sub);
-    }
     for (int64_t it = first; it < num_items; it += stride) {
-        if constexpr (MODE == KDA_GATE_RAW) {
-            if (it + stride < num_items) rp_next = load_raw_params<D>(p, head_of(it + stride), sub);
-        }
         if (!mbar_wait(&full[st], phase, p.status)) return;
         const unsigned char *stage = ring + st * RS::kBytes;
         const StageMeta sm = *meta_of(st);
@@ -572,11 +578,20 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
         TokenRaw<D, MODE> cur;
         const bool staged = ok && tok_bulk && m.bos < m.eos;
         if (staged) token_from_stage<D, MODE>(cur, p, stage, sm, sub, row0);
+        // Raw gate: the head's A_log (header) and this lane's dt_bias group
+        // (copied into the stage with the tiles).
+        RawGateParams rp{};
+        if constexpr (MODE == KDA_GATE_RAW) {
+            if (ok) {
+                const int grp = rq % (D / 32);
+                rp.dtb = *reinterpret_cast<const float4 *>(stage + RS::kDtb + (grp * 32 + sub * 4) * 4);
+                rp.a_log = sm.a_log;
+            }
+        }
         // This warp is done with the stage.
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
         if (ok) run_item<D, MODE, true>(p, m, s, row0, sub, cur, staged, rp);
-        rp = rp_next;
         if (++st == STAGES) {
             st = 0;
             phase ^= 1u;
