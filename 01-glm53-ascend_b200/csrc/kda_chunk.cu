@@ -43,10 +43,12 @@
 //   * the next chunk's q/k/g (and v) tiles are fetched by TMA (one tensor
 //     map each, the v tile written in the 128-byte swizzle the tensor core
 //     reads) while this chunk runs, each as soon as its shared-memory region
-//     is dead (q after the inverse, k and g after TB, v after u = TB v);
+//     is dead (q, k and g after the inverse, v after u = TB v);
 //     output tiles leave by TMA stores.
 //   * any sequence length: a partial last chunk is zero-filled (k = q = v =
 //     g = beta = 0), which leaves the state and the real rows unchanged.
+//     Requests of 1..16 tokens go to the token recurrence instead (launched
+//     first by kda_chunk_launch), where a token costs one step, not a chunk.
 //   * every mbarrier wait is bounded; tensor memory is freed on every path.
 
 #include "kda_common.cuh"
@@ -299,6 +301,20 @@ __device__ __forceinline__ uint64_t sdesc_noswz(uint32_t saddr, uint32_t lbo, ui
     return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
            (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
+// The descriptor of (s_base + off) from the descriptor of s_base with the same
+// lbo/sbo: the start-address field holds address >> 4 in bits 0-13, and a
+// CTA's shared-memory addresses stay below 2^18 bytes, so adding off >> 4
+// never carries out of it. With `off` a compile-time constant this is one
+// integer add per tensor-core instruction the producer thread issues.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t base, uint32_t off) { return base + (off >> 4); }
+// `x` made opaque where it is computed, so the compiler keeps the producer's
+// descriptor bases inside the producer's loop instead of hoisting them (and
+// every constant offset from them) into registers live across the kernel.
+__device__ __forceinline__ uint64_t opaque64(uint64_t x) {
+    asm volatile("" : "+l"(x));
+    return x;
+}
+
 // Instruction descriptor: fp32 accumulate, bf16 A and B, dense.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn, bool b_neg) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((b_neg ? 1u : 0u) << 14) | ((a_mn ? 1u : 0u) << 15) |
@@ -782,6 +798,7 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
             };
             issue_tiles(0, true);
             for (int c = 0; c < nchunks; ++c) {
+                const uint64_t d16 = opaque64(sdesc(s_base, 16, 1024)), d8k = opaque64(sdesc(s_base, 8192, 1024));
                 const uint32_t ph = static_cast<uint32_t>(c & 1);
                 const int64_t rt = tlen - static_cast<int64_t>(c) * BT;
                 const bool trk = tslot > 0 && rt > 0 && rt <= BT;
@@ -794,9 +811,9 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 // NU = -u^T = -(TB v)^T (needs neither S nor v')
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t a = sdesc(s_base + L::kV + kk * 2048, 8192, 1024);
-                    umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBh + kk * 32, 16, 1024), id_v, kk > 0 ? 1u : 0u);
-                    umma_ss(tmem + kColNU, a, sdesc(s_base + L::kTBl + kk * 32, 16, 1024), id_v, 1u);
+                    const uint64_t a = sdesc_add(d8k, L::kV + kk * 2048);
+                    umma_ss(tmem + kColNU, a, sdesc_add(d16, L::kTBh + kk * 32), id_v, kk > 0 ? 1u : 0u);
+                    umma_ss(tmem + kColNU, a, sdesc_add(d16, L::kTBl + kk * 32), id_v, 1u);
                 }
                 umma_commit(&bars[4]);
                 if (nxt && !trk) {
@@ -810,8 +827,8 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 for (int kk = 0; kk < KS; ++kk) {
                     const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
                     const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
-                    const uint64_t wh = sdesc(s_base + L::kX + off, 16, 1024);
-                    const uint64_t wl = sdesc(s_base + L::kX + BT * D * 2 + off, 16, 1024);
+                    const uint64_t wh = sdesc_add(d16, L::kX + off);
+                    const uint64_t wl = sdesc_add(d16, L::kX + BT * D * 2 + off);
                     umma_ts(tmem + kColNU, al, wh, id_n64, 1u);
                     umma_ts(tmem + kColNU, ah, wl, id_n64, 1u);
                     umma_ts(tmem + kColNU, ah, wh, id_n64, 1u);
@@ -823,8 +840,8 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
                 for (int kk = 0; kk < KS; ++kk) {
                     const uint32_t ah = tmem + kColSH + 8 * kk, al = tmem + kColSL + 8 * kk;
                     const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
-                    const uint64_t qh = sdesc(s_base + L::kY + off, 16, 1024);
-                    const uint64_t ql = sdesc(s_base + L::kY + BT * D * 2 + off, 16, 1024);
+                    const uint64_t qh = sdesc_add(d16, L::kY + off);
+                    const uint64_t ql = sdesc_add(d16, L::kY + BT * D * 2 + off);
                     umma_ts(tmem + kColO, al, qh, id_n64, kk > 0 ? 1u : 0u);
                     umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
                     umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
@@ -836,14 +853,14 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
-                    const uint64_t dh = sdesc(s_base + L::kZ + kk * 2048, 8192, 1024);
-                    const uint64_t dl = sdesc(s_base + L::kZ + BT * D * 2 + kk * 2048, 8192, 1024);
+                    const uint64_t dh = sdesc_add(d8k, L::kZ + kk * 2048);
+                    const uint64_t dl = sdesc_add(d8k, L::kZ + BT * D * 2 + kk * 2048);
                     umma_ts(tmem + kColS, al, dh, id_kd, 1u);
                     umma_ts(tmem + kColS, ah, dl, id_kd, 1u);
                     umma_ts(tmem + kColS, ah, dh, id_kd, 1u);
                     if (trk) {
-                        const uint64_t rh = sdesc(s_base + L::kRawQ + kk * 2048, 8192, 1024);
-                        const uint64_t rl = sdesc(s_base + L::kRawK + kk * 2048, 8192, 1024);
+                        const uint64_t rh = sdesc_add(d8k, L::kRawQ + kk * 2048);
+                        const uint64_t rl = sdesc_add(d8k, L::kRawK + kk * 2048);
                         umma_ts(tmem + kColTR, al, rh, id_kd, 1u);
                         umma_ts(tmem + kColTR, ah, rl, id_kd, 1u);
                         umma_ts(tmem + kColTR, ah, rh, id_kd, 1u);
@@ -853,8 +870,8 @@ __global__ void __launch_bounds__(kThreads + 32, 1)
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint32_t ah = tmem + kColVH + 8 * kk, al = tmem + kColVL + 8 * kk;
-                    const uint64_t qh = sdesc(s_base + L::kAQh + kk * 32, 16, 1024);
-                    const uint64_t ql = sdesc(s_base + L::kAQl + kk * 32, 16, 1024);
+                    const uint64_t qh = sdesc_add(d16, L::kAQh + kk * 32);
+                    const uint64_t ql = sdesc_add(d16, L::kAQl + kk * 32);
                     umma_ts(tmem + kColO, al, qh, id_n64, 1u);
                     umma_ts(tmem + kColO, ah, ql, id_n64, 1u);
                     umma_ts(tmem + kColO, ah, qh, id_n64, 1u);
@@ -2326,8 +2343,8 @@ __global__ void __launch_bounds__(256) chunk_combine_tc_kernel(const KdaArgs p, 
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
                 const uint32_t ah = tmem + M::cSH + 8 * kk, al = tmem + M::cSL + 8 * kk;
-                const uint64_t xh = sdesc(s_base + M::kXh + kk * 2048, D * 128, 1024);
-                const uint64_t xl = sdesc(s_base + M::kXl + kk * 2048, D * 128, 1024);
+                const uint64_t xh = sdesc_add(sdesc(s_base, D * 128, 1024), M::kXh + kk * 2048);
+                const uint64_t xl = sdesc_add(sdesc(s_base, D * 128, 1024), M::kXl + kk * 2048);
                 umma_ts(tmem + M::cS, al, xh, id, 1u);
                 umma_ts(tmem + M::cS, ah, xl, id, 1u);
                 umma_ts(tmem + M::cS, ah, xh, id, 1u);
@@ -2638,8 +2655,8 @@ __global__ void __launch_bounds__(256) chunk_out_tc_kernel(const KdaArgs p, cons
             const uint64_t ah = sdesc_noswz(s_base + M::kS + SO::kSH + kk * 4096, 2048, 128);
             const uint64_t al = sdesc_noswz(s_base + M::kS + SO::kSL + kk * 4096, 2048, 128);
             const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
-            const uint64_t wh = sdesc(s_base + M::kW + off, 16, 1024);
-            const uint64_t wl = sdesc(s_base + M::kW + BT * D * 2 + off, 16, 1024);
+            const uint64_t wh = sdesc_add(sdesc(s_base, 16, 1024), M::kW + off);
+            const uint64_t wl = sdesc_add(sdesc(s_base, 16, 1024), M::kW + BT * D * 2 + off);
             umma_ss(tmem + M::cNU, al, wh, id_n64, 1u);
             umma_ss(tmem + M::cNU, ah, wl, id_n64, 1u);
             umma_ss(tmem + M::cNU, ah, wh, id_n64, 1u);
@@ -2650,8 +2667,8 @@ __global__ void __launch_bounds__(256) chunk_out_tc_kernel(const KdaArgs p, cons
             const uint64_t ah = sdesc_noswz(s_base + M::kS + SO::kSH + kk * 4096, 2048, 128);
             const uint64_t al = sdesc_noswz(s_base + M::kS + SO::kSL + kk * 4096, 2048, 128);
             const uint32_t off = (kk >> 2) * 8192 + (kk & 3) * 32;
-            const uint64_t qh = sdesc(s_base + M::kQG + off, 16, 1024);
-            const uint64_t ql = sdesc(s_base + M::kQG + BT * D * 2 + off, 16, 1024);
+            const uint64_t qh = sdesc_add(sdesc(s_base, 16, 1024), M::kQG + off);
+            const uint64_t ql = sdesc_add(sdesc(s_base, 16, 1024), M::kQG + BT * D * 2 + off);
             umma_ss(tmem + M::cO, al, qh, id_n64, kk > 0 ? 1u : 0u);
             umma_ss(tmem + M::cO, ah, ql, id_n64, 1u);
             umma_ss(tmem + M::cO, ah, qh, id_n64, 1u);
@@ -2679,8 +2696,8 @@ __global__ void __launch_bounds__(256) chunk_out_tc_kernel(const KdaArgs p, cons
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             const uint32_t ah = tmem + M::cVH + 8 * kk, al = tmem + M::cVL + 8 * kk;
-            const uint64_t qh = sdesc(s_base + M::kAQ + kk * 32, 16, 1024);
-            const uint64_t ql = sdesc(s_base + M::kAQ + BT * BT * 2 + kk * 32, 16, 1024);
+            const uint64_t qh = sdesc_add(sdesc(s_base, 16, 1024), M::kAQ + kk * 32);
+            const uint64_t ql = sdesc_add(sdesc(s_base, 16, 1024), M::kAQ + BT * BT * 2 + kk * 32);
             umma_ts(tmem + M::cO, al, qh, id_n64, 1u);
             umma_ts(tmem + M::cO, ah, ql, id_n64, 1u);
             umma_ts(tmem + M::cO, ah, qh, id_n64, 1u);

@@ -152,7 +152,9 @@ size_t kda_chunk_workspace_bytes(int32_t num_req, int32_t num_tokens, int32_t nu
  * side and then chained, and an output kernel over all (chunk, head) pairs.
  * The choice depends only on the call's sizes and the device's SM count; the
  * split path runs only when the workspace holds it (256-byte aligned), else
- * the fused kernel. */
+ * the fused kernel. On the fused path, requests of 1..16 tokens (decode or
+ * verify requests in a mixed batch) are computed in the same call by the
+ * token recurrence of kda_recurrent_launch, launched first on the stream. */
 int kda_chunk_launch(const KdaArgs *args, void *workspace, size_t workspace_bytes, void *stream);
 
 /* Which internal path a chunk launch takes (kda_chunk_launch_path). */
