@@ -121,7 +121,47 @@ __device__ __forceinline__ void store_rows(float *base, int64_t sk, int64_t sv, 
 struct Item {
     int req, h, v0;
     int64_t bos, eos, slot, tslot, tlen;
+    bool rejected;   // valid token range, but a slot failed its bounds check
 };
+
+// The op returns its output uninitialised (empty_like) instead of zeroing it
+// first (the reference's zeros_like, kda_varlen_recurrent.cpp:142), so with
+// `zero_fill` the kernel itself writes zeros where no value is computed: the
+// tokens no request covers ([0, cu_seqlens[0]) and [cu_seqlens[num_req], T))
+// of the heads processed, and the rows of a request rejected by the bounds
+// checks. Threads `gtid` of `gthreads` share the uncovered rows, after their
+// items; c0 and cn are cu_seqlens[0] and cu_seqlens[num_req].
+template <int D>
+__device__ void zero_uncovered(const KdaArgs &p, int64_t c0, int64_t cn, int64_t gtid, int64_t gthreads) {
+    if (c0 < 0 || cn > p.num_tokens || c0 > cn) return;   // reported by the items
+    const int64_t elems = (c0 + p.num_tokens - cn) * p.head_count * D;
+    for (int64_t i = gtid; i < elems; i += gthreads) {
+        const int64_t row = i / D, col = i % D;
+        const int64_t tr = row / p.head_count;
+        const int h = p.head_begin + static_cast<int>(row % p.head_count);
+        const int64_t t = tr < c0 ? tr : cn + (tr - c0);
+        const int64_t oi = (t * p.num_heads + h) * D + col;
+        if (p.out_fp32)
+            static_cast<float *>(p.out)[oi] = 0.f;
+        else
+            static_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(0.f);
+    }
+}
+// The output rows of one rejected item (its value slice, every token).
+__device__ __forceinline__ void zero_item_rows(const KdaArgs &p, int h, int v0, int64_t bos, int64_t eos, int row0,
+                                               int sub, int D) {
+    if (sub != 0) return;
+    for (int64_t t = bos; t < eos; ++t) {
+        const int64_t oi = (t * p.num_heads + h) * D + v0 + row0;
+        if (p.out_fp32) {
+            static_cast<float *>(p.out)[oi] = 0.f;
+            static_cast<float *>(p.out)[oi + 4] = 0.f;
+        } else {
+            static_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(0.f);
+            static_cast<__nv_bfloat16 *>(p.out)[oi + 4] = __float2bfloat16_rn(0.f);
+        }
+    }
+}
 
 // Decodes item `it` and checks its metadata; false (with the status word set)
 // when the request must be skipped. Identical in every thread of the CTA.
@@ -135,18 +175,21 @@ __device__ __forceinline__ bool decode_item(const KdaArgs &p, int64_t it, int ns
     m.slot = load_index(p.indices, p.index_bytes[0], m.req);
     m.tslot = 0;
     m.tlen = -1;
+    m.rejected = false;
     if (m.bos < 0 || m.eos < m.bos || m.eos > p.num_tokens) {
         if (threadIdx.x == 0) report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
         return false;
     }
     if (m.slot < 0 || m.slot >= p.num_slots) {
         if (threadIdx.x == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+        m.rejected = true;
         return false;
     }
     if (p.track_indices != nullptr) {
         m.tslot = load_index(p.track_indices, p.index_bytes[2], m.req);
         if (m.tslot < 0 || m.tslot >= p.num_slots) {
             if (threadIdx.x == 0) report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
+            m.rejected = true;
             return false;
         }
         if (m.tslot > 0) m.tlen = load_index(p.track_lens, p.index_bytes[3], m.req);
@@ -412,7 +455,7 @@ __device__ __forceinline__ void token_from_stage(TokenRaw<D, MODE> &r, const Kda
 template <int D, int MODE, int STAGES, int MINB>
 __global__ void __launch_bounds__(kRecThreads + 32, MINB)
 recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bulk, int32_t len_lo,
-                      int32_t len_hi) {
+                      int32_t len_hi, int zero_fill) {
     using RS = RingStage<D, MODE>;
     constexpr int NC = D / 32;
     constexpr uint32_t kTileBytes = kBV * D * sizeof(float);
@@ -453,7 +496,7 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
             const int64_t bos = load_index(p.cu_seqlens, p.index_bytes[1], req);
             const int64_t eos = load_index(p.cu_seqlens, p.index_bytes[1], req + 1);
             const int64_t slot = load_index(p.indices, p.index_bytes[0], req);
-            int ok = 1;
+            int ok = 1, zero = 0;
             int64_t tslot = 0, tlen = -1;
             if (bos < 0 || eos < bos || eos > p.num_tokens) {
                 report(p.status, KDA_DEVICE_ERR_BAD_SEQLENS);
@@ -461,18 +504,20 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
             } else if (slot < 0 || slot >= p.num_slots) {
                 report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
                 ok = 0;
+                zero = zero_fill;
             } else if (p.track_indices != nullptr) {
                 tslot = load_index(p.track_indices, p.index_bytes[2], req);
                 if (tslot < 0 || tslot >= p.num_slots) {
                     report(p.status, KDA_DEVICE_ERR_BAD_SLOT);
                     ok = 0;
+                    zero = zero_fill;
                 } else if (tslot > 0) {
                     tlen = load_index(p.track_lens, p.index_bytes[3], req);
                 }
             }
             // A request outside [len_lo, len_hi] belongs to another kernel of
             // the same launch: nothing is read or written for it here.
-            if (ok && (eos - bos < len_lo || eos - bos > len_hi)) ok = 0;
+            if (eos - bos < len_lo || eos - bos > len_hi) ok = zero = 0;
             // beta (raw b) of the first token into the header by a 4-byte
             // cp.async that the stage's barrier also waits for (its tracking
             // arrive precedes the expect-tx arrive, so the phase cannot
@@ -502,6 +547,18 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
             hdr->v0 = v0;
             hdr->ok = ok;
             hdr->bsel = bsel;   // bword is written only by the copy below
+            // A rejected request's output rows: zeros, written here by the
+            // producer thread (a rare path the compute warps never see).
+            if (zero) {
+                for (int64_t t = bos; t < eos; ++t)
+                    for (int r = 0; r < kBV; ++r) {
+                        const int64_t oi = (t * p.num_heads + h) * D + v0 + r;
+                        if (p.out_fp32)
+                            static_cast<float *>(p.out)[oi] = 0.f;
+                        else
+                            static_cast<__nv_bfloat16 *>(p.out)[oi] = __float2bfloat16_rn(0.f);
+                    }
+            }
             if constexpr (MODE == KDA_GATE_RAW) hdr->a_log = ok ? __ldg(p.A_log + h) : 0.f;
             if (bsrc != nullptr) {
                 asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(&hdr->bword)), "l"(bsrc)
@@ -540,6 +597,10 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
                 ++use;
             }
         }
+        // Tokens no request covers (normally none): the last CTA's producer.
+        if (zero_fill && blockIdx.x == gridDim.x - 1)
+            zero_uncovered<D>(p, load_index(p.cu_seqlens, p.index_bytes[1], 0),
+                              load_index(p.cu_seqlens, p.index_bytes[1], p.num_req), 0, 1);
         return;
     }
 
@@ -603,15 +664,29 @@ recurrent_ring_kernel(const KdaArgs p, int nslice, int64_t num_items, int tok_bu
 // pool (used by prepared_recurrent on a [K,V]-contiguous state).
 template <int D, int MODE>
 __global__ void __launch_bounds__(kRecThreads, 3)
-recurrent_strided_kernel(const KdaArgs p, int nslice, int32_t len_lo, int32_t len_hi) {
+recurrent_strided_kernel(const KdaArgs p, int nslice, int32_t len_lo, int32_t len_hi, int zero_fill) {
     constexpr int NE = D / 8;
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int sub = lane & 7, rq = lane >> 3;
     const int row0 = warp * kRowsPerWarp + rq;
+    int64_t c0 = 0, cn = 0;
+    if (zero_fill) {
+        c0 = load_index(p.cu_seqlens, p.index_bytes[1], 0);
+        cn = load_index(p.cu_seqlens, p.index_bytes[1], p.num_req);
+    }
+    auto finish = [&] {
+        if (zero_fill)
+            zero_uncovered<D>(p, c0, cn, static_cast<int64_t>(blockIdx.x) * kRecThreads + tid,
+                              static_cast<int64_t>(gridDim.x) * kRecThreads);
+    };
     Item m;
-    if (!decode_item(p, blockIdx.x, nslice, m)) return;
-    if (m.eos - m.bos < len_lo || m.eos - m.bos > len_hi) return;   // another kernel's request
+    const bool valid = decode_item(p, blockIdx.x, nslice, m);
+    if (m.eos - m.bos < len_lo || m.eos - m.bos > len_hi) return finish();   // another kernel's request
+    if (!valid) {
+        if (zero_fill && m.rejected) zero_item_rows(p, m.h, m.v0, m.bos, m.eos, row0, sub, D);
+        return finish();
+    }
     const int64_t sk = p.state_stride[2], sv = p.state_stride[3];
     float s[2][NE];
     if (m.slot > 0) {
@@ -633,6 +708,7 @@ recurrent_strided_kernel(const KdaArgs p, int nslice, int32_t len_lo, int32_t le
     RawGateParams rp{};
     if constexpr (MODE == KDA_GATE_RAW) rp = load_raw_params<D>(p, m.h, sub);
     run_item<D, MODE, false>(p, m, s, row0, sub, cur, false, rp);
+    finish();
 }
 
 // ---------------------------------------------------------------------------
@@ -722,7 +798,7 @@ static int sm_count() {
 }
 
 template <int D, int MODE>
-static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st, int32_t len_lo, int32_t len_hi) {
+static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st, int32_t len_lo, int32_t len_hi, int zero_fill) {
     const int nslice = D / kBV;
     const int64_t items = static_cast<int64_t>(a->num_req) * a->head_count * nslice;
     if (fast) {
@@ -748,20 +824,20 @@ static void launch_rec(const KdaArgs *a, bool fast, cudaStream_t st, int32_t len
         const void *gate = MODE == KDA_GATE_RAW ? static_cast<const void *>(a->a) : static_cast<const void *>(a->g);
         const int tok_bulk = aligned16(a->q) && aligned16(a->k) && aligned16(gate) && aligned16(a->v) ? 1 : 0;
         recurrent_ring_kernel<D, MODE, RingShape<MODE>::kStages, RingShape<MODE>::kMinBlocks>
-            <<<static_cast<unsigned>(grid), kRecThreads + 32, smem, st>>>(*a, nslice, items, tok_bulk, len_lo, len_hi);
+            <<<static_cast<unsigned>(grid), kRecThreads + 32, smem, st>>>(*a, nslice, items, tok_bulk, len_lo, len_hi, zero_fill);
     } else {
         recurrent_strided_kernel<D, MODE>
-            <<<static_cast<unsigned>(items), kRecThreads, 0, st>>>(*a, nslice, len_lo, len_hi);
+            <<<static_cast<unsigned>(items), kRecThreads, 0, st>>>(*a, nslice, len_lo, len_hi, zero_fill);
     }
 }
 
 template <int D>
-static void dispatch_mode(const KdaArgs *a, bool fast, cudaStream_t st, int32_t len_lo = 0,
-                          int32_t len_hi = INT32_MAX) {
+static void dispatch_mode(const KdaArgs *a, bool fast, cudaStream_t st, int32_t len_lo, int32_t len_hi,
+                          int zero_fill) {
     switch (a->gate_mode) {
-        case KDA_GATE_RAW: launch_rec<D, KDA_GATE_RAW>(a, fast, st, len_lo, len_hi); break;
-        case KDA_GATE_LOG: launch_rec<D, KDA_GATE_LOG>(a, fast, st, len_lo, len_hi); break;
-        default: launch_rec<D, KDA_GATE_PREPARED>(a, fast, st, len_lo, len_hi); break;
+        case KDA_GATE_RAW: launch_rec<D, KDA_GATE_RAW>(a, fast, st, len_lo, len_hi, zero_fill); break;
+        case KDA_GATE_LOG: launch_rec<D, KDA_GATE_LOG>(a, fast, st, len_lo, len_hi, zero_fill); break;
+        default: launch_rec<D, KDA_GATE_PREPARED>(a, fast, st, len_lo, len_hi, zero_fill); break;
     }
 }
 
@@ -774,9 +850,9 @@ int recurrent_launch_range(const KdaArgs *args, int32_t len_lo, int32_t len_hi, 
     if (args->num_req == 0 || args->head_count == 0) return KDA_OK;
     const bool fast = state_fast(args) && mid_fast(args);
     if (args->head_dim == 128)
-        dispatch_mode<128>(args, fast, st, len_lo, len_hi);
+        dispatch_mode<128>(args, fast, st, len_lo, len_hi, 0);
     else
-        dispatch_mode<64>(args, fast, st, len_lo, len_hi);
+        dispatch_mode<64>(args, fast, st, len_lo, len_hi, 0);
     return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
 }
 
@@ -801,17 +877,25 @@ extern "C" const char *kda_status_string(int code) {
     }
 }
 
-extern "C" int kda_recurrent_launch(const KdaArgs *args, void *stream) {
-    const int rc = kda::validate_common(args);
+namespace kda {
+// Every request; with `zero_fill` the output rows no value is computed for
+// are written as zeros (kda_recurrent_launch); prepared_recurrent's output is
+// the caller's tensor and keeps its other rows.
+static int recurrent_launch_all(const KdaArgs *args, cudaStream_t st, int zero_fill) {
+    const int rc = validate_common(args);
     if (rc != KDA_OK) return rc;
     if (args->num_req == 0 || args->head_count == 0) return KDA_OK;
-    const bool fast = kda::state_fast(args) && kda::mid_fast(args);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const bool fast = state_fast(args) && mid_fast(args);
     if (args->head_dim == 128)
-        kda::dispatch_mode<128>(args, fast, st);
+        dispatch_mode<128>(args, fast, st, 0, INT32_MAX, zero_fill);
     else
-        kda::dispatch_mode<64>(args, fast, st);
+        dispatch_mode<64>(args, fast, st, 0, INT32_MAX, zero_fill);
     return cudaGetLastError() == cudaSuccess ? KDA_OK : KDA_ERR_LAUNCH;
+}
+}  // namespace kda
+
+extern "C" int kda_recurrent_launch(const KdaArgs *args, void *stream) {
+    return kda::recurrent_launch_all(args, static_cast<cudaStream_t>(stream), 1);
 }
 
 extern "C" int kda_prepared_recurrent_launch(const KdaArgs *args, void *stream) {
@@ -819,5 +903,5 @@ extern "C" int kda_prepared_recurrent_launch(const KdaArgs *args, void *stream) 
     KdaArgs a = *args;
     a.gate_mode = KDA_GATE_PREPARED;
     a.intermediate = nullptr;
-    return kda_recurrent_launch(&a, stream);
+    return kda::recurrent_launch_all(&a, static_cast<cudaStream_t>(stream), 0);
 }

@@ -220,7 +220,10 @@ at::Tensor kda_varlen_recurrent(const at::Tensor &A_log, const at::Tensor &a, co
     if (intermediate_state.has_value()) check_intermediate(*intermediate_state, d, q);
     check_regime(op, d, prefill, intermediate_state.has_value(), track_state_indices.has_value());
     c10::cuda::CUDAGuard guard(q.device());
-    at::Tensor out = at::zeros_like(v);
+    // The reference returns zeros_like(v) (kda_varlen_recurrent.cpp:142); the
+    // kernel writes zeros itself wherever it computes no value (tokens no
+    // request covers, rejected requests), which saves a separate fill.
+    at::Tensor out = d.num_req > 0 ? at::empty_like(v) : at::zeros_like(v);
     KdaArgs args = base_args(d, q, k, v, out, initial_state_source, initial_state_indices, cu_seqlens,
                              track_state_indices, track_state_lens, scale);
     args.gate_mode = KDA_GATE_RAW;
@@ -272,7 +275,10 @@ at::Tensor kda_varlen_recurrent_g(const at::Tensor &q, const at::Tensor &k, cons
     if (intermediate_state.has_value()) check_intermediate(*intermediate_state, d, q);
     check_regime(op, d, prefill, intermediate_state.has_value(), track_state_indices.has_value());
     c10::cuda::CUDAGuard guard(q.device());
-    at::Tensor out = at::zeros_like(v);
+    // The reference returns zeros_like(v) (kda_varlen_recurrent.cpp:142); the
+    // kernel writes zeros itself wherever it computes no value (tokens no
+    // request covers, rejected requests), which saves a separate fill.
+    at::Tensor out = d.num_req > 0 ? at::empty_like(v) : at::zeros_like(v);
     KdaArgs args = base_args(d, q, k, v, out, initial_state_source, initial_state_indices, cu_seqlens,
                              track_state_indices, track_state_lens, scale);
     args.gate_mode = KDA_GATE_LOG;

@@ -903,6 +903,11 @@ def main():
                     help="kernel / prefill-kernel: only the timed decode / chunk op loop (profiler captures)")
     ap.add_argument("--prefill-heads", type=int, default=32,
                     help="prefill-kernel mode: heads of config 3 (fewer keeps a full ncu capture small)")
+    ap.add_argument("--decode-gate", choices=("log", "raw"), default="log",
+                    help="kernel mode: config 2's log-gate op, or the raw-gate op on the reference benches' inputs")
+    ap.add_argument("--decode-batch", type=int, default=256, help="kernel mode: requests (1 token each), H=32")
+    ap.add_argument("--prefill-path", choices=("op", "auto", "fused", "split"), default="op",
+                    help="prefill-kernel mode: the torch op, or the C ABI with the chunk path forced")
     ap.add_argument("--long-tokens", type=int, default=131072,
                     help="prefill-long mode: sequence length of config 4 (shorter keeps an ncu capture small)")
     args = ap.parse_args()
@@ -923,9 +928,25 @@ def main():
     args.peaks = (hbm_gbs, bf16_tf)
     if args.mode == "prefill-kernel":
         import kda_workloads as workloads
-        from sgl_glm53_ascend_ops import ops
-        kw = workloads.config3(seed=2000 + dist.rank, heads=args.prefill_heads).to("cuda").kwargs()
-        ms = time_steps(lambda: ops.kda_varlen_chunk_g(**kw, prefill=True), args.steps, args.warmup, dist)
+        from sgl_glm53_ascend_ops import abi, ops
+        d = workloads.config3(seed=2000 + dist.rank, heads=args.prefill_heads).to("cuda")
+        kw = d.kwargs()
+        if args.prefill_path == "op":
+            step = lambda: ops.kda_varlen_chunk_g(**kw, prefill=True)   # noqa: E731
+        else:
+            path = {"auto": abi.KDA_CHUNK_AUTO, "fused": abi.KDA_CHUNK_FUSED, "split": abi.KDA_CHUNK_SPLIT}[
+                args.prefill_path]
+            cargs = abi.args_from_tensors(q=d.q, k=d.k, v=d.v, out=torch.empty_like(d.v), state=d.pool,
+                                          indices=d.indices, cu_seqlens=d.cu_seqlens, scale=d.scale,
+                                          gate_mode=abi.KDA_GATE_LOG, g=d.g, beta=d.beta)
+            nws = abi.chunk_path_workspace_bytes(cargs.num_req, cargs.num_tokens, cargs.head_count, 128, path)
+            ws = torch.empty(max(nws, 1), dtype=torch.uint8, device="cuda")
+
+            def step():
+                rc = abi.chunk_launch_path(cargs, ws, nws, path)
+                if rc != 0:
+                    raise RuntimeError(f"kda_chunk_launch_path: {abi.status_string(rc)}")
+        ms = time_steps(step, args.steps, args.warmup, dist)
         if dist.rank == 0:
             print(json.dumps({"mode": "prefill-kernel", "ms_per_step": ms / args.steps}), flush=True)
         dist.close()
@@ -939,8 +960,15 @@ def main():
     if args.mode == "kernel":
         import kda_workloads as workloads
         from sgl_glm53_ascend_ops import ops
-        kw = workloads.config2(seed=1000 + dist.rank).to("cuda").kwargs()
-        ms = time_steps(lambda: ops.kda_varlen_recurrent_g(**kw, prefill=False), args.steps, args.warmup, dist)
+        if args.decode_gate == "raw":
+            # the reference's own op interface: raw gate, 1 token per request,
+            # the reference benches' inputs (bench_kda_varlen_recurrent.py)
+            rk = _raw_case(32, [1] * args.decode_batch, 513, seed=1000 + dist.rank)
+            step = lambda: ops.kda_varlen_recurrent(**rk, prefill=False)   # noqa: E731
+        else:
+            kw = workloads.config2(seed=1000 + dist.rank, requests=args.decode_batch).to("cuda").kwargs()
+            step = lambda: ops.kda_varlen_recurrent_g(**kw, prefill=False)   # noqa: E731
+        ms = time_steps(step, args.steps, args.warmup, dist)
         if dist.rank == 0:
             print(json.dumps({"mode": "kernel", "ms_per_step": ms / args.steps}), flush=True)
         dist.close()

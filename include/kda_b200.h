@@ -123,10 +123,13 @@ int kda_abi_version(void);
 const char *kda_status_string(int code);
 
 /* Token-at-a-time recurrence: decode (one or more tokens per request, the
- * EAGLE verify regime with `intermediate`) and recurrent prefill. One CTA per
- * (request, head, 32-row value slice); the 128x128 fp32 state slice is staged
- * into shared memory with a bulk TMA copy. Replaces LaunchKdaDecodeH{16,32,64}
- * and LaunchKdaPrefillH{4,8} (kda_varlen_recurrent.h:94-98). */
+ * EAGLE verify regime with `intermediate`) and recurrent prefill. Persistent
+ * CTAs walk (request, head, 32-row value slice) items through a ring of
+ * shared-memory stages filled by bulk TMA copies. Every token row of `out`
+ * for the heads processed is written: tokens no request covers, and the
+ * tokens of a request rejected by the slot bounds check, as zeros.
+ * Replaces LaunchKdaDecodeH{16,32,64} and LaunchKdaPrefillH{4,8}
+ * (kda_varlen_recurrent.h:94-98). */
 int kda_recurrent_launch(const KdaArgs *args, void *stream);
 
 /* Bytes of device workspace kda_chunk_launch needs for these sizes (replaces

@@ -177,6 +177,35 @@ def test_decode_checkpoints_match_oracle(ops, heads, lengths):
     assert torch.equal(dkw["initial_state_source"].cpu(), kw["initial_state_source"])
 
 
+@pytest.mark.parametrize("lengths", [(4,) * 3, (1, 2, 3, 4, 6), (2, 2)], ids=str)
+@pytest.mark.parametrize("log_gate", (False, True))
+def test_verify_sized_batches_d64(ops, lengths, log_gate):
+    """Verify-sized batches (a few tokens per request, per-step checkpoints)
+    at D = 64, with both gate forms."""
+    heads, D = 4, 64
+    kw = _raw_case(heads, lengths, D=D, seed=17)
+    if log_gate:
+        T = sum(lengths)
+        g = torch.nn.functional.logsigmoid(torch.randn(1, T, heads, D)).clamp(-5.0, 0.0)
+        beta = torch.sigmoid(torch.randn(1, T, heads))
+        kw = dict(q=kw["q"], k=kw["k"], v=kw["v"], g=g, beta=beta, initial_state_source=kw["initial_state_source"],
+                  initial_state_indices=kw["initial_state_indices"], cu_seqlens=kw["cu_seqlens"], scale=kw["scale"])
+    noise = (torch.randn(len(lengths), max(lengths), heads, D, D) * 0.1).transpose(-1, -2)
+    mid = clone_pool(noise).transpose(-1, -2).to(DEV).transpose(-1, -2)
+    dkw = _dev(kw)
+    op = ops.kda_varlen_recurrent_g if log_gate else ops.kda_varlen_recurrent
+    out = op(**dkw, intermediate_state=mid, prefill=False)
+    torch.cuda.synchronize()
+    ref_mid = clone_pool(noise)
+    ref_fn = kda_ref.kda_varlen_recurrent_g if log_gate else kda_ref.kda_varlen_recurrent
+    ref = ref_fn(**dict(kw, initial_state_source=clone_pool(kw["initial_state_source"])),
+                 intermediate_state=ref_mid, out_fp32=True)
+    assert_out_close(out.cpu(), ref)
+    got = mid.cpu()
+    for r, n in enumerate(lengths):
+        assert_state_close(got[r, :n], ref_mid[r, :n], what=f"checkpoints of request {r}")
+
+
 def test_cfg2_decode_full_size(ops):
     """BASELINE config 2 at full size: 256 requests, H=32, pool of 512 slots."""
     import kda_workloads as workloads
@@ -271,6 +300,51 @@ def test_abi_reports_bad_slot_without_touching_memory(abi):
     assert int(status.item()) == 0x102
     touched = [int(s) for i, s in enumerate(d.indices.tolist()) if i != 2]
     assert_untouched(d.pool, before, touched)
+
+
+@pytest.mark.parametrize("prefill", (False, True))
+def test_uncovered_tokens_read_zero(ops, prefill):
+    """The op returns zeros wherever it computes nothing, as the reference's
+    zeros_like output does (kda_varlen_recurrent.cpp:142): tokens before
+    cu_seqlens[0] and after cu_seqlens[-1]. The output memory is dirtied first
+    so a missing write cannot pass by the allocator's luck."""
+    kw = _raw_case(3, (3, 4), slots=6, seed=8)
+    tokens = 12
+    for n in ("q", "k", "v", "a"):
+        kw[n] = (torch.randn(1, tokens, 3, 128) * 0.2).bfloat16()
+    kw["b"] = torch.randn(1, tokens, 3).bfloat16()
+    kw["cu_seqlens"] = torch.tensor([2, 5, 9], dtype=torch.int32)
+    ref_kw = dict(kw)
+    ref_pool = clone_pool(kw["initial_state_source"])
+    ref = kda_ref.kda_varlen_recurrent(**dict(ref_kw, initial_state_source=ref_pool), out_fp32=True,
+                                       prefill=prefill)
+    for _ in range(3):                                 # leave non-zero bytes in the allocator's blocks
+        junk = torch.full((1, tokens, 3, 128), 7.0, dtype=torch.bfloat16, device=DEV)
+        del junk
+    out, pool = _run_op(ops.kda_varlen_recurrent, kw, prefill=prefill)
+    assert torch.equal(out[:, :2], torch.zeros_like(out[:, :2]))
+    assert torch.equal(out[:, 9:], torch.zeros_like(out[:, 9:]))
+    assert_out_close(out[:, 2:9], ref[:, 2:9])
+    assert_state_close(pool[1:3], ref_pool[1:3])
+
+
+def test_rejected_request_rows_read_zero(abi):
+    """A request whose slot fails the bounds check computes nothing: its
+    output rows are zeros (the C ABI writes every token), the others match."""
+    import kda_workloads as workloads
+    w = workloads.config2(requests=4, heads=2, slots=8)
+    d = w.to(DEV)
+    d.indices[1] = 8                                   # one past the pool
+    out = torch.full_like(d.v, 7.0)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    args = abi.args_from_tensors(q=d.q, k=d.k, v=d.v, out=out, state=d.pool, indices=d.indices,
+                                 cu_seqlens=d.cu_seqlens, scale=d.scale, gate_mode=abi.KDA_GATE_LOG,
+                                 g=d.g, beta=d.beta, status=status)
+    assert abi.recurrent_launch(args) == abi.KDA_OK
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0x102
+    assert torch.equal(out[:, 1], torch.zeros_like(out[:, 1]))
+    assert (out[:, [0, 2, 3]] != 7.0).all()
 
 
 # ---------------------------------------------------------------------------
