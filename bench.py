@@ -25,14 +25,23 @@ Also reported:
 * ``cpu_baseline``: the CPU oracle (``oracle/kda_ref.py``, a port of the
   reference's PyTorch recurrence) on this host's cores, on a bounded sample;
 * ``prefill``: the chunked prefill of ``configs[2]`` (8 varlen sequences,
-  33,494 tokens, H=32) with its tensor/HBM roofline;
+  33,494 tokens, H=32) with its tensor/HBM roofline, per rank (weak);
+* ``prefill_strong`` / ``mixed``: ``configs[2]`` and ``configs[4]`` (64
+  one-token requests + 4 resumed 2048-token prefills) split 32/N heads per
+  rank (strong scaling), verified after timing against one GPU running all
+  heads (outputs and updated slots gathered with NCCL on rank 0, untouched
+  slots checked on every rank);
 * ``prefill_long``: ``configs[3]`` (one 131,072-token sequence, 4 heads per
-  GPU) through the same op;
+  GPU) through the same op, with the split path's phases and DRAM traffic;
+* ``published_shapes``: every shape the reference publishes an Ascend 910B
+  time for (decode H16/32/64 x B1/32/128, the five verify shapes with the
+  commit, chunk prefill H8 x T1024/2048/4096), through the raw-gate ops;
 * ``clocks``: SM clock and throttle reasons sampled by NVML during timing.
 
-``--impl reference`` times the reference's own CPU algorithm (the oracle port;
-the reference is Python and Ascend-only, so nothing of it can run on the GPU
-box) on the same metric and configuration.
+``--lines`` picks the secondary lines (default: all). ``--impl reference``
+times the reference's own CPU algorithm (the oracle port; the reference is
+PyTorch plus Ascend-only kernels, so nothing of it can run on the GPU box) on
+the headline's exact workload, loading no library of this repository.
 """
 
 from __future__ import annotations
