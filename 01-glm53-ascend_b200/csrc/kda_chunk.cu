@@ -3156,9 +3156,13 @@ static int chunk_launch_path(const KdaArgs *args, void *workspace, size_t worksp
     // kernel.
     int32_t skip_hi = 0;
     if (path == KDA_CHUNK_AUTO) {
+        // The recurrence wants 16-byte aligned dt_bias for the raw gate, which
+        // the chunk kernel does not: without it every request stays here.
         rc = recurrent_launch_range(args, 1, kShortLen, st);
-        if (rc != KDA_OK) return rc;
-        skip_hi = kShortLen;
+        if (rc == KDA_OK)
+            skip_hi = kShortLen;
+        else if (rc != KDA_ERR_ALIGNMENT)
+            return rc;
     }
     if (args->head_dim == 128)
         rc = args->gate_mode == KDA_GATE_RAW ? launch_chunk<128, KDA_GATE_RAW>(args, order, st, skip_hi)
