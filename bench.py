@@ -141,9 +141,9 @@ class Dist:
         if self.pg is None:
             return x
         x = x.contiguous()
-        buf = torch.empty((self.world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
-        self.pg.all_gather_into_tensor(buf, x)
-        return torch.cat(list(buf.unbind(0)), dim=dim)
+        buf = torch.empty(self.world * x.numel(), dtype=x.dtype, device=x.device)
+        self.pg.all_gather_into_tensor(buf, x.reshape(-1))
+        return torch.cat(list(buf.view((self.world,) + tuple(x.shape)).unbind(0)), dim=dim)
 
     def close(self):
         if self.pg is not None:

@@ -70,6 +70,39 @@ def test_head_shards_reassemble_on_two_gloo_ranks(tmp_path):
     assert got["max"] == 2.0
 
 
+def _gather_worker(rank: int, world: int, port: int, result_path: str):
+    sys.path[:0] = [str(ROOT), str(ROOT / "01-glm53-ascend_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+        from kda_workloads import config5
+
+        d = bench.Dist()
+        d.world, d.rank, d.pg = world, rank, dist
+        w = config5(heads=4, decode=3, prefills=1, prefill_len=5, slots=9)
+        shard = w.head_shard(rank, world)
+        got_q = d.gather_heads(shard.q, dim=2)                    # [1, T, H, D] along heads
+        got_pool = d.gather_heads(shard.pool[1:3], dim=1)         # [slots, H, K, V] along heads
+        if rank == 0:
+            torch.save({"q": got_q, "pool": got_pool}, result_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_bench_gather_reassembles_head_shards(tmp_path):
+    """bench.py's verification gather (Dist.gather_heads) puts every rank's
+    head shard back in rank order, for token tensors and pool slices."""
+    from kda_workloads import config5
+
+    result = tmp_path / "g.pt"
+    mp.start_processes(_gather_worker, args=(2, _free_port(), str(result)), nprocs=2, start_method="spawn")
+    got = torch.load(result)
+    w = config5(heads=4, decode=3, prefills=1, prefill_len=5, slots=9)
+    assert torch.equal(got["q"], w.q)
+    assert torch.equal(got["pool"], w.pool[1:3])
+
+
 def test_head_shard_layout():
     sys.path[:0] = [str(ROOT / "01-glm53-ascend_b200")]
     from kda_workloads import config3
