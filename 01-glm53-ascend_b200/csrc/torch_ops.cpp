@@ -11,7 +11,8 @@
 // plus two log-gate ops (`kda_varlen_recurrent_g`, `kda_varlen_chunk_g`) that
 // take the fp32 log-decay g and beta directly, and the speculative-decoding
 // commit `move_intermediate_cache_kda` (sgl_kernel_npu's function of that name,
-// which the reference's MTP test calls after a verify).
+// which the reference's MTP test calls after a verify), and the causal-conv
+// front end `kda_causal_conv1d` that feeds q, k and v to the KDA ops.
 //
 // Error messages keep the reference's wording where a caller matches on it
 // ("must be K-contiguous", "does not support", "expects ...",
@@ -443,6 +444,103 @@ void move_intermediate_cache_kda(at::Tensor &dst, const at::Tensor &src, const a
     check_kda(kda_commit_intermediate_launch(&a, current_stream(dst)), "move_intermediate_cache_kda");
 }
 
+// kda_causal_conv1d: the causal-conv front end of the attention layer
+// (kda_conv_launch), the causal_conv1d step sglang's backend runs on the mixed
+// q | k | v projection before the KDA op
+// (sgl-glm53-ascend-ops/tests/integration/test_glm53_kda_prefix_ascendc.py:325-387):
+//   x          [T, C] or [1, T, C] bf16, channels contiguous (a column slice of
+//              a wider projection is fine: any row stride that is a multiple of 8)
+//   weight     [C, W] (W <= 4; any float dtype, used as fp32), bias [C] or None
+//   conv_state [slots, window, C] bf16, updated in place (W - 1 <= window <= 8)
+//   cache_indices [R], query_start_loc [R + 1]: int32 or int64
+//   has_initial_state [R] bool/int or None (None: every request continues)
+//   track_conv_indices, track_conv_lens [R] or None: tracked-prefix checkpoint
+// Returns [num_parts, T, C / num_parts] bf16: with num_parts = 3 the q, k and v
+// planes, each the contiguous [T, H, D] tensor the KDA op takes.
+at::Tensor kda_causal_conv1d(const at::Tensor &x, const at::Tensor &weight, const c10::optional<at::Tensor> &bias,
+                             at::Tensor &conv_state, const at::Tensor &cache_indices,
+                             const at::Tensor &query_start_loc, const c10::optional<at::Tensor> &has_initial_state,
+                             const c10::optional<at::Tensor> &track_conv_indices,
+                             const c10::optional<at::Tensor> &track_conv_lens, int64_t num_parts, bool silu) {
+    TORCH_CHECK(x.is_cuda(), "x must be a CUDA tensor");
+    TORCH_CHECK(x.scalar_type() == at::kBFloat16, "x must be bf16");
+    TORCH_CHECK(x.dim() == 2 || (x.dim() == 3 && x.size(0) == 1), "kda_causal_conv1d expects [T, C] or [1, T, C] x");
+    const at::Tensor x2 = x.dim() == 3 ? x.select(0, 0) : x;
+    TORCH_CHECK(x2.stride(1) == 1, "x must be channel-contiguous (stride(-1) == 1)");
+    const int64_t T = x2.size(0), C = x2.size(1);
+    TORCH_CHECK(weight.dim() == 2 && weight.size(0) == C, "weight must be [C, W] with C = ", C);
+    const int64_t W = weight.size(1);
+    TORCH_CHECK(W >= 1 && W <= 4, "kda_causal_conv1d does not support ", W, " taps (1..4)");
+    TORCH_CHECK(weight.device() == x.device(), "weight must be on the same device as x");
+    const at::Tensor w32 = weight.to(at::kFloat).contiguous();
+    at::Tensor b32;
+    if (bias.has_value() && bias->defined()) {
+        TORCH_CHECK(bias->numel() == C && bias->device() == x.device(), "bias must be [C] on the device of x");
+        b32 = bias->to(at::kFloat).contiguous();
+    }
+    TORCH_CHECK(conv_state.dim() == 3 && conv_state.scalar_type() == at::kBFloat16 && conv_state.size(2) == C,
+                "conv_state must be a bf16 [slots, window, C] tensor with C = ", C);
+    TORCH_CHECK(conv_state.stride(2) == 1, "conv_state must be channel-contiguous (stride(2) == 1)");
+    TORCH_CHECK(conv_state.device() == x.device(), "conv_state must be on the same device as x");
+    TORCH_CHECK(conv_state.size(1) >= W - 1, "conv_state window (", conv_state.size(1), ") must hold W - 1 = ",
+                W - 1, " rows");
+    TORCH_CHECK(num_parts >= 1 && C % num_parts == 0, "num_parts must divide C");
+    check_index("cache_indices", cache_indices, x);
+    check_index("query_start_loc", query_start_loc, x);
+    const int64_t R = cache_indices.numel();
+    TORCH_CHECK(query_start_loc.numel() == R + 1, "query_start_loc must have len(cache_indices) + 1 entries");
+    TORCH_CHECK(track_conv_indices.has_value() == track_conv_lens.has_value(),
+                "track_conv_indices and track_conv_lens must be given together");
+    if (track_conv_indices.has_value()) {
+        check_index("track_conv_indices", *track_conv_indices, x);
+        check_index("track_conv_lens", *track_conv_lens, x);
+        TORCH_CHECK(track_conv_indices->numel() == R && track_conv_lens->numel() == R,
+                    "track_conv_indices and track_conv_lens must have one entry per request");
+    }
+    int32_t init_bytes = 1;
+    if (has_initial_state.has_value()) {
+        const auto &hi = *has_initial_state;
+        TORCH_CHECK(hi.numel() == R && hi.is_contiguous() && hi.device() == x.device(),
+                    "has_initial_state must be a contiguous [R] tensor on the device of x");
+        TORCH_CHECK(hi.scalar_type() == at::kBool || hi.scalar_type() == at::kByte || hi.scalar_type() == at::kInt ||
+                        hi.scalar_type() == at::kLong,
+                    "has_initial_state must be bool, uint8, int32 or int64");
+        init_bytes = static_cast<int32_t>(hi.element_size());
+    }
+    c10::cuda::CUDAGuard guard(x.device());
+    at::Tensor out = at::empty({num_parts, T, C / num_parts}, x.options());
+    KdaConvArgs a{};
+    a.x = x2.data_ptr();
+    a.x_row_stride = x2.stride(0);
+    a.weight = w32.data_ptr<float>();
+    a.bias = b32.defined() ? b32.data_ptr<float>() : nullptr;
+    a.conv_state = conv_state.data_ptr();
+    a.state_stride[0] = conv_state.stride(0);
+    a.state_stride[1] = conv_state.stride(1);
+    a.num_slots = conv_state.size(0);
+    a.window = static_cast<int32_t>(conv_state.size(1));
+    a.indices = cache_indices.data_ptr();
+    a.cu_seqlens = query_start_loc.data_ptr();
+    a.has_initial = has_initial_state.has_value() ? has_initial_state->data_ptr() : nullptr;
+    a.track_indices = track_conv_indices.has_value() ? track_conv_indices->data_ptr() : nullptr;
+    a.track_lens = track_conv_lens.has_value() ? track_conv_lens->data_ptr() : nullptr;
+    a.index_bytes[0] = index_bytes(cache_indices);
+    a.index_bytes[1] = index_bytes(query_start_loc);
+    a.index_bytes[2] = init_bytes;
+    a.index_bytes[3] = track_conv_indices.has_value() ? index_bytes(*track_conv_indices) : 4;
+    a.index_bytes[4] = track_conv_lens.has_value() ? index_bytes(*track_conv_lens) : 4;
+    a.num_req = static_cast<int32_t>(R);
+    a.num_tokens = static_cast<int32_t>(T);
+    a.channels = static_cast<int32_t>(C);
+    a.width = static_cast<int32_t>(W);
+    a.num_parts = static_cast<int32_t>(num_parts);
+    a.activation = silu ? KDA_CONV_ACT_SILU : KDA_CONV_ACT_NONE;
+    a.out = out.data_ptr();
+    a.status = status_ptr(x.device());
+    check_kda(kda_conv_launch(&a, current_stream(x)), "kda_causal_conv1d");
+    return out;
+}
+
 // Registers (or clears, with an undefined tensor) an int32 device word that
 // the kernels on that device report KDA_DEVICE_ERR_* codes into.
 void kda_set_status_buffer(int64_t device, const c10::optional<at::Tensor> &buf) {
@@ -485,6 +583,9 @@ TORCH_LIBRARY(sgl_glm53_ascend, m) {
           "bool prefill=False, Tensor? track_state_indices=None, Tensor? track_state_lens=None) -> Tensor");
     m.def("move_intermediate_cache_kda(Tensor(a!) dst, Tensor src, Tensor dst_indices, Tensor src_indices, "
           "Tensor step_indices, int h_block_size=1) -> ()");
+    m.def("kda_causal_conv1d(Tensor x, Tensor weight, Tensor? bias, Tensor(a!) conv_state, Tensor cache_indices, "
+          "Tensor query_start_loc, Tensor? has_initial_state=None, Tensor? track_conv_indices=None, "
+          "Tensor? track_conv_lens=None, int num_parts=3, bool silu=True) -> Tensor");
     m.def("kda_set_status_buffer(int device, Tensor? buf) -> ()");
     m.def("kda_abi_version() -> int");
     m.impl("kda_set_status_buffer", &kda_set_status_buffer);
@@ -500,4 +601,5 @@ TORCH_LIBRARY_IMPL(sgl_glm53_ascend, CUDA, m) {
     m.impl("kda_varlen_recurrent_g", &kda_varlen_recurrent_g);
     m.impl("kda_varlen_chunk_g", &kda_varlen_chunk_g);
     m.impl("move_intermediate_cache_kda", &move_intermediate_cache_kda);
+    m.impl("kda_causal_conv1d", &kda_causal_conv1d);
 }

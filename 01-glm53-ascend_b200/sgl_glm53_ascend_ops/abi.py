@@ -2,7 +2,7 @@
 
 This is the binding a non-torch host (or a maintainer wiring the library into
 another runtime) would write: a ``KdaArgs`` struct of raw device pointers,
-strides and sizes, and the four launch entry points. ``args_from_tensors``
+strides and sizes, and the launch entry points. ``args_from_tensors``
 fills the struct from torch tensors for tests and the benchmark; the library
 itself never sees a torch type.
 """
@@ -24,6 +24,7 @@ KDA_OK = 0
  KDA_ERR_TOO_LARGE) = range(1, 7)
 KDA_GATE_RAW, KDA_GATE_LOG, KDA_GATE_PREPARED = 0, 1, 2
 KDA_CHUNK_AUTO, KDA_CHUNK_FUSED, KDA_CHUNK_SPLIT = 0, 1, 2
+KDA_CONV_ACT_NONE, KDA_CONV_ACT_SILU = 0, 1
 
 # Entry points declared in include/kda_b200.h.
 EXPORTED = (
@@ -39,6 +40,7 @@ EXPORTED = (
     "kda_chunk_launch_no_alloc",
     "kda_commit_intermediate_launch",
     "kda_selftest_wait_timeout",
+    "kda_conv_launch",
 )
 
 
@@ -99,6 +101,33 @@ class KdaCommitArgs(ctypes.Structure):
     ]
 
 
+class KdaConvArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", ctypes.c_void_p),
+        ("x_row_stride", ctypes.c_int64),
+        ("weight", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("conv_state", ctypes.c_void_p),
+        ("state_stride", ctypes.c_int64 * 2),
+        ("num_slots", ctypes.c_int64),
+        ("window", ctypes.c_int32),
+        ("indices", ctypes.c_void_p),
+        ("cu_seqlens", ctypes.c_void_p),
+        ("has_initial", ctypes.c_void_p),
+        ("track_indices", ctypes.c_void_p),
+        ("track_lens", ctypes.c_void_p),
+        ("index_bytes", ctypes.c_int32 * 5),
+        ("num_req", ctypes.c_int32),
+        ("num_tokens", ctypes.c_int32),
+        ("channels", ctypes.c_int32),
+        ("width", ctypes.c_int32),
+        ("num_parts", ctypes.c_int32),
+        ("activation", ctypes.c_int32),
+        ("out", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 
 
@@ -131,6 +160,8 @@ def lib() -> ctypes.CDLL:
         L.kda_selftest_wait_timeout.restype = ctypes.c_int
         L.kda_selftest_wait_timeout.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
                                                 ctypes.c_int32, ctypes.c_void_p]
+        L.kda_conv_launch.restype = ctypes.c_int
+        L.kda_conv_launch.argtypes = [ctypes.POINTER(KdaConvArgs), ctypes.c_void_p]
         L.kda_chunk_launch_phases.restype = ctypes.c_int
         L.kda_chunk_launch_phases.argtypes = [ctypes.POINTER(KdaArgs), ctypes.c_void_p, ctypes.c_size_t,
                                               ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]
@@ -261,6 +292,36 @@ def selftest_wait_timeout(status: torch.Tensor, expired: torch.Tensor, polls: in
     """Waits that must run out (see kda_selftest_wait_timeout in the header)."""
     return lib().kda_selftest_wait_timeout(_ptr(status), _ptr(expired), polls, waits, int(give_up),
                                            stream_handle(stream))
+
+
+def conv_args_from_tensors(*, x, weight, conv_state, indices, cu_seqlens, out, bias=None, has_initial=None,
+                           track_indices=None, track_lens=None, num_parts=3, silu=True,
+                           status=None) -> KdaConvArgs:
+    """KdaConvArgs from device tensors: x [T, C] bf16 (channel-contiguous rows),
+    weight [C, W] fp32 contiguous, conv_state [slots, window, C] bf16
+    (channel-contiguous), out [num_parts, T, C / num_parts] bf16."""
+    a = KdaConvArgs()
+    a.x, a.x_row_stride = _ptr(x), x.stride(0)
+    a.weight, a.bias = _ptr(weight), _ptr(bias)
+    a.conv_state = _ptr(conv_state)
+    a.state_stride[0], a.state_stride[1] = conv_state.stride(0), conv_state.stride(1)
+    a.num_slots, a.window = conv_state.shape[0], conv_state.shape[1]
+    a.indices, a.cu_seqlens, a.has_initial = _ptr(indices), _ptr(cu_seqlens), _ptr(has_initial)
+    a.track_indices, a.track_lens = _ptr(track_indices), _ptr(track_lens)
+    a.index_bytes[0], a.index_bytes[1] = _ibytes(indices), _ibytes(cu_seqlens)
+    a.index_bytes[2] = has_initial.element_size() if has_initial is not None else 1
+    a.index_bytes[3], a.index_bytes[4] = _ibytes(track_indices), _ibytes(track_lens)
+    a.num_req, a.num_tokens = indices.numel(), x.shape[0]
+    a.channels, a.width = x.shape[1], weight.shape[1]
+    a.num_parts = num_parts
+    a.activation = KDA_CONV_ACT_SILU if silu else KDA_CONV_ACT_NONE
+    a.out = _ptr(out)
+    a.status = _ptr(status)
+    return a
+
+
+def conv_launch(args: KdaConvArgs, stream: Optional[torch.cuda.Stream] = None) -> int:
+    return lib().kda_conv_launch(ctypes.byref(args), stream_handle(stream))
 
 
 def status_string(code: int) -> str:

@@ -36,6 +36,8 @@ Also reported:
 * ``published_shapes``: every shape the reference publishes an Ascend 910B
   time for (decode H16/32/64 x B1/32/128, the five verify shapes with the
   commit, chunk prefill H8 x T1024/2048/4096), through the raw-gate ops;
+* ``frontend``: the causal-conv front end that feeds the op (``kda_causal_conv1d``)
+  on config 3's prefill and config 2's decode shapes at H=32, against HBM;
 * ``clocks``: SM clock and throttle reasons sampled by NVML during timing.
 
 ``--lines`` picks the secondary lines (default: all). ``--impl reference``
@@ -806,6 +808,63 @@ def bench_published_shapes(args, dist: Dist, hbm_gbs: float, bf16_tf: float, ite
             "decode": decode, "verify": verify, "chunk_prefill": chunk}
 
 
+# ---------------------------------------------------------------------------
+# Causal-conv front end (the step before the KDA op in the attention layer)
+# ---------------------------------------------------------------------------
+
+CONV_TAPS = 4
+CONV_WINDOW = 3
+
+
+def conv_bytes(T: int, R: int, C: int, window: int) -> int:
+    """Algorithmic bytes of one conv call: the mixed projection read and the
+    q/k/v planes written (bf16), each request's window read and written, the
+    fp32 weights read once."""
+    return 2 * T * C * 2 + 2 * R * window * C * 2 + C * CONV_TAPS * 4
+
+
+def bench_frontend(args, dist: Dist, hbm_gbs: float, steps: int, warmup: int) -> dict:
+    """The causal-conv front end (``kda_causal_conv1d``: depthwise 4-tap conv
+    over the mixed q|k|v projection, SiLU, q/k/v planes, conv-state window
+    update) at H=32 on config 3's 8 prefill sequences (inputs larger than L2:
+    no flush) and on config 2's 256 one-token decode requests (L2-sized:
+    flushed per call). Per rank (weak)."""
+    import kda_workloads as workloads
+    import sgl_glm53_ascend_ops  # noqa: F401  (registers the torch ops)
+
+    H = 32
+    C = 3 * H * 128
+    lengths = workloads.config3_lengths()
+    w = workloads.conv_frontend(lengths, heads=H, window=CONV_WINDOW, seed=6000 + dist.rank, device="cuda")
+    op = torch.ops.sgl_glm53_ascend.kda_causal_conv1d
+    call = lambda: op(w["x"], w["weight"], None, w["conv_state"], w["cache_indices"],   # noqa: E731
+                      w["query_start_loc"], None, None, None, 3, True)
+    T, R = sum(lengths), len(lengths)
+    ms = time_steps(call, steps, warmup, dist) / steps
+    nbytes = conv_bytes(T, R, C, CONV_WINDOW)
+    pre = {"workload": f"cfg3 lengths {lengths} (T={T}), C = 3 x 32 x 128 = {C}, {CONV_TAPS} taps, "
+                       f"window {CONV_WINDOW}, every request continuing from its slot",
+           "ms_per_step": round(ms, 4), "tokens_per_s": round(T / (ms / 1e3), 1),
+           "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms / 1e3) / 1e9, 1), "peak": hbm_gbs,
+                        "unit": "GB/s", "frac": round(nbytes / (ms / 1e3) / 1e9 / hbm_gbs, 4),
+                        "algorithmic_bytes": nbytes},
+           "l2": "inputs larger than L2, no flush"}
+    del w
+    d = workloads.conv_frontend([1] * 256, heads=H, window=CONV_WINDOW, seed=6100 + dist.rank, device="cuda")
+    dcall = lambda: op(d["x"], d["weight"], None, d["conv_state"], d["cache_indices"],   # noqa: E731
+                       d["query_start_loc"], None, None, None, 3, True)
+    dms = time_flushed(dcall, 20, warmup, dist)
+    dbytes = conv_bytes(256, 256, C, CONV_WINDOW)
+    dec = {"workload": f"cfg2 shape: 256 one-token requests, C = {C}, window {CONV_WINDOW}",
+           "us": round(dms * 1e3, 2), "tokens_per_s": round(256 / (dms / 1e3), 1),
+           "hbm_gbs": round(dbytes / (dms / 1e3) / 1e9, 1), "hbm_frac": round(dbytes / (dms / 1e3) / 1e9 / hbm_gbs, 4),
+           "algorithmic_bytes": dbytes, "l2": "256 MiB flush before each call, median of 20"}
+    del d
+    torch.cuda.empty_cache()
+    return {"metric": "KDA causal-conv front end (kda_causal_conv1d) tokens/s and HBM GB/s",
+            "prefill": pre, "decode": dec, "gpu_launches_per_call": 1}
+
+
 def cpu_prefill_rate(tokens: int, budget_s: float, seed: int = 8):
     """tokens/s of the CPU chunk oracle on one sequence of `tokens` tokens, H=32."""
     from oracle import kda_ref
@@ -895,7 +954,7 @@ def run_reference(args, dist: Dist):
 
 DECODE_WORKLOAD = ("cfg2 decode: 256 req x 1 tok, H=32, K=V=128, fp32 pool 512 slots, "
                    "256 distinct slots updated in place (log-gate op)")
-LINES = ("prefill", "strong", "mixed", "long", "shapes")
+LINES = ("prefill", "strong", "mixed", "long", "shapes", "frontend")
 
 
 def main():
@@ -908,8 +967,10 @@ def main():
     ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--lines", default=",".join(LINES),
                     help="secondary lines to run besides the headline decode: " + ",".join(LINES))
-    ap.add_argument("--mode", choices=("full", "kernel", "prefill-kernel", "prefill-long"), default="full",
-                    help="kernel / prefill-kernel: only the timed decode / chunk op loop (profiler captures)")
+    ap.add_argument("--mode", choices=("full", "kernel", "prefill-kernel", "prefill-long", "frontend-kernel"),
+                    default="full",
+                    help="kernel / prefill-kernel / frontend-kernel: only the timed decode / chunk / conv op "
+                         "loop (profiler captures)")
     ap.add_argument("--prefill-heads", type=int, default=32,
                     help="prefill-kernel mode: heads of config 3 (fewer keeps a full ncu capture small)")
     ap.add_argument("--decode-gate", choices=("log", "raw"), default="log",
@@ -960,6 +1021,19 @@ def main():
             print(json.dumps({"mode": "prefill-kernel", "ms_per_step": ms / args.steps}), flush=True)
         dist.close()
         return
+    if args.mode == "frontend-kernel":
+        import kda_workloads as workloads
+        import sgl_glm53_ascend_ops  # noqa: F401
+        w = workloads.conv_frontend(workloads.config3_lengths(), heads=args.prefill_heads, window=CONV_WINDOW,
+                                    seed=6000 + dist.rank, device="cuda")
+        op = torch.ops.sgl_glm53_ascend.kda_causal_conv1d
+        step = lambda: op(w["x"], w["weight"], None, w["conv_state"], w["cache_indices"],   # noqa: E731
+                          w["query_start_loc"], None, None, None, 3, True)
+        ms = time_steps(step, args.steps, args.warmup, dist)
+        if dist.rank == 0:
+            print(json.dumps({"mode": "frontend-kernel", "ms_per_step": ms / args.steps}), flush=True)
+        dist.close()
+        return
     if args.mode == "prefill-long":
         r = bench_prefill_long(args, dist, steps=args.steps, warmup=args.warmup)
         if dist.rank == 0:
@@ -1002,6 +1076,8 @@ def main():
         torch.cuda.empty_cache()
     if "shapes" in lines:
         extra["published_shapes"] = bench_published_shapes(args, dist, hbm_gbs, bf16_tf, iters=20, warmup=3)
+    if "frontend" in lines:
+        extra["frontend"] = bench_frontend(args, dist, hbm_gbs, steps=args.prefill_steps, warmup=3)
 
     cpu = None
     if dist.rank == 0 and dist.world == 1:

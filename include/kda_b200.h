@@ -267,6 +267,72 @@ int kda_commit_intermediate_launch(const KdaCommitArgs *args, void *stream);
 int kda_selftest_wait_timeout(int32_t *status, int32_t *expired, int32_t polls, int32_t waits, int32_t give_up,
                               void *stream);
 
+/* ---- Causal-conv front end ---------------------------------------------
+ * The short depthwise causal convolution the attention layer runs over the
+ * mixed q | k | v projection before the KDA op, with its conv-state pool.
+ * Replaces the causal_conv1d step of sglang's attention backend
+ * (AscendKDAAttnBackend.forward_extend, run by
+ * sgl-glm53-ascend-ops/tests/integration/test_glm53_kda_prefix_ascendc.py:325-387;
+ * the conv code itself is sglang's and not in the reference tree):
+ *   out[t, c] = act(bias[c] + sum_{k<W} weight[c, k] * xin[t + k, c]),
+ * xin = the W-1 rows before the request's first token, then its tokens.
+ * Rules:
+ *   - The conv state of a slot is `window` (W-1 <= window <= 8) raw input
+ *     rows, oldest first. A request that continues (has_initial nonzero, or
+ *     has_initial NULL) reads the last W-1 rows of its slot as the rows before
+ *     its first token; one that does not reads zeros. After the call the slot
+ *     holds the last `window` rows of (old window, or zeros, ++ the request's
+ *     tokens); an empty request leaves it unchanged.
+ *   - Tracked-prefix checkpoint: with track_indices[r] > 0 and
+ *     0 <= track_lens[r] <= the request's length, that slot receives the
+ *     `window` rows ending after the first track_lens[r] tokens (rows before
+ *     the request from the old window, or zeros). A tracked length outside
+ *     that range takes no checkpoint.
+ *   - Slot 0 is the padding row: it reads as zeros and is never written.
+ *   - A slot or checkpoint slot outside [0, num_slots), or a malformed
+ *     cu_seqlens entry, rejects the request: KDA_DEVICE_ERR_BAD_SLOT /
+ *     _BAD_SEQLENS in *status, zero output rows, no state written.
+ *   - Every token row of `out` is written: zeros where no request covers it.
+ *   - The requests' slots and checkpoint slots must all be distinct.
+ * Layouts: x bf16 [T][x_row_stride] (channels contiguous); weight fp32
+ * [channels][width]; bias fp32 [channels] or NULL; conv state bf16, element
+ * (slot, row, channel) at slot*s[0] + row*s[1] + channel; out bf16
+ * [num_parts][T][channels / num_parts] (num_parts = 3: contiguous q, k, v
+ * planes, the [T, H, D] tensors the KDA op reads). channels / num_parts, the
+ * row strides and both pool strides must be multiples of 8 elements, and the
+ * x, out and state pointers 16-byte aligned (else KDA_ERR_ALIGNMENT). */
+#define KDA_CONV_ACT_NONE 0
+#define KDA_CONV_ACT_SILU 1
+
+typedef struct KdaConvArgs {
+    const void *x;              /* bf16 [T][x_row_stride]: the mixed projection */
+    int64_t x_row_stride;       /* elements, >= channels */
+    const float *weight;        /* fp32 [channels][width] */
+    const float *bias;          /* fp32 [channels] or NULL */
+    void *conv_state;           /* bf16 pool, updated in place */
+    int64_t state_stride[2];    /* slot, row (elements) */
+    int64_t num_slots;
+    int32_t window;             /* rows per slot, width - 1 .. 8 */
+    const void *indices;        /* [num_req] slot per request */
+    const void *cu_seqlens;     /* [num_req + 1] packed sequence boundaries */
+    const void *has_initial;    /* [num_req] nonzero: continue from the slot; NULL: all continue */
+    const void *track_indices;  /* [num_req] or NULL: checkpoint slot (0: none) */
+    const void *track_lens;     /* [num_req] or NULL: tokens before the checkpoint */
+    int32_t index_bytes[5];     /* indices, cu_seqlens (4|8), has_initial (1|4|8), track_indices, track_lens (4|8) */
+    int32_t num_req;
+    int32_t num_tokens;         /* T */
+    int32_t channels;           /* C */
+    int32_t width;              /* W: 1..4 taps */
+    int32_t num_parts;          /* output planes */
+    int32_t activation;         /* KDA_CONV_ACT_NONE or KDA_CONV_ACT_SILU */
+    void *out;                  /* bf16 [num_parts][T][channels / num_parts] */
+    int32_t *status;            /* optional device word for KDA_DEVICE_ERR_* */
+} KdaConvArgs;
+
+/* The conv front end over a varlen batch (prefill, decode and verify requests
+ * alike), one kernel on the stream. With no requests it zeroes `out`. */
+int kda_conv_launch(const KdaConvArgs *args, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

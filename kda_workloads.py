@@ -23,6 +23,11 @@ Configurations (BASELINE.json ``configs``):
      zero initial state in slots 1..8
   4: one sequence of 131072 tokens, H=32 (sharded by heads), D=128
   5: mixed batch, 64 decode requests + 4 x 2048-token prefills, pool of 1024
+
+plus ``conv_frontend``: the causal-conv front end's inputs for a batch of
+request lengths (the mixed q | k | v projection ~ 0.2 N(0, 1) bf16, 4-tap
+weights ~ 0.1 N(0, 1) fp32, a bf16 conv-state pool ~ 0.1 N(0, 1); requests
+in slots 1..R), the shapes of the reference's backend test at any H.
 """
 
 from __future__ import annotations
@@ -163,3 +168,17 @@ def config5(seed: int = 0, heads: int = 32, decode: int = 64, prefills: int = 4,
     pool = _pool(slots, heads, D)
     indices = (torch.randperm(slots - 1)[:len(lengths)] + 1).to(torch.int32)
     return Workload("cfg5", q, k, v, g, beta, pool, indices, _cu(lengths), D ** -0.5, lengths)
+
+
+def conv_frontend(lengths: list, heads: int = 32, window: int = 3, seed: int = 0, D: int = 128,
+                  device: str = "cpu") -> dict:
+    """Inputs of one ``kda_causal_conv1d`` call: x [T, 3*H*D], weight [3*H*D, 4],
+    conv_state [R + 1, window, 3*H*D], cache_indices, query_start_loc."""
+    torch.manual_seed(seed)
+    C = 3 * heads * D
+    T = sum(lengths)
+    d = dict(x=(torch.randn(T, C) * 0.2).bfloat16(), weight=torch.randn(C, 4) * 0.1,
+             conv_state=(torch.randn(len(lengths) + 1, window, C) * 0.1).bfloat16(),
+             cache_indices=torch.arange(1, len(lengths) + 1, dtype=torch.int32),
+             query_start_loc=_cu(lengths))
+    return {k: v.to(device) for k, v in d.items()}

@@ -50,7 +50,7 @@ def test_status_codes_match_header(abi):
         assert getattr(abi, name) == int(value), name
 
 
-@pytest.mark.parametrize("struct", ["KdaArgs", "KdaCommitArgs"])
+@pytest.mark.parametrize("struct", ["KdaArgs", "KdaCommitArgs", "KdaConvArgs"])
 def test_struct_layout_matches_header(abi, tmp_path, struct):
     cls = getattr(abi, struct)
     fields = [f[0] for f in cls._fields_]
@@ -106,6 +106,44 @@ def test_commit_arguments_rejected_without_launch(abi):
     assert lib.kda_commit_intermediate_launch(ctypes.byref(c), None) == 1
 
 
+def test_conv_arguments_rejected_without_launch(abi):
+    lib = abi.lib()
+    assert lib.kda_conv_launch(None, None) == abi.KDA_ERR_INVALID_ARGUMENT
+    c = abi.KdaConvArgs()
+    c.index_bytes[:] = [4, 4, 1, 4, 4]
+    c.channels, c.num_parts, c.width, c.window = 1536, 3, 4, 3
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_OK            # no requests, no tokens: nothing to do
+    c.num_tokens = 4
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_INVALID_ARGUMENT   # tokens to zero, null x/out
+    c.num_tokens, c.window = 0, 9
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_UNSUPPORTED        # window beyond 8 rows
+    c.width = 5
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_UNSUPPORTED
+    c.width, c.window = 4, 2
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_INVALID_ARGUMENT   # window < W - 1
+    c.window, c.activation = 3, 2
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_UNSUPPORTED
+    c.activation, c.num_req = abi.KDA_CONV_ACT_SILU, 2
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_INVALID_ARGUMENT   # null pointers
+    c.index_bytes[1] = 2
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_INVALID_ARGUMENT   # bad index width
+    c.index_bytes[1] = 4
+    buf = (ctypes.c_uint8 * 64)()
+    base = (ctypes.addressof(buf) + 15) // 16 * 16
+    c.x = c.weight = c.out = c.indices = c.cu_seqlens = c.conv_state = base
+    c.x_row_stride, c.state_stride[0], c.state_stride[1] = 1536, 3 * 1536, 1536
+    c.num_parts = 5
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_INVALID_ARGUMENT   # parts do not divide C
+    c.num_parts, c.channels, c.x_row_stride = 3, 1524, 1524                            # C / 3 = 508: not 8-aligned
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_ALIGNMENT
+    c.channels, c.x_row_stride = 1536, 1536
+    c.x = base + 2
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_ALIGNMENT
+    c.x = base
+    c.track_indices = base                                                              # lens missing
+    assert lib.kda_conv_launch(ctypes.byref(c), None) == abi.KDA_ERR_INVALID_ARGUMENT
+
+
 def test_workspace_size_is_queryable(abi):
     n = abi.chunk_workspace_bytes(8, 33494, 32, 128)
     assert n >= 0
@@ -159,6 +197,11 @@ def test_ops_registered_with_reference_schemas():
     for name in ("kda_varlen_recurrent_v2", "kda_varlen_chunk_v2", "kda_varlen_recurrent_g",
                  "kda_varlen_chunk_g"):
         assert hasattr(ns, name)
+    conv = str(ns.kda_causal_conv1d.default._schema)
+    assert conv == ("sgl_glm53_ascend::kda_causal_conv1d(Tensor x, Tensor weight, Tensor? bias, "
+                    "Tensor(a!) conv_state, Tensor cache_indices, Tensor query_start_loc, "
+                    "Tensor? has_initial_state=None, Tensor? track_conv_indices=None, "
+                    "Tensor? track_conv_lens=None, int num_parts=3, bool silu=True) -> Tensor")
     commit = str(ns.move_intermediate_cache_kda.default._schema)
     assert commit == ("sgl_glm53_ascend::move_intermediate_cache_kda(Tensor(a!) dst, Tensor src, "
                       "Tensor dst_indices, Tensor src_indices, Tensor step_indices, int h_block_size=1) -> ()")
