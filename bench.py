@@ -862,7 +862,8 @@ def bench_frontend(args, dist: Dist, hbm_gbs: float, steps: int, warmup: int) ->
     del d
     torch.cuda.empty_cache()
     return {"metric": "KDA causal-conv front end (kda_causal_conv1d) tokens/s and HBM GB/s",
-            "prefill": pre, "decode": dec, "gpu_launches_per_call": 1}
+            "prefill": pre, "decode": dec,
+            "gpu_launches_per_call": 2, "launches": "conv_request_kernel + conv_stream_kernel"}
 
 
 def cpu_prefill_rate(tokens: int, budget_s: float, seed: int = 8):
@@ -978,6 +979,8 @@ def main():
     ap.add_argument("--decode-batch", type=int, default=256, help="kernel mode: requests (1 token each), H=32")
     ap.add_argument("--prefill-path", choices=("op", "auto", "fused", "split"), default="op",
                     help="prefill-kernel mode: the torch op, or the C ABI with the chunk path forced")
+    ap.add_argument("--frontend-batch", type=int, default=0,
+                    help="frontend-kernel mode: 0 = config 3's prefill sequences, N = N one-token requests")
     ap.add_argument("--long-tokens", type=int, default=131072,
                     help="prefill-long mode: sequence length of config 4 (shorter keeps an ncu capture small)")
     args = ap.parse_args()
@@ -1024,7 +1027,8 @@ def main():
     if args.mode == "frontend-kernel":
         import kda_workloads as workloads
         import sgl_glm53_ascend_ops  # noqa: F401
-        w = workloads.conv_frontend(workloads.config3_lengths(), heads=args.prefill_heads, window=CONV_WINDOW,
+        lengths = workloads.config3_lengths() if args.frontend_batch == 0 else [1] * args.frontend_batch
+        w = workloads.conv_frontend(lengths, heads=args.prefill_heads, window=CONV_WINDOW,
                                     seed=6000 + dist.rank, device="cuda")
         op = torch.ops.sgl_glm53_ascend.kda_causal_conv1d
         step = lambda: op(w["x"], w["weight"], None, w["conv_state"], w["cache_indices"],   # noqa: E731

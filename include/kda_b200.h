@@ -300,7 +300,8 @@ int kda_selftest_wait_timeout(int32_t *status, int32_t *expired, int32_t polls, 
  * [num_parts][T][channels / num_parts] (num_parts = 3: contiguous q, k, v
  * planes, the [T, H, D] tensors the KDA op reads). channels / num_parts, the
  * row strides and both pool strides must be multiples of 8 elements, and the
- * x, out and state pointers 16-byte aligned (else KDA_ERR_ALIGNMENT). */
+ * x, out, state, weight and bias pointers 16-byte aligned (else
+ * KDA_ERR_ALIGNMENT). */
 #define KDA_CONV_ACT_NONE 0
 #define KDA_CONV_ACT_SILU 1
 
@@ -330,7 +331,9 @@ typedef struct KdaConvArgs {
 } KdaConvArgs;
 
 /* The conv front end over a varlen batch (prefill, decode and verify requests
- * alike), one kernel on the stream. With no requests it zeroes `out`. */
+ * alike): two kernels on the stream, one per request (state work and each
+ * request's first W-1 outputs) and one per 64 tokens (the other outputs).
+ * With no requests it zeroes `out`. */
 int kda_conv_launch(const KdaConvArgs *args, void *stream);
 
 #ifdef __cplusplus
