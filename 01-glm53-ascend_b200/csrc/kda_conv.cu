@@ -18,7 +18,8 @@
 //     window. It loads every row it stores before its first store, so the
 //     in-place window update needs no ordering between CTAs: no other CTA
 //     reads the slot. In batches of short requests (decode, verify: at most 4
-//     tokens per request on average) it computes every token.
+//     tokens per request on average) it computes every token, zeroes the rows
+//     no request covers, and is the only launch.
 //   * the streaming kernel, one CTA per (64 tokens, 1024 channels; 8 channels
 //     per thread): every other output, from token rows only, straight into its
 //     plane of the [P][T][C/P] output (P = 3: q, k and v as the contiguous
@@ -256,6 +257,15 @@ __global__ void __launch_bounds__(kThreads, 5) conv_request_kernel(const KdaConv
     const OutCol<V> oc = out_col<V>(p, c);
     const int64_t len = q.eos - q.bos;
     const int64_t n_out = len < head ? len : head;
+    if (head == INT_MAX && q.code != KDA_DEVICE_ERR_BAD_SEQLENS) {
+        // Short batch, one launch: the first and the last request also zero the
+        // rows no request covers (before the first and after the last request;
+        // 0 <= bos <= eos <= T here).
+        if (r == 0)
+            for (int64_t t = 0; t < q.bos; ++t) *oc.at(t) = zero<V>();
+        if (r == p.num_req - 1)
+            for (int64_t t = q.eos; t < p.num_tokens; ++t) *oc.at(t) = zero<V>();
+    }
     if (q.code != 0) {
         if (c == 0) report(p.status, q.code);
         if (q.code == KDA_DEVICE_ERR_BAD_SEQLENS) return;
@@ -316,8 +326,8 @@ __global__ void __launch_bounds__(kThreads, 5) conv_request_kernel(const KdaConv
 // tokens no request covers and for rejected requests. The span is walked in
 // sub-tiles of kSub tokens, the next sub-tile's rows loading while the
 // current one computes; the CTA's first rows are issued before it looks up
-// its requests, so the lookup hides under them. With ZERO_ONLY (every token
-// is the request kernel's) it only zeroes the tokens no request covers.
+// its requests, so the lookup hides under them. With ZERO_ONLY (a batch with
+// no requests) it only zeroes the rows.
 // ---------------------------------------------------------------------------
 
 struct TileMeta {
@@ -452,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 4) conv_stream_kernel(const KdaConvA
 template <int W>
 cudaError_t launch_w(const KdaConvArgs &a, cudaStream_t st) {
     // Batches of short requests (decode, verify): the request kernel computes
-    // every token and the streaming kernel only zeroes uncovered rows.
+    // every token and zeroes the uncovered rows; no second launch.
     const bool short_batch = a.num_req > 0 && a.num_tokens <= static_cast<int64_t>(kShortAvg) * a.num_req;
     if (a.num_req > 0) {
         const dim3 grid(a.num_req, (a.channels + kThreads * kReqVec - 1) / (kThreads * kReqVec));
@@ -463,9 +473,9 @@ cudaError_t launch_w(const KdaConvArgs &a, cudaStream_t st) {
             conv_request_kernel<W, kMaxWindow><<<grid, kThreads, 0, st>>>(a, head);
     }
     const int64_t spans = (static_cast<int64_t>(a.num_tokens) + kSpan - 1) / kSpan;
-    if (spans > 0) {
+    if (spans > 0 && !short_batch) {
         const dim3 grid(static_cast<unsigned>(spans), (a.channels + kThreads * kStreamVec - 1) / (kThreads * kStreamVec));
-        if (short_batch || a.num_req == 0)
+        if (a.num_req == 0)
             conv_stream_kernel<W, true><<<grid, kThreads, 0, st>>>(a);
         else
             conv_stream_kernel<W, false><<<grid, kThreads, 0, st>>>(a);

@@ -155,14 +155,36 @@ def test_padding_slot_and_empty_batch_checkpoint(status):
     _check(e, num_parts=1)
 
 
-def test_rejected_requests(status):
-    b = _batch([5, 9, 3], C=256, window=3, seed=11)
+@pytest.mark.parametrize("lengths", [[1] * 8, [10, 20, 7]])
+def test_uncovered_rows_read_zero(lengths):
+    """Tokens before the first request and after the last one get zero rows,
+    in a batch of short requests (one launch) and of longer ones (two)."""
+    b = _batch(lengths, C=768, window=3, seed=13)
+    lead, tail = 3, 5
+    T = sum(lengths) + lead + tail
+    g = torch.Generator().manual_seed(14)
+    b["x_full"] = (torch.randn(T, 768, generator=g) * 0.5).bfloat16()
+    b["x"] = b["x_full"]
+    b["cu"] = b["cu"] + lead
+    out, st = _check(b)
+    assert torch.equal(out[:, :lead], torch.zeros_like(out[:, :lead]))
+    assert torch.equal(out[:, T - tail:], torch.zeros_like(out[:, T - tail:]))
+
+
+@pytest.mark.parametrize("lengths", [[5, 9, 3], [1, 2, 1]])
+def test_rejected_requests(status, lengths):
+    b = _batch(lengths, C=256, window=3, seed=11)
     b["idx"][1] = 10 ** 6                                     # slot out of range
     out, st = _run_gpu(b, num_parts=1)
     assert status.item() == conv_ref.BAD_SLOT
     ref32, ref_st, ref_status = _run_oracle(b, num_parts=1)
     assert ref_status == conv_ref.BAD_SLOT
-    assert torch.equal(out[0, 5:14], torch.zeros(9, 256, dtype=torch.bfloat16))
+    lo, hi = lengths[0], lengths[0] + lengths[1]
+    assert torch.equal(out[0, lo:hi], torch.zeros(hi - lo, 256, dtype=torch.bfloat16))
+    keep = torch.ones(out.shape[1], dtype=torch.bool)
+    keep[lo:hi] = False
+    d = (out[0, keep].float() - ref32[0, keep]).abs() - _ulp(ref32[0, keep])
+    assert bool((d <= 2.0 ** -20).all())
     assert torch.equal(st, ref_st)
 
 
