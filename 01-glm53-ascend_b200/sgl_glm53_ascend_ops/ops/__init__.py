@@ -1,4 +1,4 @@
-from .conv import causal_conv1d, conv_qkv, kda_forward_extend
+from .conv import causal_conv1d, conv_qkv, kda_forward_decode, kda_forward_extend
 from .kda import (
     kda_varlen_chunk,
     kda_varlen_chunk_g,
@@ -13,6 +13,7 @@ from .kda import (
 __all__ = [
     "causal_conv1d",
     "conv_qkv",
+    "kda_forward_decode",
     "kda_forward_extend",
     "kda_varlen_chunk",
     "kda_varlen_chunk_g",

@@ -7,7 +7,8 @@ depthwise causal conv1d (4 taps, SiLU) that keeps each request's last input
 rows in a conv-state pool, then runs the KDA op. These functions run that
 step on the B200 kernels: ``causal_conv1d`` and ``conv_qkv`` call the
 ``kda_causal_conv1d`` op (one pass over the projection, q, k and v written as
-contiguous planes), ``kda_forward_extend`` chains it with ``kda_varlen_chunk``.
+contiguous planes), ``kda_forward_extend`` chains it with ``kda_varlen_chunk``
+(prefill) and ``kda_forward_decode`` with ``kda_varlen_recurrent`` (decode).
 """
 
 from __future__ import annotations
@@ -120,3 +121,39 @@ def kda_forward_extend(
         cu_seqlens=query_start_loc, lower_bound=lower_bound,
         scale=head_dim ** -0.5 if scale is None else scale, prefill=True,
         track_state_indices=track_indices, track_state_lens=track_lens)
+
+
+def kda_forward_decode(
+    *,
+    mixed: torch.Tensor,
+    a: torch.Tensor,
+    b: torch.Tensor,
+    conv_weights: torch.Tensor,
+    conv_bias: Optional[torch.Tensor],
+    A_log: torch.Tensor,
+    dt_bias: torch.Tensor,
+    lower_bound: float,
+    conv_state: torch.Tensor,
+    temporal_state: torch.Tensor,
+    cache_indices: torch.Tensor,
+    query_start_loc: torch.Tensor,
+    head_dim: int = 128,
+    scale: Optional[float] = None,
+    intermediate_state: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """One KDA layer's decode step after its projections: the conv front end
+    on ``mixed`` (each request continues from its conv window), then the token
+    recurrence with the raw gate. Same tensors as :func:`kda_forward_extend`;
+    ``intermediate_state`` takes the recurrence's per-step checkpoints of a
+    verify pass (its conv window then holds all of the step's draft tokens).
+    Returns the KDA output [1, T, H, head_dim] bf16.
+    """
+    q, k, v = conv_qkv(mixed, conv_weights, conv_bias, conv_state, cache_indices, query_start_loc,
+                       head_dim=head_dim)
+    T, H = q.shape[1], q.shape[2]
+    return torch.ops.sgl_glm53_ascend.kda_varlen_recurrent(
+        A_log=A_log, a=a.reshape(1, T, H, head_dim), dt_bias=dt_bias, q=q, k=k, v=v,
+        b=b.reshape(1, T, H), initial_state_source=temporal_state, initial_state_indices=cache_indices,
+        cu_seqlens=query_start_loc, lower_bound=lower_bound,
+        scale=head_dim ** -0.5 if scale is None else scale, intermediate_state=intermediate_state,
+        prefill=False)

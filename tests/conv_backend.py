@@ -119,3 +119,81 @@ def oracle_impl(mixed, a, b, layer, conv, temporal, idx, cu, has_init, tidx, tle
         A_log=layer.A_log, a=a.reshape(1, T, HEADS, D), dt_bias=layer.dt_bias, q=q, k=k, v=v,
         b=b.reshape(1, T, HEADS), initial_state_source=temporal, initial_state_indices=idx, cu_seqlens=cu,
         lower_bound=layer.lower_bound, scale=D ** -0.5, track_state_indices=tidx, track_state_lens=tlen)
+
+
+def oracle_decode_impl(mixed, a, b, layer, conv, temporal, idx, cu):
+    """The decode step on the CPU oracles (conv, then the token recurrence)."""
+    from oracle import conv_ref, kda_ref
+
+    planes, status = conv_ref.causal_conv1d(mixed, layer.conv_weights, None, conv, idx, cu,
+                                            activation="silu", num_parts=3)
+    assert status == 0
+    T = mixed.shape[0]
+    q, k, v = (planes[i].view(1, T, HEADS, D) for i in range(3))
+    return kda_ref.kda_varlen_recurrent(
+        A_log=layer.A_log, a=a.reshape(1, T, HEADS, D), dt_bias=layer.dt_bias, q=q, k=k, v=v,
+        b=b.reshape(1, T, HEADS), initial_state_source=temporal, initial_state_indices=idx, cu_seqlens=cu,
+        lower_bound=layer.lower_bound, scale=D ** -0.5, prefill=False)
+
+
+PREFIX_LENS = (20, 7, 33)
+DECODE_STEPS = 3
+DECODE_SLOTS = (2, 5, 8)
+
+
+def decode_continuation(extend_impl, decode_impl, ins) -> dict:
+    """Extend three requests over their prefixes, then decode DECODE_STEPS
+    tokens of each, one batched step at a time; against one extend over the
+    whole sequences. Both runs start from the same pools; returns the decode
+    outputs and final pools of both."""
+    dev = ins.mixed.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    R = len(PREFIX_LENS)
+    full_lens = [n + DECODE_STEPS for n in PREFIX_LENS]
+    # token rows: request r's tokens are rows starts[r] .. starts[r] + full_lens[r]
+    starts = [0]
+    for n in full_lens[:-1]:
+        starts.append(starts[-1] + n)
+    idx = torch.tensor(DECODE_SLOTS, **i32)
+    init = torch.ones(R, dtype=torch.bool, device=dev)
+
+    def rows(pick):
+        sel = torch.cat([torch.arange(s + lo, s + hi) for s, (lo, hi) in zip(starts, pick)]).to(dev)
+        cu = [0]
+        for lo, hi in pick:
+            cu.append(cu[-1] + hi - lo)
+        return sel, torch.tensor(cu, **i32)
+
+    def take(sel):
+        return ins.mixed[sel], ins.a[:, sel], ins.b[:, sel]
+
+    whole = new_cache(ins)
+    sel, cu = rows([(0, n) for n in full_lens])
+    out_whole = extend_impl(*take(sel), ins.layer, whole.conv, whole.temporal, idx, cu, init, None, None)
+    stepped = new_cache(ins)
+    sel, cu = rows([(0, n) for n in PREFIX_LENS])
+    extend_impl(*take(sel), ins.layer, stepped.conv, stepped.temporal, idx, cu, init, None, None)
+    outs = []
+    for step in range(DECODE_STEPS):
+        sel, cu = rows([(n + step, n + step + 1) for n in PREFIX_LENS])
+        outs.append(decode_impl(*take(sel), ins.layer, stepped.conv, stepped.temporal, idx, cu))
+    # the whole run's outputs at the decoded positions, in step order
+    want = []
+    for step in range(DECODE_STEPS):
+        pos = [sum(full_lens[:r]) + PREFIX_LENS[r] + step for r in range(R)]
+        want.append(out_whole[:, pos])
+    return dict(decoded=torch.stack(outs), whole=torch.stack(want), stepped=stepped, whole_cache=whole)
+
+
+def check_decode_continuation(extend_impl, decode_impl, ins) -> dict:
+    r = decode_continuation(extend_impl, decode_impl, ins)
+    cpu = lambda t: t.detach().cpu()  # noqa: E731
+    torch.testing.assert_close(cpu(r["decoded"]).float(), cpu(r["whole"]).float(), rtol=0.008, atol=0.001)
+    for s in DECODE_SLOTS:
+        torch.testing.assert_close(cpu(r["stepped"].temporal[s]), cpu(r["whole_cache"].temporal[s]),
+                                   rtol=2e-4, atol=2e-5)
+        assert torch.equal(cpu(r["stepped"].conv[s]), cpu(r["whole_cache"].conv[s]))
+    for s in set(range(SLOTS)) - set(DECODE_SLOTS):
+        assert torch.equal(cpu(r["stepped"].conv[s]), cpu(ins.conv_seed[s]))
+        assert torch.equal(cpu(r["stepped"].temporal[s]), cpu(ins.temporal_seed[s]))
+    return r

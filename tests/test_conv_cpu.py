@@ -10,6 +10,9 @@
 * The reference's backend checkpoint contract
   (test_glm53_kda_prefix_ascendc.py:325-387, via ``tests/conv_backend.py``)
   holds for the oracle composition conv -> chunked KDA, windows 3 and 6.
+* Decode continuation: extending prefixes and then decoding one token per
+  request at a time (conv, then the token recurrence) reproduces one extend
+  over the whole sequences (the backend's suffix tolerances).
 * State rules: padding slot 0, requests that start fresh, empty requests, a
   checkpoint at length 0, rejected slots.
 """
@@ -57,6 +60,11 @@ def test_oracle_matches_vllm_causal_conv1d(name):
 @pytest.mark.parametrize("window", [3, 6])
 def test_oracle_meets_backend_checkpoint_contract(window):
     conv_backend.check_contract(conv_backend.oracle_impl, conv_backend.make_inputs(window))
+
+
+def test_oracle_decode_continues_extend():
+    conv_backend.check_decode_continuation(conv_backend.oracle_impl, conv_backend.oracle_decode_impl,
+                                           conv_backend.make_inputs(3))
 
 
 def _small(window=4, W=4, C=16, slots=6, seed=3):

@@ -16,7 +16,9 @@ a tile's last token), short mixed requests and a decode batch (all work in
 the per-request CTAs), empty and one-token requests, fresh and continuing
 requests, checkpoints at 0, inside and at the end of a request, row strides
 wider than the channel count, and the reference's backend checkpoint
-contract through ``kda_forward_extend`` (conv, then the chunked KDA op).
+contract through ``kda_forward_extend`` (conv, then the chunked KDA op), and
+decode steps through ``kda_forward_decode`` (conv, then the token recurrence)
+continuing an extend as one longer extend would, against the oracles.
 """
 
 import pytest
@@ -226,3 +228,26 @@ def test_backend_checkpoint_contract_on_gpu(ops, window):
     assert_state_close(got["checkpoint"], ref["checkpoint"], what="temporal checkpoint")
     assert torch.equal(got["conv_checkpoint"].cpu(), ref["conv_checkpoint"])
     assert torch.equal(got["final_conv"].cpu(), ref["final_conv"])
+
+
+def _gpu_decode_impl(ops):
+    def impl(mixed, a, b, layer, conv, temporal, idx, cu):
+        return ops.kda_forward_decode(
+            mixed=mixed, a=a, b=b, conv_weights=layer.conv_weights, conv_bias=None, A_log=layer.A_log,
+            dt_bias=layer.dt_bias, lower_bound=layer.lower_bound, conv_state=conv, temporal_state=temporal,
+            cache_indices=idx, query_start_loc=cu, head_dim=conv_backend.D)
+    return impl
+
+
+def test_decode_continues_extend_on_gpu(ops):
+    """Prefixes through kda_forward_extend, then three batched one-token steps
+    through kda_forward_decode: the same outputs and pools as one longer
+    extend, and as the oracles' run of the same steps."""
+    got = conv_backend.check_decode_continuation(_gpu_impl(ops), _gpu_decode_impl(ops),
+                                                 conv_backend.make_inputs(3, device=DEV))
+    ref = conv_backend.decode_continuation(conv_backend.oracle_impl, conv_backend.oracle_decode_impl,
+                                           conv_backend.make_inputs(3))
+    assert_out_close(got["decoded"], ref["decoded"], what="decode outputs")
+    for s in conv_backend.DECODE_SLOTS:
+        assert_state_close(got["stepped"].temporal[s], ref["stepped"].temporal[s], what=f"temporal slot {s}")
+        assert torch.equal(got["stepped"].conv[s].cpu(), ref["stepped"].conv[s])
