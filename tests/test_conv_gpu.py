@@ -173,6 +173,19 @@ def test_uncovered_rows_read_zero(lengths):
     assert torch.equal(out[:, T - tail:], torch.zeros_like(out[:, T - tail:]))
 
 
+def test_no_requests_zero_every_row():
+    x = torch.randn(5, 768, device=DEV).bfloat16()
+    w = torch.randn(768, 4, device=DEV)
+    st = torch.randn(3, 3, 768, device=DEV).bfloat16()
+    before = st.clone()
+    out = torch.ops.sgl_glm53_ascend.kda_causal_conv1d(
+        x, w, None, st, torch.zeros(0, dtype=torch.int32, device=DEV), torch.zeros(1, dtype=torch.int32, device=DEV),
+        None, None, None, 3, True)
+    torch.cuda.synchronize()
+    assert out.shape == (3, 5, 256) and not bool(out.any())
+    assert torch.equal(st, before)
+
+
 @pytest.mark.parametrize("lengths", [[5, 9, 3], [1, 2, 1]])
 def test_rejected_requests(status, lengths):
     b = _batch(lengths, C=256, window=3, seed=11)
