@@ -863,7 +863,9 @@ def bench_frontend(args, dist: Dist, hbm_gbs: float, steps: int, warmup: int) ->
     torch.cuda.empty_cache()
     return {"metric": "KDA causal-conv front end (kda_causal_conv1d) tokens/s and HBM GB/s",
             "prefill": pre, "decode": dec,
-            "gpu_launches_per_call": 2, "launches": "conv_request_kernel + conv_stream_kernel"}
+            "gpu_launches_per_call": {"prefill": 2, "decode": 1},
+            "launches": "prefill: conv_request_kernel + conv_stream_kernel; decode (<= 4 tokens per request on "
+                        "average): conv_request_kernel alone"}
 
 
 def cpu_prefill_rate(tokens: int, budget_s: float, seed: int = 8):
